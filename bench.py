@@ -1,0 +1,391 @@
+"""Benchmark of the spike-sparse conv path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline workload (one line of JSON on rank 0): the reference's headline
+layer shape, a SparseConv2d 3x3/s1/p1 64->64 on a 5-D spike tensor
+T=16, N=64, 56x56, Bernoulli(0.01) fp32 spikes (99% sparsity), kaiming-normal
+fp32 weights + bias -- BASELINE.json's sweep cell (C=64, H=56, density 0.01,
+block 16 per the H->block rule), i.e. layer1.x.conv2 of Spiking-ResNet50.
+A step is one ``SparseConv2d.forward`` over the whole batch.
+
+* ``value``: GB/s of algorithmic traffic (x read + y written + weights + bias,
+  once each) over the timed device time, inputs resident in HBM; x and y are
+  822 MB each, larger than L2, so no flush is needed between steps.
+* ``e2e``: the same metric through the public module call with the spikes
+  copied from pinned host memory and the output copied back every step.
+* ``roofline``: the sparse-conv kernel against the measured HBM copy peak.
+* ``cpu_baseline``: the reference's CPU path (F.conv2d, all host threads) on
+  a bounded sample of the same workload.
+* ``extra``: the other hot-path kernels on their BASELINE.json configs
+  (prescan GB/s on the same input; C2 1x1 with bf16 weights; C3 fused
+  conv+BN+LIF over T=16) and cuDNN dense time for the speedup figures.
+
+Multi-GPU (torchrun): every rank runs the same per-GPU workload on its own
+shard of the batch (weak scaling, no collective in the data path); the
+timed region is bracketed by barriers and the max over ranks is reported.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+import torch.nn as nn  # noqa: E402
+
+T_STEPS, N_BATCH, C, H, W = 16, 64, 64, 56, 56
+DENSITY = 0.01
+METRIC = "sparse conv3x3 GB/s (layer1.x.conv2 shape, 99% spike sparsity)"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-extra", action="store_true", help="skip the C2/C3/prescan side measurements")
+    return ap.parse_args()
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d.get("bf16_tflops", 1590.0)), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def conv_bytes(n_img, c, h, w, co, ho, wo, k, esz=4, wsz=4, bias=True):
+    return esz * n_img * c * h * w + esz * n_img * co * ho * wo + wsz * co * c * k * k + (4 * co if bias else 0)
+
+
+def make_conv(c, co, k, s, p, bias, seed, wdtype=torch.float32, device="cuda"):
+    g = torch.Generator().manual_seed(seed)
+    conv = nn.Conv2d(c, co, k, s, p, bias=bias)
+    w = torch.empty(co, c, k, k)
+    nn.init.kaiming_normal_(w, mode="fan_out", nonlinearity="relu", generator=g)
+    conv.weight.data.copy_(w)
+    if bias:
+        conv.bias.data.copy_(torch.randn(co, generator=g) * 0.1)
+    conv = conv.to(device)
+    if wdtype != torch.float32:
+        conv = conv.to(wdtype)
+    return conv
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clock and throttle reasons while the GPU is busy."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (FileNotFoundError, OSError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cuda_time(fn, steps, warmup, dist=None):
+    """Device time of `steps` calls of fn, CUDA events on the current stream, max over ranks."""
+    for _ in range(warmup):
+        fn()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    ms = s.elapsed_time(e)
+    if dist is not None:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
+def cpu_baseline(conv_cpu, x_sample, bytes_sample):
+    from oracle import oracle
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    with torch.no_grad():
+        oracle.reference_cpu_conv2d(x_sample, conv_cpu.weight, conv_cpu.bias, 1, 1)  # warm-up
+        times = []
+        t_end = time.perf_counter() + 15.0
+        while len(times) < 3 or (time.perf_counter() < t_end and len(times) < 10):
+            t0 = time.perf_counter()
+            oracle.reference_cpu_conv2d(x_sample, conv_cpu.weight, conv_cpu.bias, 1, 1)
+            times.append(time.perf_counter() - t0)
+    sec = statistics.median(times)
+    return bytes_sample / sec / 1e9, threads, sec
+
+
+def run_reference(args):
+    """The reference's own CPU implementation of the path (F.conv2d, Ops/sparse_conv2d.py:819-834)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    g = torch.Generator().manual_seed(0)
+    conv = make_conv(C, C, 3, 1, 1, True, 1, device="cpu")
+    n_img = 16  # 16 of the 1024 (T*N) images per step
+    x = (torch.rand(n_img, C, H, W, generator=g) < DENSITY).float()
+    nbytes = conv_bytes(n_img, C, H, W, C, H, W, 3)
+    from oracle import oracle
+    torch.set_num_threads(os.cpu_count() or 1)
+    with torch.no_grad():
+        for _ in range(max(1, min(args.warmup, 3))):
+            oracle.reference_cpu_conv2d(x, conv.weight, conv.bias, 1, 1)
+        t0 = time.perf_counter()
+        steps = max(1, min(args.steps, 20))
+        for _ in range(steps):
+            oracle.reference_cpu_conv2d(x, conv.weight, conv.bias, 1, 1)
+        sec = (time.perf_counter() - t0) / steps
+    val = nbytes / sec / 1e9
+    sample = f"{n_img} of {T_STEPS * N_BATCH} images (T*N) per step, same shapes/density/weights init"
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(val, 3), "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "C5 cell conv3x3 C64 56x56 T16 N64 p0.01 (CPU sample)", "sample": sample},
+        "cpu_baseline": {"value": round(val, 3), "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
+                         "sample": sample + "; torch F.conv2d = the reference SparseConv2d CPU path"},
+        "e2e": {"value": round(val, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }))
+
+
+def extras(dev, hbm_peak, steps):
+    """Side measurements: prescan GB/s, C2 1x1 bf16, C3 fused conv+BN+LIF, cuDNN comparisons."""
+    from sparseflow_b200.Kernels._prescan_common import prescan2d
+    from sparseflow_b200.Ops.sparse_conv2d import SparseConv2d
+    from sparseflow_b200.Ops.sparse_fused_conv_lif import FusedSparseConvLIF
+    from sparseflow_b200.Ops.lif_node import LIFNode
+    out = {}
+    steps = max(3, min(steps, 50))
+    g = torch.Generator(device=dev).manual_seed(17)
+
+    # Prescan on the headline input (fp32 NCHW, 3x3 RF, 8x16 tiles, gs 16).
+    x = (torch.rand(T_STEPS * N_BATCH, C, H, W, device=dev, generator=g) < DENSITY).float()
+    nt = T_STEPS * N_BATCH * 7 * 4
+    ag = torch.empty(nt, dtype=torch.int32, device=dev)
+    tc = torch.empty_like(ag)
+    ids = torch.empty_like(ag)
+    cnt = torch.zeros(1, dtype=torch.int32, device=dev)
+    fn = lambda: prescan2d(x, 0, (H, W), (3, 3), 1, 1, (8, 16), 16, 1e-6, ag, tc, ids, cnt)  # noqa: E731
+    ms = cuda_time(fn, steps, 3) / steps
+    pb = x.numel() * 4 + nt * 12
+    out["prescan_c5"] = {"GBps": round(pb / ms / 1e6, 1), "frac_of_measured_hbm": round(pb / ms / 1e6 / hbm_peak, 3),
+                         "ms": round(ms, 4), "bytes": pb}
+    del x
+
+    # C2: 1x1 256->64, T16 N32 56x56 block-clustered spikes, bf16 weights.
+    n2 = 16 * 32
+    blk = (torch.rand(n2, 256, 4, 4, device=dev, generator=g) < 0.05).float()
+    mask = blk.repeat_interleave(16, 2).repeat_interleave(16, 3)[:, :, :56, :56]
+    x2 = (mask * (torch.rand(n2, 256, 56, 56, device=dev, generator=g) < 0.3).float()).reshape(16, 32, 256, 56, 56)
+    del blk, mask
+    conv2 = nn.Conv2d(256, 64, 1, bias=False)
+    conv2.weight.data = (torch.randn(64, 256, 1, 1, generator=torch.Generator().manual_seed(2)) * 0.02)
+    conv2 = conv2.to(dev).to(torch.bfloat16)
+    m2 = SparseConv2d.from_dense(conv2, block_size=16)
+    m2.set_inference_mode(True)
+    ms = cuda_time(lambda: m2(x2), steps, 3) / steps
+    b2 = conv_bytes(n2, 256, 56, 56, 64, 56, 56, 1, wsz=2, bias=False)
+    x2f = x2.reshape(n2, 256, 56, 56)
+    wf = conv2.weight.float()
+    cud = cuda_time(lambda: torch.nn.functional.conv2d(x2f, wf), steps, 3) / steps
+    out["c2_conv1x1_bf16w"] = {"GBps": round(b2 / ms / 1e6, 1), "frac_of_measured_hbm": round(b2 / ms / 1e6 / hbm_peak, 3),
+                               "ms": round(ms, 4), "cudnn_ms": round(cud, 4), "speedup_vs_cudnn": round(cud / ms, 2),
+                               "density": round(float((x2 != 0).float().mean()), 5)}
+    del x2, x2f
+
+    # C3: fused conv3x3 + BN-fold + LIF, T16 N64 C128 28x28, Bernoulli(0.005).
+    x3 = (torch.rand(16, 64, 128, 28, 28, device=dev, generator=g) < 0.005).float()
+    conv3 = make_conv(128, 128, 3, 1, 1, False, 3, device=dev)
+    bn = nn.BatchNorm2d(128).to(dev).eval()
+    gg = torch.Generator(device=dev).manual_seed(4)
+    bn.weight.data = torch.rand(128, device=dev, generator=gg) + 0.5
+    bn.bias.data = torch.randn(128, device=dev, generator=gg) * 0.1
+    bn.running_mean = torch.randn(128, device=dev, generator=gg) * 0.1
+    bn.running_var = torch.rand(128, device=dev, generator=gg) + 0.5
+    m3 = FusedSparseConvLIF.from_conv_bn_lif(conv3, bn, LIFNode(tau=2.0, v_threshold=1.0, v_reset=0.0))
+
+    def c3_step():
+        m3.reset()
+        return m3(x3)
+    ms = cuda_time(c3_step, steps, 3) / steps
+    b3 = 4 * x3.numel() * 2 + 4 * 64 * 128 * 28 * 28 * 2 + 4 * 128 * 128 * 9
+    out["c3_fused_conv_bn_lif"] = {"GBps": round(b3 / ms / 1e6, 1), "frac_of_measured_hbm": round(b3 / ms / 1e6 / hbm_peak, 3),
+                                   "ms": round(ms, 4)}
+    return out
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as tdist
+        tdist.init_process_group("nccl", device_id=dev)
+        dist = tdist
+
+    from sparseflow_b200.Ops.sparse_conv2d import SparseConv2d
+
+    hbm_peak, _, peak_kind = peaks()
+    n_img = T_STEPS * N_BATCH
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    x = (torch.rand(T_STEPS, N_BATCH, C, H, W, device=dev, generator=g) < DENSITY).float()
+    conv = make_conv(C, C, 3, 1, 1, True, 1, device=dev)
+    mod = SparseConv2d.from_dense(conv, block_size=16)
+    mod.set_inference_mode(True)
+    step_bytes = conv_bytes(n_img, C, H, W, C, H, W, 3)
+
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    phys = int(vis.split(",")[local]) if vis and vis.split(",")[local].strip().isdigit() else local
+    sampler = ClockSampler(phys)
+    sampler.start()
+    with torch.no_grad():
+        ms_total = cuda_time(lambda: mod(x), args.steps, args.warmup, dist)
+    clocks = sampler.stop()
+    ms_step = ms_total / args.steps
+    value = world * step_bytes * args.steps / (ms_total / 1e3) / 1e9
+    achieved = step_bytes / (ms_step / 1e3) / 1e9
+
+    # cuDNN dense on the same input (fp32, torch defaults: TF32 allowed for convs).
+    x4 = x.reshape(n_img, C, H, W)
+    with torch.no_grad():
+        cud_ms = cuda_time(lambda: torch.nn.functional.conv2d(x4, conv.weight, conv.bias, 1, 1),
+                           max(3, min(args.steps, 20)), 3) / max(3, min(args.steps, 20))
+        tf32 = torch.backends.cudnn.allow_tf32
+        torch.backends.cudnn.allow_tf32 = False
+        cud32_ms = cuda_time(lambda: torch.nn.functional.conv2d(x4, conv.weight, conv.bias, 1, 1), 3, 1) / 3
+        torch.backends.cudnn.allow_tf32 = tf32
+
+    # End to end through the module: pinned host spikes in, output back to host, every step.
+    e2e_steps = max(2, min(args.steps, 5))
+    x_host = x.cpu().pin_memory()
+    y_host = torch.empty((T_STEPS, N_BATCH, C, H, W), dtype=torch.float32).pin_memory()
+    x_dev = torch.empty_like(x)
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        y = mod(x_dev)
+        y_host.copy_(y, non_blocking=True)
+    with torch.no_grad():
+        e2e_ms = cuda_time(e2e_step, e2e_steps, 1, dist) / e2e_steps
+    e2e_val = world * step_bytes / (e2e_ms / 1e3) / 1e9
+    del x_host, y_host, x_dev
+
+    extra = None
+    if not args.no_extra and rank == 0:
+        with torch.no_grad():
+            extra = extras(dev, hbm_peak, args.steps)
+
+    cpu = None
+    if rank == 0 and world == 1:
+        conv_cpu = make_conv(C, C, 3, 1, 1, True, 1, device="cpu")
+        xs = x.reshape(n_img, C, H, W)[:16].cpu()
+        val, cores, sec = cpu_baseline(conv_cpu, xs, conv_bytes(16, C, H, W, C, H, W, 3))
+        cpu = {"value": round(val, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+               "sample": f"16 of {n_img} images per call ({sec * 1e3:.1f} ms median); torch F.conv2d on CPU = "
+                         "the reference SparseConv2d CPU path (Ops/sparse_conv2d.py:819-834)"}
+
+    traffic = None
+    tf = ROOT / "profiles" / "sparse_conv_c5.traffic.json"
+    if tf.exists():
+        traffic = json.loads(tf.read_text()).get("dram_bytes_per_launch")
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded Bernoulli spikes, kaiming weights)",
+            "config": {"workload": "C5 cell: SparseConv2d 3x3/s1/p1 C64->64, T16 N64 56x56, Bernoulli(0.01) "
+                                   "fp32 spikes, block 16 (per GPU)", "global_batch": N_BATCH * world,
+                       "seq_len": T_STEPS, "parallelism": f"N-shard x{world}",
+                       "l2": "inputs (822 MB) and outputs larger than L2; no flush"},
+            "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": x.numel() * 4,
+                    "d2h_bytes_per_step": x.numel() * 4, "ms_per_step": round(e2e_ms, 3)},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
+                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                         else "fallback 6650 GB/s", "kernel": "sparse_conv_kernel<3,1,2,16,float,float,false>",
+                         "algorithmic_bytes_per_launch": step_bytes},
+            "speedup_vs_cudnn": {"cudnn_default_ms": round(cud_ms, 4), "cudnn_fp32_no_tf32_ms": round(cud32_ms, 4),
+                                 "ours_ms": round(ms_step, 4), "vs_default": round(cud_ms / ms_step, 2),
+                                 "vs_fp32": round(cud32_ms / ms_step, 2)},
+            "gpu_launches": args.steps,
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+            "extra": extra,
+        }
+        print(json.dumps(line))
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,146 @@
+/*
+ * sparseflow_b200.h -- C ABI of the B200 (sm_100a) spike-sparse convolution path.
+ *
+ * Every entry point:
+ *   - takes plain device pointers, sizes and a CUDA stream (passed as void*,
+ *     a cudaStream_t; NULL means the legacy default stream);
+ *   - only enqueues work on that stream (no host synchronisation, no device
+ *     allocation) and returns a status code; it never throws;
+ *   - has no CPU fallback: a configuration the kernels do not cover returns
+ *     SF_ERR_UNSUPPORTED and the caller decides what to do.
+ *
+ * Reference interfaces replaced (paths inside hpcyhr/SparseFlow):
+ *   sf_prescan2d          Kernels/_prescan_common.py:231-306 (_build_rf_prescan_metadata_impl,
+ *                         build_rf_prescan_metadata) as called from
+ *                         Kernels/conv2d.py:158-206 (_build_two_stage_metadata), fused with
+ *                         Kernels/conv2d.py:113-123 (_build_active_tile_ids).
+ *   sf_pack_weights       Ops/sparse_conv2d.py:339-350 (_get_w_cl weight repack).
+ *   sf_sparse_conv2d      Kernels/conv2d.py:893-1178 (sparse_conv2d_forward: the
+ *                         sparse_conv3x3s1/s2 and conv1x1 NHWC kernels, :236-886).
+ *   sf_fused_conv_lif     Kernels/fused_conv_lif.py:310-484 (sparse_fused_conv_lif_forward)
+ *                         with the LIF semantics of Ops/sparse_fused_conv_lif.py:271-293,
+ *                         run over all T steps in one launch.
+ */
+#ifndef SPARSEFLOW_B200_H
+#define SPARSEFLOW_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SF_ABI_VERSION 1
+
+typedef int32_t sf_status;
+enum {
+  SF_OK = 0,
+  SF_ERR_INVALID_ARG = 1,   /* null pointer, non-positive size, inconsistent shape */
+  SF_ERR_UNSUPPORTED = 2,   /* valid request outside what the kernels implement */
+  SF_ERR_ALIGNMENT = 3,     /* a pointer is not 16-byte aligned */
+  SF_ERR_WORKSPACE = 4,     /* workspace missing or too small */
+  SF_ERR_CUDA = 5,          /* a CUDA runtime call failed (launch, attribute, ...) */
+  SF_ERR_DEVICE_TIMEOUT = 6 /* reported by sf_prescan2d_status: a bounded device wait expired */
+};
+
+enum { SF_DTYPE_F32 = 0, SF_DTYPE_F16 = 1, SF_DTYPE_BF16 = 2 };
+enum { SF_LAYOUT_NCHW = 0, SF_LAYOUT_NHWC = 1 };
+
+/* Tile classes written by sf_prescan2d (Utils/sparse_helpers.py:28-30). */
+enum { SF_TILE_ZERO = 0, SF_TILE_SPARSE = 1, SF_TILE_DENSEISH = 2 };
+
+int32_t sf_abi_version(void);
+const char* sf_status_string(sf_status s);
+
+/* ------------------------------------------------------------------------ */
+/* Stage 1: receptive-field prescan.                                         */
+/* ------------------------------------------------------------------------ */
+typedef struct sf_prescan_desc {
+  int32_t n, c, h, w;          /* input dims; n folds T*B for 5-D inputs */
+  int32_t h_out, w_out;        /* conv output dims */
+  int32_t kernel, stride, padding;
+  int32_t block_h, block_w;    /* output tile; GH = ceil(h_out/block_h) */
+  int32_t group_size;          /* channels per group; ceil(c/group_size) <= 32 */
+  double threshold;            /* compared as IEEE half, like the reference */
+  int32_t dtype;               /* SF_DTYPE_* of x */
+  int32_t layout;              /* SF_LAYOUT_* of x */
+} sf_prescan_desc;
+
+/* Bytes of caller-owned device workspace sf_prescan2d needs. The workspace
+ * must be zero-filled once when first allocated; afterwards the kernel keeps it
+ * consistent itself. One workspace serves one stream at a time. */
+size_t sf_prescan2d_workspace_size(const sf_prescan_desc* d);
+
+/* Writes, for the N*GH*GW tiles in (n, gh, gw) row-major order:
+ *   ag_mask[t]     bit g set iff channel group g has |half(x)| > half(threshold)
+ *                  somewhere in tile t's receptive field (NaN in that field
+ *                  clears the bit, as max-pooling a NaN does in the reference);
+ *   tile_class[t]  SF_TILE_ZERO / SPARSE / DENSEISH;
+ *   active_ids     ascending ids of tiles with tile_class != ZERO;
+ *   *active_count  their number.
+ * active_ids / active_count may be NULL (then no compaction is done). */
+sf_status sf_prescan2d(const void* x, const sf_prescan_desc* d,
+                       int32_t* ag_mask, int32_t* tile_class,
+                       int32_t* active_ids, int32_t* active_count,
+                       void* workspace, size_t workspace_bytes, void* stream);
+
+/* Reads back (synchronously on `stream`) the device error word of a prescan
+ * workspace: SF_OK or SF_ERR_DEVICE_TIMEOUT. Not for hot loops. */
+sf_status sf_prescan2d_status(void* workspace, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Stage 2: gather-style sparse convolution (deterministic, atomic-free).    */
+/* ------------------------------------------------------------------------ */
+
+/* Packed layout: [c_in][kernel*kernel][c_out_pad] with c_out_pad =
+ * round_up(c_out, 128), zero padded; element type w_dst_dtype (F32 or BF16). */
+size_t sf_packed_weight_bytes(int32_t c_out, int32_t c_in, int32_t kernel, int32_t w_dst_dtype);
+sf_status sf_pack_weights(const void* w_oihw, int32_t w_src_dtype,
+                          int32_t c_out, int32_t c_in, int32_t kernel,
+                          int32_t w_dst_dtype, void* w_packed, void* stream);
+
+typedef struct sf_conv_desc {
+  int32_t n, c_in, h, w;       /* NCHW input; n folds T*B */
+  int32_t c_out, h_out, w_out; /* NCHW output */
+  int32_t kernel, stride, padding;  /* (1,1,0), (3,1,1), (3,2,1) */
+  int32_t x_dtype;             /* dtype of x and y */
+  int32_t w_dtype;             /* dtype of the packed weights: F32 or BF16 */
+  int32_t has_bias;            /* bias: fp32 [c_out] */
+} sf_conv_desc;
+
+/* y = conv2d(x, w) + bias, computed in fp32 over the nonzero input elements
+ * only (exact zeros contribute nothing, so skipping them is exact). */
+sf_status sf_sparse_conv2d(const void* x, const void* w_packed, const float* bias,
+                           void* y, const sf_conv_desc* d, void* stream);
+
+/* Reads back (synchronously on `stream`) the device error word shared by
+ * sf_sparse_conv2d and sf_fused_conv_lif: SF_OK or SF_ERR_DEVICE_TIMEOUT.
+ * Not for hot loops. */
+sf_status sf_sparse_conv2d_status(void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Fused conv + (BN-folded) bias + LIF over all time steps in one launch.    */
+/* ------------------------------------------------------------------------ */
+typedef struct sf_lif_desc {
+  int32_t t_steps, n, c_in, h, w;   /* x: [t_steps, n, c_in, h, w] */
+  int32_t c_out, h_out, w_out;      /* spikes: [t_steps, n, c_out, h_out, w_out] */
+  int32_t kernel, stride, padding;
+  float tau, v_threshold, v_reset;  /* v_reset is used as 0 when hard_reset == 0 */
+  int32_t hard_reset;               /* 1: v = v_reset on spike; 0: v -= v_threshold */
+  int32_t decay_input;              /* 1: v += (I - (v - v_reset)) / tau */
+  int32_t x_dtype;                  /* dtype of x and of spikes_out */
+  int32_t w_dtype;                  /* packed weight dtype: F32 or BF16 */
+  int32_t has_bias;
+} sf_lif_desc;
+
+/* v_inout: fp32 [n, c_out, h_out, w_out], read as v[0] and overwritten with
+ * the membrane state after the last step. */
+sf_status sf_fused_conv_lif(const void* x, const void* w_packed, const float* bias,
+                            float* v_inout, void* spikes_out,
+                            const sf_lif_desc* d, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SPARSEFLOW_B200_H */

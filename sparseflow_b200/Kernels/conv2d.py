@@ -1,0 +1,199 @@
+"""Sparse conv2d entry point on the native sm_100a kernels.
+
+Reference: Kernels/conv2d.py:893-1178 (``sparse_conv2d_forward``), with the
+same argument list and the same variable-arity return
+``(y, ms[, avg_active_ratio][, tile_stats][, backend_meta])``.
+
+What differs is the machinery behind it. The reference casts x to fp16,
+repacks it NHWC, runs a torch-op prescan, syncs on ``torch.nonzero`` and
+launches a Triton kernel over active (tile, group) blocks in fp16. Here one
+native launch reads x in its own NCHW layout and dtype, skips every exact
+zero element (element-level sparsity), accumulates in fp32 against fp32 (or
+bf16) weights and writes y; no host sync happens unless timing or
+statistics are requested. The stage-1 prescan runs only when its metadata is
+asked for (statistics, or caller-provided metadata buffers).
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.nn.functional as F
+
+from .. import _lib
+from ..Utils.config import PRESCAN_ACTIVITY_EPS, SPARSE_DENSE_RATIO_THRESHOLD
+from ..Utils.sparse_helpers import (TILE_DENSEISH, TILE_SPARSE, TILE_ZERO, choose_group_size, popcount_buf,
+                                    select_tile_sizes)
+from ._prescan_common import prescan2d
+
+FALLBACK_RATIO = SPARSE_DENSE_RATIO_THRESHOLD
+
+SUPPORTED_PATTERNS = ((1, 1, 0), (3, 1, 1), (3, 2, 1))
+
+
+def _select_tile_sizes(h: int, w: int):
+    return select_tile_sizes(h, w)
+
+
+def _select_block_sizes(h, w, c_in, c_out, kernel_size, n):
+    bh, bw = select_tile_sizes(h, w)
+    return bh, bw, bh * bw, 64, choose_group_size(c_in)
+
+
+def _popcount_buf(ag_mask_buf, n_tiles):
+    return popcount_buf(ag_mask_buf, n_tiles)
+
+
+def output_hw(h: int, w: int, k: int, s: int, p: int, d: int = 1):
+    return (h + 2 * p - d * (k - 1) - 1) // s + 1, (w + 2 * p - d * (k - 1) - 1) // s + 1
+
+
+def prepare_input(x: torch.Tensor) -> torch.Tensor:
+    """Contiguous, 16-byte aligned input whose byte size is a multiple of 16.
+
+    The bulk copies in the kernel move each channel's rows as 16-byte aligned
+    ranges, so the last range may extend up to 15 bytes past the last element;
+    inputs that do not meet that are copied (on the GPU) into a padded buffer.
+    """
+    x = x.contiguous()
+    nbytes = x.numel() * x.element_size()
+    if x.data_ptr() % 16 == 0 and nbytes % 16 == 0:
+        return x
+    pad = (-nbytes % 16) // x.element_size()
+    buf = torch.empty(x.numel() + pad, dtype=x.dtype, device=x.device)
+    buf[: x.numel()].copy_(x.reshape(-1))
+    return buf[: x.numel()].view(x.shape)
+
+
+def pack_weight(weight: torch.Tensor) -> torch.Tensor:
+    """Pack [C_out, C_in, k, k] for the kernel: fp32 stays fp32 (fp16 widens
+    exactly to fp32), bf16 stays bf16."""
+    out_dtype = torch.bfloat16 if weight.dtype == torch.bfloat16 else torch.float32
+    return _lib.pack_weights(weight, out_dtype)
+
+
+def sparse_conv2d_forward(
+    x, weight, bias,
+    kernel_size=3, stride=1, padding=0, dilation=1, groups=1,
+    threshold=PRESCAN_ACTIVITY_EPS, w_cl=None,
+    ag_mask_buf=None, tile_class_buf=None,
+    return_ms=False, fallback_ratio=FALLBACK_RATIO,
+    return_avg_active_ratio=False, return_tile_stats=False,
+    return_backend_meta=False,
+    x_nhwc=None, active_tile_ids_buf=None,
+    launch_all_tiles=False,
+    output_dtype=None,
+):
+    """Sparse conv2d of an NCHW CUDA tensor. See the module docstring.
+
+    ``w_cl`` is an optional pre-packed weight buffer (from ``pack_weight``);
+    ``x_nhwc`` and ``fallback_ratio`` are accepted for signature compatibility
+    and unused (the kernel reads NCHW; the runtime dense policy is off).
+    """
+    if not x.is_cuda:
+        raise RuntimeError("sparse_conv2d_forward needs a CUDA tensor (the B200 path has no CPU fallback)")
+    if isinstance(stride, (tuple, list)):
+        stride = stride[0]
+    if isinstance(padding, (tuple, list)):
+        padding = padding[0]
+    if isinstance(dilation, (tuple, list)):
+        dilation = dilation[0]
+    n, c_in, h_in, w_in = x.shape
+    c_out = weight.shape[0]
+    out_dtype = x.dtype if output_dtype is None else output_dtype
+    need_stats = bool(return_tile_stats or return_avg_active_ratio)
+
+    def _finalize(y, ms, ratio=None, tile_stats=None, meta=None):
+        ret = (y, ms)
+        if return_avg_active_ratio:
+            ret = ret + (ratio,)
+        if return_tile_stats:
+            ret = ret + (tile_stats,)
+        if return_backend_meta:
+            ret = ret + (meta,)
+        return ret
+
+    def _dense(reason):
+        # Patterns outside the sparse kernels (never produced by the analyzer)
+        # keep the reference's behaviour: the dense GPU convolution.
+        ms = 0.0
+        if return_ms:
+            se, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            se.record()
+        y = F.conv2d(x, weight, bias, stride=stride, padding=padding, dilation=dilation, groups=groups)
+        if y.dtype != out_dtype:
+            y = y.to(out_dtype)
+        if return_ms:
+            ee.record()
+            torch.cuda.synchronize(x.device)
+            ms = se.elapsed_time(ee)
+        return _finalize(y, ms, 1.0, None, {"backend": "dense_fallback", "reason": reason})
+
+    if groups != 1 or dilation != 1:
+        return _dense("unsupported_groups_or_dilation")
+    h_out, w_out = output_hw(h_in, w_in, kernel_size, stride, padding, dilation)
+    if h_out <= 0 or w_out <= 0:
+        return _dense("invalid_output_shape")
+    if (kernel_size, stride, padding) not in SUPPORTED_PATTERNS:
+        return _dense("split_1x1s2_downsample" if (kernel_size, stride) == (1, 2) else "unsupported_pattern")
+
+    gs = choose_group_size(c_in)
+    n_groups = -(-c_in // gs)
+    bh, bw = select_tile_sizes(h_out, w_out)
+    gh, gw = -(-h_out // bh), -(-w_out // bw)
+    n_tiles = n * gh * gw
+
+    x = prepare_input(x)
+    w_packed = w_cl if w_cl is not None else pack_weight(weight)
+    b = None if bias is None else bias.detach().to(torch.float32).contiguous()
+
+    avg_ratio = None
+    tile_stats = None
+    active_tiles = None
+    want_meta = need_stats or ag_mask_buf is not None or tile_class_buf is not None or active_tile_ids_buf is not None
+    if want_meta:
+        count = torch.zeros(1, dtype=torch.int32, device=x.device) if active_tile_ids_buf is not None else None
+        tc, agm, _, _ = prescan2d(x, _lib.SF_LAYOUT_NCHW, (h_out, w_out), (kernel_size, kernel_size), stride,
+                                  padding, (bh, bw), gs, threshold, ag_mask_out=ag_mask_buf,
+                                  tile_class_out=tile_class_buf, active_ids_out=active_tile_ids_buf,
+                                  active_count_out=count)
+        if need_stats:
+            zc = int((tc == TILE_ZERO).sum().item())
+            sc = int((tc == TILE_SPARSE).sum().item())
+            dc = int((tc == TILE_DENSEISH).sum().item())
+            active_tiles = sc + dc
+            pc = popcount_buf(agm, n_tiles)
+            avg_ratio = float(pc.sum().item()) / max(float(n_tiles * n_groups), 1.0)
+            if return_tile_stats:
+                tile_stats = {
+                    "zero_tiles": zc, "sparse_tiles": sc, "denseish_tiles": dc, "total_tiles": n_tiles,
+                    "prescan_mode": "b200_single_pass", "active_tiles": active_tiles,
+                    "active_tile_ratio": active_tiles / max(n_tiles, 1),
+                    "denseish_ratio_nonzero": dc / max(active_tiles, 1),
+                }
+
+    y = torch.empty(n, c_out, h_out, w_out, dtype=x.dtype, device=x.device)
+    ms = 0.0
+    if return_ms:
+        se, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        se.record()
+    _lib.sparse_conv2d(x, w_packed, b, y, c_out, kernel_size, stride, padding)
+    if return_ms:
+        ee.record()
+        torch.cuda.synchronize(x.device)
+        ms = se.elapsed_time(ee)
+    if y.dtype != out_dtype:
+        y = y.to(out_dtype)
+    meta = {
+        "backend": "sparse_b200", "reason": "element_gather_sm100a",
+        "total_tiles": n_tiles, "launch_count": n_tiles,
+        "launch_mode": "persistent", "launch_mode_reason": "persistent_gather",
+    }
+    if active_tiles is not None:
+        meta["active_tiles"] = active_tiles
+    return _finalize(y, ms, avg_ratio, tile_stats, meta)
+
+
+# Reference-compatible aliases.
+choose_group_size = choose_group_size
+TILE_ZERO, TILE_SPARSE, TILE_DENSEISH = TILE_ZERO, TILE_SPARSE, TILE_DENSEISH

@@ -1,0 +1,64 @@
+"""Multi-step LIF neuron used by the synthetic spiking models.
+
+spikingjelly (the reference's neuron library, pinned 0.0.0.0.14) is not
+installed here, so models built for benchmarks and tests use this module: the
+same charge / fire / reset rule as spikingjelly's ``LIFNode`` with
+``decay_input=True`` and the rule restated in Ops/sparse_fused_conv_lif.py:283-292
+of the reference, applied over the leading time axis of a [T, N, ...] input
+(``step_mode='m'``). It is plain tensor code: it is not part of the sparse
+convolution path, which consumes its output spikes.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.nn as nn
+
+
+class LIFNode(nn.Module):
+    def __init__(self, tau: float = 2.0, v_threshold: float = 1.0, v_reset: Optional[float] = 0.0,
+                 decay_input: bool = True, detach_reset: bool = False, step_mode: str = "m"):
+        super().__init__()
+        self.tau = float(tau)
+        self.v_threshold = float(v_threshold)
+        self.v_reset = v_reset
+        self.decay_input = bool(decay_input)
+        self.detach_reset = detach_reset
+        self.step_mode = step_mode
+        self.v = None
+
+    def reset(self):
+        self.v = None
+
+    def _step(self, x: torch.Tensor) -> torch.Tensor:
+        vr = 0.0 if self.v_reset is None else float(self.v_reset)
+        if self.v is None or self.v.shape != x.shape:
+            self.v = torch.full_like(x, vr, dtype=torch.float32)
+        v = self.v
+        xf = x.float()
+        if self.decay_input:
+            v_tmp = v + (xf - (v - vr)) / self.tau
+        else:
+            v_tmp = v - (v - vr) / self.tau + xf
+        spike = (v_tmp >= self.v_threshold).to(torch.float32)
+        if self.v_reset is None:
+            self.v = v_tmp - spike * self.v_threshold
+        else:
+            self.v = torch.where(spike.bool(), torch.full_like(v_tmp, vr), v_tmp)
+        return spike.to(x.dtype)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self.step_mode == "s":
+            return self._step(x)
+        return torch.stack([self._step(x[t]) for t in range(x.shape[0])], 0)
+
+    def extra_repr(self):
+        return f"tau={self.tau}, v_threshold={self.v_threshold}, v_reset={self.v_reset}, step_mode={self.step_mode}"
+
+
+def reset_net(model: nn.Module) -> None:
+    """Clear the membrane state of every stateful module (spikingjelly's functional.reset_net)."""
+    for m in model.modules():
+        if hasattr(m, "reset") and callable(m.reset) and m is not model:
+            m.reset()

@@ -1,0 +1,11 @@
+// Sparse-conv kernel instantiations for __nv_bfloat16 activations (split per dtype so
+// the build compiles them in parallel).
+#include "conv_kernel.cuh"
+
+namespace sf {
+namespace conv {
+sf_status dispatch_bf16(bool lif, int wdt, int K, int S, const ConvParams& p, const Plan& pl, cudaStream_t st) {
+  return dispatch_x<__nv_bfloat16>(lif, wdt, K, S, p, pl, st);
+}
+}  // namespace conv
+}  // namespace sf

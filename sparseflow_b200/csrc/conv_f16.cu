@@ -1,0 +1,11 @@
+// Sparse-conv kernel instantiations for __half activations (split per dtype so
+// the build compiles them in parallel).
+#include "conv_kernel.cuh"
+
+namespace sf {
+namespace conv {
+sf_status dispatch_f16(bool lif, int wdt, int K, int S, const ConvParams& p, const Plan& pl, cudaStream_t st) {
+  return dispatch_x<__half>(lif, wdt, K, S, p, pl, st);
+}
+}  // namespace conv
+}  // namespace sf

@@ -1,0 +1,149 @@
+"""Stage-2 sparse conv on the GPU vs the reference golden outputs and the CPU oracle."""
+import numpy as np
+import pytest
+import torch
+import torch.nn as nn
+
+from conftest import load_cases
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+CONV = load_cases("conv")
+RTOL = 1e-5  # fp32 weights: rel 1e-5 of the output scale
+
+
+def _assert_close(y, ref, rtol=RTOL):
+    y = np.asarray(y, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    scale = max(np.abs(ref).max(), 1e-6)
+    err = np.abs(y - ref).max()
+    assert err <= rtol * scale, f"max abs err {err} > {rtol} * {scale}"
+
+
+@pytest.mark.parametrize("case", sorted(CONV))
+def test_conv_matches_reference_golden(case):
+    from sparseflow_b200.Ops.sparse_conv2d import SparseConv2d
+    c = CONV[case]
+    k, s, p = (int(v) for v in c["geom"])
+    w = torch.from_numpy(c["w"])
+    conv = nn.Conv2d(w.shape[1], w.shape[0], k, s, p, bias="b" in c)
+    conv.weight.data.copy_(w)
+    if "b" in c:
+        conv.bias.data.copy_(torch.from_numpy(c["b"]))
+    sp = SparseConv2d.from_dense(conv.cuda(), block_size=8)
+    y = sp(torch.from_numpy(c["x"]).cuda())
+    assert tuple(y.shape) == c["y"].shape and y.dtype == torch.float32
+    _assert_close(y.cpu().numpy(), c["y"])
+
+
+GRID = [
+    # n, c, h, w, co, k, s, p, density
+    (2, 64, 32, 32, 64, 3, 1, 1, 0.02),
+    (3, 3, 17, 9, 8, 3, 1, 1, 1.0),
+    (2, 40, 13, 30, 24, 3, 1, 1, 0.1),
+    (2, 130, 14, 14, 100, 3, 1, 1, 0.05),
+    (2, 64, 56, 56, 64, 3, 1, 1, 0.01),
+    (1, 256, 56, 56, 64, 1, 1, 0, 0.02),
+    (2, 256, 28, 28, 200, 1, 1, 0, 0.05),
+    (2, 32, 15, 15, 64, 3, 2, 1, 0.1),
+    (2, 64, 56, 56, 128, 3, 2, 1, 0.02),
+    (4, 64, 7, 7, 64, 3, 1, 1, 0.2),
+    (2, 16, 57, 57, 32, 3, 1, 1, 0.05),
+    (2, 32, 1, 1, 16, 3, 1, 1, 1.0),
+    (1, 64, 20, 250, 32, 3, 1, 1, 0.01),
+    (3, 512, 7, 7, 512, 1, 1, 0, 0.01),
+    (2, 48, 12, 12, 256, 3, 1, 1, 0.0),
+]
+
+
+@pytest.mark.parametrize("n,c,h,w,co,k,s,p,density", GRID)
+def test_conv_vs_oracle(n, c, h, w, co, k, s, p, density):
+    from sparseflow_b200.Kernels.conv2d import sparse_conv2d_forward
+    g = torch.Generator().manual_seed(c * 31 + co + h)
+    x = (torch.rand(n, c, h, w, generator=g) < density).float()
+    if density == 1.0:
+        x = torch.randn(n, c, h, w, generator=g) * (torch.rand(n, c, h, w, generator=g) < 0.5)
+    wt = torch.randn(co, c, k, k, generator=g) * (2.0 / (c * k * k)) ** 0.5
+    b = torch.randn(co, generator=g) * 0.1
+    y, _ = sparse_conv2d_forward(x.cuda(), wt.cuda(), b.cuda(), kernel_size=k, stride=s, padding=p)
+    ref = oracle.conv2d(x.numpy(), wt.numpy(), b.numpy(), s, p)
+    _assert_close(y.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("xdt", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("wdt", [torch.float32, torch.bfloat16])
+def test_conv_dtypes_vs_oracle(xdt, wdt):
+    from sparseflow_b200.Kernels.conv2d import sparse_conv2d_forward
+    g = torch.Generator().manual_seed(11)
+    x = ((torch.rand(4, 64, 28, 28, generator=g) < 0.03).float()).to(xdt)
+    wt = (torch.randn(96, 64, 3, 3, generator=g) * 0.05).to(wdt)
+    y, _ = sparse_conv2d_forward(x.cuda(), wt.cuda(), None, kernel_size=3, stride=1, padding=1)
+    assert y.dtype == xdt
+    ref = oracle.conv2d(x.float().numpy(), wt.float().numpy(), None, 1, 1)
+    # fp32 accumulation; the only rounding is the final cast to the 16-bit output dtype
+    _assert_close(y.float().cpu().numpy(), ref, rtol=1e-2)
+
+
+def test_conv_bf16_weights_c2_like():
+    """C2-style 1x1 bottleneck with bf16 weights and fp32 spikes: within 1e-2 (bf16-weight bound)."""
+    from sparseflow_b200.Ops.sparse_conv2d import SparseConv2d
+    g = torch.Generator().manual_seed(5)
+    conv = nn.Conv2d(256, 64, 1, bias=False)
+    conv.weight.data = (torch.randn(64, 256, 1, 1, generator=g) * 0.02).bfloat16()
+    blk = (torch.rand(2, 4, 256, 4, 4, generator=g) < 0.05).float()
+    mask = blk.repeat_interleave(16, 3).repeat_interleave(16, 4)[..., :56, :56]
+    x = mask * (torch.rand(2, 4, 256, 56, 56, generator=g) < 0.3).float()
+    sp = SparseConv2d.from_dense(conv.cuda(), block_size=16)
+    y = sp(x.cuda())
+    ref = oracle.conv2d(x.reshape(8, 256, 56, 56).numpy(), conv.weight.float().numpy(), None, 1, 0)
+    _assert_close(y.reshape(8, 64, 56, 56).cpu().numpy(), ref, rtol=1e-5)
+
+
+def test_conv_deterministic_and_5d_shape():
+    from sparseflow_b200.Ops.sparse_conv2d import SparseConv2d
+    conv = nn.Conv2d(64, 64, 3, 1, 1).cuda()
+    sp = SparseConv2d.from_dense(conv, block_size=16)
+    g = torch.Generator(device="cuda").manual_seed(1)
+    x = (torch.rand(4, 8, 64, 32, 32, device="cuda", generator=g) < 0.02).float()
+    y1 = sp(x)
+    y2 = sp(x)
+    assert y1.shape == (4, 8, 64, 32, 32)
+    assert torch.equal(y1, y2)
+
+
+def test_conv_full_size_c5_cell_vs_cudnn_fp32():
+    """Full bench workload (T=16, N=64, C=64, 56x56, p=0.01): against cuDNN with TF32 off."""
+    from sparseflow_b200.Kernels.conv2d import sparse_conv2d_forward
+    g = torch.Generator(device="cuda").manual_seed(2)
+    x = (torch.rand(1024, 64, 56, 56, device="cuda", generator=g) < 0.01).float()
+    w = torch.randn(64, 64, 3, 3, device="cuda", generator=g) * 0.06
+    b = torch.randn(64, device="cuda", generator=g) * 0.1
+    y, _ = sparse_conv2d_forward(x, w, b, kernel_size=3, stride=1, padding=1)
+    prev = torch.backends.cudnn.allow_tf32
+    torch.backends.cudnn.allow_tf32 = False
+    try:
+        ref = torch.nn.functional.conv2d(x, w, b, 1, 1)
+    finally:
+        torch.backends.cudnn.allow_tf32 = prev
+    err = (y - ref).abs().max().item()
+    assert err <= RTOL * ref.abs().max().item()
+    y2, _ = sparse_conv2d_forward(x, w, b, kernel_size=3, stride=1, padding=1)
+    assert torch.equal(y, y2)
+
+
+def test_conv_metadata_buffers_match_prescan():
+    from sparseflow_b200.Kernels.conv2d import sparse_conv2d_forward
+    g = torch.Generator().manual_seed(9)
+    x = (torch.rand(4, 64, 32, 32, generator=g) < 0.0005).float()
+    w = torch.randn(64, 64, 3, 3, generator=g) * 0.05
+    nt = 4 * 4 * 4
+    agb = torch.empty(nt, dtype=torch.int32, device="cuda")
+    tcb = torch.empty(nt, dtype=torch.int32, device="cuda")
+    y, ms, ratio, stats, meta = sparse_conv2d_forward(
+        x.cuda(), w.cuda(), None, kernel_size=3, stride=1, padding=1, ag_mask_buf=agb, tile_class_buf=tcb,
+        return_ms=True, return_avg_active_ratio=True, return_tile_stats=True, return_backend_meta=True)
+    oag, otc, oids = oracle.prescan2d(x.numpy(), 0, 32, 32, 3, 1, 1, 8, 8, 16, 1e-6)
+    np.testing.assert_array_equal(agb.cpu().numpy(), oag)
+    assert stats["zero_tiles"] == int((otc == 0).sum())
+    assert ms > 0 and meta["backend"] == "sparse_b200"
