@@ -110,7 +110,11 @@ typedef struct sf_conv_desc {
 } sf_conv_desc;
 
 /* y = conv2d(x, w) + bias, computed in fp32 over the nonzero input elements
- * only (exact zeros contribute nothing, so skipping them is exact). */
+ * only (exact zeros contribute nothing, so skipping them is exact).
+ * x must be 16-byte aligned and readable up to the next 16-byte boundary past
+ * its last element (the input rows are moved as 16-byte aligned ranges); any
+ * allocation from cudaMalloc or the torch caching allocator that starts at x
+ * satisfies this. The same holds for x of sf_fused_conv_lif. */
 sf_status sf_sparse_conv2d(const void* x, const void* w_packed, const float* bias,
                            void* y, const sf_conv_desc* d, void* stream);
 

@@ -29,11 +29,14 @@ namespace sf {
 namespace conv {
 
 
-constexpr int kNWarps = 16;
+constexpr int kNWarps = 32;
 constexpr int kThreads = kNWarps * 32;
-constexpr int kCC = 32;  // channels per chunk (one mask bit each)
+constexpr int kCC = 16;  // channels per chunk (one mask bit each)
 constexpr int kMaxStages = 4;
 constexpr int kSmemLimit = 227 * 1024;
+// Shared memory the planner aims to stay under, so that the L1 share of the
+// SM's 256 KB keeps the packed weights of a layer resident.
+constexpr int kSmemBudget = 96 * 1024;
 
 
 struct ConvParams {
@@ -72,6 +75,8 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_conv_kernel(const ConvPara
   constexpr int KK = K * K;
   constexpr int COB = 32 * CPL;
   constexpr int ESZ = (int)sizeof(XT);
+  // Pixel slots per warp written back per epilogue pass (bounds out_s).
+  constexpr int IPASS = (CPL == 4) ? 1 : 2;
 
   XT* stages = reinterpret_cast<XT*>(smem);
   float* out_s = reinterpret_cast<float*>(smem + p.out_off);
@@ -154,20 +159,28 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_conv_kernel(const ConvPara
     const size_t hw_out = (size_t)p.Ho * p.Wo;
 
     if (LIF) {
-      // v[n, co, r0:r0+rows_out, :] -> out_s (coalesced) -> registers.
-      for (int idx = tid; idx < COB * npix; idx += kThreads) {
-        const int col = idx / npix, pix = idx - col * npix;
-        const int co = co_base + col;
-        out_s[col * p.os + pix] = (co < p.Co) ? p.v[((size_t)n * p.Co + co) * hw_out + (size_t)r0 * p.Wo + pix] : 0.f;
-      }
-      __syncthreads();
+      // v[n, co, band pixels] -> out_s (coalesced) -> registers, one pass of
+      // IPASS pixel slots per warp at a time.
 #pragma unroll
-      for (int i = 0; i < PPW; ++i) {
-        const int pix = warp + i * kNWarps;
+      for (int i0 = 0; i0 < PPW; i0 += IPASS) {
+        const int pbase = i0 * kNWarps;
+        const int pcnt = min(IPASS * kNWarps, npix - pbase);
+        for (int idx = tid; idx < COB * pcnt; idx += kThreads) {
+          const int col = idx / pcnt, pp = idx - col * pcnt;
+          const int co = co_base + col;
+          out_s[col * p.os + pp] =
+              (co < p.Co) ? p.v[((size_t)n * p.Co + co) * hw_out + (size_t)r0 * p.Wo + pbase + pp] : 0.f;
+        }
+        __syncthreads();
 #pragma unroll
-        for (int j = 0; j < CPL; ++j) vreg[i][j] = (pix < npix) ? out_s[(j * 32 + lane) * p.os + pix] : 0.f;
+        for (int ii = 0; ii < IPASS; ++ii) {
+          const int pix = warp + (i0 + ii) * kNWarps;
+#pragma unroll
+          for (int j = 0; j < CPL; ++j)
+            vreg[i0 + ii][j] = (pix < npix) ? out_s[(j * 32 + lane) * p.os + warp + ii * kNWarps] : 0.f;
+        }
+        __syncthreads();
       }
-      __syncthreads();
     }
 
     for (int t = 0; t < T; ++t) {
@@ -189,20 +202,27 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_conv_kernel(const ConvPara
         const int c0 = k * kCC;
         const int cc = min(kCC, p.C - c0);
 
-        // Per-halo-pixel nonzero-channel masks.
-        for (int q = tid; q < p.th_in * p.W; q += kThreads) {
+        // Per-halo-pixel nonzero-channel masks: four lanes per pixel, four
+        // channels each, combined with shuffles.
+        const int mtotal = p.th_in * p.W * 4;
+        for (int base = 0; base < mtotal; base += kThreads) {
+          const int it = base + tid;  // every lane iterates, so the shuffles below see full warps
+          const int q = it >> 2, part = it & 3;
           const int hl = q / p.W;
           const int iw = q - hl * p.W;
           const int ih = ihs + hl;
           uint32_t m = 0;
-          if (ih >= ih_lo && ih < ih_hi) {
+          if (it < mtotal && ih >= ih_lo && ih < ih_hi) {
             const int off = (ih - ih_lo) * p.W + iw;
-            for (int ci = 0; ci < cc; ++ci) {
-              const XT v = st[ci * p.slot_elems + e0[ci] + off];
-              m |= (uint32_t)DT<XT>::nonzero(v) << ci;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int ci = part * 4 + u;
+              if (ci < cc) m |= (uint32_t)DT<XT>::nonzero(st[ci * p.slot_elems + e0[ci] + off]) << ci;
             }
           }
-          masks[q] = m;
+          m |= __shfl_xor_sync(0xffffffffu, m, 1);
+          m |= __shfl_xor_sync(0xffffffffu, m, 2);
+          if (part == 0 && it < mtotal) masks[q] = m;
         }
         __syncthreads();
 
@@ -242,62 +262,76 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_conv_kernel(const ConvPara
         }
       }
 
-      // Epilogue for (unit, t).
-#pragma unroll
-      for (int i = 0; i < PPW; ++i) {
-        const int pix = warp + i * kNWarps;
-        if (pix < npix) {
-#pragma unroll
-          for (int j = 0; j < CPL; ++j) {
-            const int col = j * 32 + lane;
-            const int co = co_base + col;
-            const float b = (p.bias != nullptr && co < p.Co) ? __ldg(p.bias + co) : 0.f;
-            float val = acc[i][j] + b;
-            if (LIF) {
-              const float vp = vreg[i][j];
-              const float vr = p.hard_reset ? p.vreset : 0.f;
-              float vt;
-              if (p.decay_input)
-                vt = vp + (val - (vp - vr)) / p.tau;
-              else
-                vt = vp - (vp - vr) / p.tau + val;
-              const bool spk = vt >= p.vth;
-              vreg[i][j] = p.hard_reset ? (spk ? p.vreset : vt) : (vt - (spk ? p.vth : 0.f));
-              val = spk ? 1.f : 0.f;
-            }
-            out_s[col * p.os + pix] = val;
-          }
-        }
-      }
-      __syncthreads();
+      // Epilogue for (unit, t), in passes of IPASS pixel slots per warp.
       {
         XT* y = static_cast<XT*>(p.y);
         const size_t img = (size_t)(LIF ? t * p.N + n : n);
-        for (int idx = tid; idx < COB * npix; idx += kThreads) {
-          const int col = idx / npix, pix = idx - col * npix;
-          const int co = co_base + col;
-          if (co < p.Co) y[(img * p.Co + co) * hw_out + (size_t)r0 * p.Wo + pix] = DT<XT>::from_f(out_s[col * p.os + pix]);
+#pragma unroll
+        for (int i0 = 0; i0 < PPW; i0 += IPASS) {
+          const int pbase = i0 * kNWarps;
+          if (pbase < npix) {
+#pragma unroll
+            for (int ii = 0; ii < IPASS; ++ii) {
+              const int i = i0 + ii;
+              const int pix = warp + i * kNWarps;
+              if (pix < npix) {
+#pragma unroll
+                for (int j = 0; j < CPL; ++j) {
+                  const int col = j * 32 + lane;
+                  const int co = co_base + col;
+                  const float b = (p.bias != nullptr && co < p.Co) ? __ldg(p.bias + co) : 0.f;
+                  float val = acc[i][j] + b;
+                  if (LIF) {
+                    const float vp = vreg[i][j];
+                    const float vr = p.hard_reset ? p.vreset : 0.f;
+                    float vt;
+                    if (p.decay_input)
+                      vt = vp + (val - (vp - vr)) / p.tau;
+                    else
+                      vt = vp - (vp - vr) / p.tau + val;
+                    const bool spk = vt >= p.vth;
+                    vreg[i][j] = p.hard_reset ? (spk ? p.vreset : vt) : (vt - (spk ? p.vth : 0.f));
+                    val = spk ? 1.f : 0.f;
+                  }
+                  out_s[col * p.os + warp + ii * kNWarps] = val;
+                }
+              }
+            }
+          }
+          __syncthreads();
+          const int pcnt = min(IPASS * kNWarps, npix - pbase);
+          for (int idx = tid; idx < COB * pcnt; idx += kThreads) {
+            const int col = idx / pcnt, pp = idx - col * pcnt;
+            const int co = co_base + col;
+            if (co < p.Co)
+              y[(img * p.Co + co) * hw_out + (size_t)r0 * p.Wo + pbase + pp] = DT<XT>::from_f(out_s[col * p.os + pp]);
+          }
+          __syncthreads();
         }
       }
-      __syncthreads();
     }
 
     if (LIF) {
 #pragma unroll
-      for (int i = 0; i < PPW; ++i) {
-        const int pix = warp + i * kNWarps;
-        if (pix < npix) {
+      for (int i0 = 0; i0 < PPW; i0 += IPASS) {
+        const int pbase = i0 * kNWarps;
 #pragma unroll
-          for (int j = 0; j < CPL; ++j) out_s[(j * 32 + lane) * p.os + pix] = vreg[i][j];
+        for (int ii = 0; ii < IPASS; ++ii) {
+          const int pix = warp + (i0 + ii) * kNWarps;
+          if (pix < npix) {
+#pragma unroll
+            for (int j = 0; j < CPL; ++j) out_s[(j * 32 + lane) * p.os + warp + ii * kNWarps] = vreg[i0 + ii][j];
+          }
         }
+        __syncthreads();
+        const int pcnt = min(IPASS * kNWarps, npix - pbase);
+        for (int idx = tid; idx < COB * pcnt; idx += kThreads) {
+          const int col = idx / pcnt, pp = idx - col * pcnt;
+          const int co = co_base + col;
+          if (co < p.Co) p.v[((size_t)n * p.Co + co) * hw_out + (size_t)r0 * p.Wo + pbase + pp] = out_s[col * p.os + pp];
+        }
+        __syncthreads();
       }
-      __syncthreads();
-      for (int idx = tid; idx < COB * npix; idx += kThreads) {
-        const int col = idx / npix, pix = idx - col * npix;
-        const int co = co_base + col;
-        if (co < p.Co) p.v[((size_t)n * p.Co + co) * hw_out + (size_t)r0 * p.Wo + pix] = out_s[col * p.os + pix];
-      }
-      __syncthreads();
     }
   }
 }
@@ -312,6 +346,10 @@ sf_status launch_conv(const ConvParams& p, int smem, cudaStream_t st) {
   auto kern = sparse_conv_kernel<K, S, CPL, PPW, XT, WT, LIF>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return SF_ERR_CUDA;
+  // Prefer L1 over shared memory: the driver still grants the dynamic shared
+  // memory the launch needs, and the rest of the SM's array caches weights.
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 0) != cudaSuccess)
+    return SF_ERR_CUDA;
   const int grid = std::max(1, std::min(p.n_units, num_sms_current_device()));
   kern<<<grid, kThreads, smem, st>>>(p);
   return cudaGetLastError() == cudaSuccess ? SF_OK : SF_ERR_CUDA;
@@ -319,10 +357,10 @@ sf_status launch_conv(const ConvParams& p, int smem, cudaStream_t st) {
 
 template <int K, int S, typename XT, typename WT, bool LIF>
 sf_status dispatch_cpl(const ConvParams& p, const Plan& pl, cudaStream_t st) {
-  if (pl.CPL == 1) return launch_conv<K, S, 1, 16, XT, WT, LIF>(p, pl.smem, st);
-  if (pl.CPL == 2) return launch_conv<K, S, 2, 16, XT, WT, LIF>(p, pl.smem, st);
-  if constexpr (LIF) return launch_conv<K, S, 4, 8, XT, WT, LIF>(p, pl.smem, st);
-  else return launch_conv<K, S, 4, 16, XT, WT, LIF>(p, pl.smem, st);
+  if (pl.CPL == 1) return launch_conv<K, S, 1, 8, XT, WT, LIF>(p, pl.smem, st);
+  if (pl.CPL == 2) return launch_conv<K, S, 2, 8, XT, WT, LIF>(p, pl.smem, st);
+  if constexpr (LIF) return launch_conv<K, S, 4, 4, XT, WT, LIF>(p, pl.smem, st);
+  else return launch_conv<K, S, 4, 8, XT, WT, LIF>(p, pl.smem, st);
 }
 
 template <typename XT, typename WT, bool LIF>

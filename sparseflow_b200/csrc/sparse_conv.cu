@@ -40,7 +40,8 @@ __global__ void pack_weights_kernel(const void* __restrict__ w, int src_dtype, W
 bool make_plan(int K, int S, int P, int C, int H, int W, int Co, int Ho, int Wo, int esz, bool lif, Plan& pl) {
   (void)C; (void)H; (void)P;
   pl.CPL = Co <= 32 ? 1 : (Co <= 64 ? 2 : 4);
-  pl.PPW = (lif && pl.CPL == 4) ? 8 : 16;
+  pl.PPW = (lif && pl.CPL == 4) ? 4 : 8;
+  const int ipass = pl.CPL == 4 ? 1 : 2;
   const int npix_cap = kNWarps * pl.PPW;
   if (Wo > npix_cap) return false;
   const int COB = 32 * pl.CPL;
@@ -48,14 +49,15 @@ bool make_plan(int K, int S, int P, int C, int H, int W, int Co, int Ho, int Wo,
     const int th_in = (TH - 1) * S + K;
     const int slot_bytes = ((th_in * W * esz + 15) / 16) * 16 + 16;
     const int stage_bytes = kCC * slot_bytes;
-    const int npix = TH * Wo;
-    const int os = npix | 1;
+    const int os = (ipass * kNWarps) | 1;
     const int out_bytes = ((COB * os * 4 + 15) / 16) * 16;
     const int mask_bytes = ((th_in * W * 4 + 15) / 16) * 16;
     const int e0_bytes = kMaxStages * kCC;
     const int bar_bytes = kMaxStages * 8;
     const int fixed = out_bytes + mask_bytes + e0_bytes + bar_bytes + 64;
-    int nstage = std::min(kMaxStages, (kSmemLimit - fixed) / stage_bytes);
+    // As many stages as fit the L1-friendly budget (at least 2, within the hard limit).
+    int nstage = std::min(kMaxStages, (kSmemBudget - fixed) / stage_bytes);
+    if (nstage < 2) nstage = std::min(2, (kSmemLimit - fixed) / stage_bytes);
     if (nstage < 2) continue;
     pl.TH = TH;
     pl.th_in = th_in;
@@ -110,9 +112,6 @@ sf_status conv_common(const void* x, const void* w_packed, const float* bias, vo
   const size_t esz = dtype_size(xdt);
   if (esz == 0 || (wdt != SF_DTYPE_F32 && wdt != SF_DTYPE_BF16)) return SF_ERR_INVALID_ARG;
   if (!aligned16(x) || !aligned16(w_packed)) return SF_ERR_ALIGNMENT;
-  // The bulk copies round each channel's byte range out to 16 bytes; the
-  // whole input must therefore span a multiple of 16 bytes.
-  if (((size_t)T * N * C * H * W * esz) % 16 != 0) return SF_ERR_ALIGNMENT;
   if (!make_plan(K, S, P, C, H, W, Co, Ho, Wo, (int)esz, lif, pl)) return SF_ERR_UNSUPPORTED;
   p.x = x;
   p.wp = w_packed;

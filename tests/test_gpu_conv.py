@@ -94,9 +94,10 @@ def test_conv_bf16_weights_c2_like():
     blk = (torch.rand(2, 4, 256, 4, 4, generator=g) < 0.05).float()
     mask = blk.repeat_interleave(16, 3).repeat_interleave(16, 4)[..., :56, :56]
     x = mask * (torch.rand(2, 4, 256, 56, 56, generator=g) < 0.3).float()
+    w_ref = conv.weight.detach().float().numpy().copy()
     sp = SparseConv2d.from_dense(conv.cuda(), block_size=16)
     y = sp(x.cuda())
-    ref = oracle.conv2d(x.reshape(8, 256, 56, 56).numpy(), conv.weight.float().numpy(), None, 1, 0)
+    ref = oracle.conv2d(x.reshape(8, 256, 56, 56).numpy(), w_ref, None, 1, 0)
     _assert_close(y.reshape(8, 64, 56, 56).cpu().numpy(), ref, rtol=1e-5)
 
 

@@ -75,11 +75,12 @@ def test_fused_conv_bn_lif_c3_like_vs_oracle():
     bn.running_var = torch.rand(C, generator=g) + 0.5
     lif = LIFNode(tau=2.0, v_threshold=1.0, v_reset=0.0)
     x = (torch.rand(16, 4, C, 28, 28, generator=g) < 0.02).float()
+    bnp = dict(mean=bn.running_mean.numpy().copy(), var=bn.running_var.numpy().copy(),
+               gamma=bn.weight.detach().numpy().copy(), beta=bn.bias.detach().numpy().copy(), eps=bn.eps)
+    w_ref = conv.weight.detach().numpy().copy()
     mod = FusedSparseConvLIF.from_conv_bn_lif(conv.cuda(), bn.cuda(), lif)
     sp = mod(x.cuda()).cpu().numpy()
-    bnp = dict(mean=bn.running_mean.numpy(), var=bn.running_var.numpy(), gamma=bn.weight.detach().numpy(),
-               beta=bn.bias.detach().numpy(), eps=bn.eps)
-    ref_sp, near, v_ref = _oracle_with_margin(x.numpy(), conv.weight.detach().numpy(), None, bnp, 2.0, 1.0, 0.0, True)
+    ref_sp, near, v_ref = _oracle_with_margin(x.numpy(), w_ref, None, bnp, 2.0, 1.0, 0.0, True)
     diff = sp != ref_sp
     # Once a near-threshold spike flips, that neuron's later trajectory may
     # legitimately differ; require every first mismatch per neuron to be a near-tie.
