@@ -89,6 +89,24 @@ sf_status sf_prescan2d(const void* x, const sf_prescan_desc* d,
  * workspace: SF_OK or SF_ERR_DEVICE_TIMEOUT. Not for hot loops. */
 sf_status sf_prescan2d_status(void* workspace, void* stream);
 
+/* sf_prescan2d without a workspace argument, for callers that cannot allocate
+ * device memory at the point they run the prescan (a host runtime that owns
+ * every allocation, or a hot path where cudaMalloc would synchronise). No
+ * counterpart in the reference: its prescan allocates through torch.
+ * The look-back workspace is a static device array inside this library, sized
+ * for at most SF_PRESCAN_STATIC_MAX_ROWS tile rows (n * ceil(h_out / block_h),
+ * 256 KiB + 16 bytes per GPU, held until process exit); larger requests
+ * return SF_ERR_WORKSPACE. The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress); make that first call before any
+ * stream capture. Each call clears the counters it needs and allocates
+ * nothing. All calls share the one array, so calls that may overlap on the
+ * GPU (different streams, or several host threads) race and must be
+ * serialised by the caller. */
+#define SF_PRESCAN_STATIC_MAX_ROWS 32768
+sf_status sf_prescan2d_static_ws(const void* x, const sf_prescan_desc* d,
+                                 int32_t* ag_mask, int32_t* tile_class,
+                                 int32_t* active_ids, int32_t* active_count, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Stage 2: gather-style sparse convolution (deterministic, atomic-free).    */
 /* ------------------------------------------------------------------------ */

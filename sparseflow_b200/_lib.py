@@ -80,6 +80,7 @@ _SIGNATURES = {
     "sf_prescan2d": (ctypes.c_int32, [_VP, ctypes.POINTER(PrescanDesc), _VP, _VP, _VP, _VP, _VP,
                                       ctypes.c_size_t, _VP]),
     "sf_prescan2d_status": (ctypes.c_int32, [_VP, _VP]),
+    "sf_prescan2d_static_ws": (ctypes.c_int32, [_VP, ctypes.POINTER(PrescanDesc), _VP, _VP, _VP, _VP, _VP]),
     "sf_packed_weight_bytes": (ctypes.c_size_t, [ctypes.c_int32] * 4),
     "sf_pack_weights": (ctypes.c_int32, [_VP, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                          ctypes.c_int32, _VP, _VP]),

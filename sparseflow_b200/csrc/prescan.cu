@@ -411,3 +411,61 @@ extern "C" sf_status sf_prescan2d_status(void* workspace, void* stream) {
   if (cudaStreamSynchronize(st) != cudaSuccess) return SF_ERR_CUDA;
   return err ? SF_ERR_DEVICE_TIMEOUT : SF_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of sf_prescan2d.
+//
+// Some callers cannot allocate device memory when they run the prescan:
+// code inside a host runtime that owns all allocations (an engine with a
+// fixed arena, a plugin whose host forbids cudaMalloc while it executes), or
+// a hot path where an allocation would synchronise the device. For them the
+// look-back workspace lives in this file-scope device array instead of a
+// caller buffer. It is sized for SF_PRESCAN_STATIC_MAX_ROWS tile rows
+// (n * ceil(h_out / block_h)); every GPU that loads this library holds it
+// until the process exits.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+namespace {
+
+constexpr size_t kStaticWsBytes = 16 + 8 * (size_t)SF_PRESCAN_STATIC_MAX_ROWS;
+static __device__ __align__(256) unsigned char g_prescan_static_ws[kStaticWsBytes];
+
+std::mutex g_static_ws_mu;
+void* g_static_ws_ptr[64] = {nullptr};
+
+// Device address of g_prescan_static_ws on the current device, looked up
+// once per device (the host-side symbol is not a device address).
+sf_status static_ws_for_current_device(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return SF_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(g_static_ws_mu);
+  if (g_static_ws_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_prescan_static_ws) != cudaSuccess || ptr == nullptr) return SF_ERR_CUDA;
+    g_static_ws_ptr[dev] = ptr;
+  }
+  *out = g_static_ws_ptr[dev];
+  return SF_OK;
+}
+
+}  // namespace
+
+extern "C" sf_status sf_prescan2d_static_ws(const void* x, const sf_prescan_desc* d, int32_t* ag_mask,
+                                            int32_t* tile_class, int32_t* active_ids, int32_t* active_count,
+                                            void* stream) {
+  const size_t need = sf_prescan2d_workspace_size(d);
+  if (need == 0) return validate_prescan(d) != SF_OK ? validate_prescan(d) : SF_ERR_INVALID_ARG;
+  if (need > kStaticWsBytes) return SF_ERR_WORKSPACE;  // more than SF_PRESCAN_STATIC_MAX_ROWS tile rows
+  void* ws = nullptr;
+  sf_status s = static_ws_for_current_device(&ws);
+  if (s != SF_OK) return s;
+  // The array keeps the previous call's contents. The ticket and done
+  // counters (bytes 0-7) and the error word (bytes 12-15) must start at zero;
+  // the epoch word (bytes 8-11) must not be reset, since it keeps the
+  // previous call's look-back status words from being read as current.
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(ws, 0, 8, st) != cudaSuccess) return SF_ERR_CUDA;
+  if (cudaMemsetAsync(static_cast<char*>(ws) + 12, 0, 4, st) != cudaSuccess) return SF_ERR_CUDA;
+  return sf_prescan2d(x, d, ag_mask, tile_class, active_ids, active_count, ws, kStaticWsBytes, stream);
+}
