@@ -14,7 +14,11 @@ from typing import Optional
 
 import torch
 
-LIB_PATH = Path(__file__).resolve().parent / "libsparseflow_b200.so"
+import os
+
+# SPARSEFLOW_B200_LIB may point at another build of the same ABI (e.g. an
+# instrumented one); by default the in-tree library is used.
+LIB_PATH = Path(os.environ.get("SPARSEFLOW_B200_LIB", Path(__file__).resolve().parent / "libsparseflow_b200.so"))
 
 SF_OK = 0
 SF_ERR_INVALID_ARG = 1

@@ -1,6 +1,9 @@
 // C-ABI entry points of stage 2 (sparse conv) and of the fused conv+LIF
 // kernel: argument checks, launch planning, weight packing. The kernel itself
 // is in conv_kernel.cuh.
+#include <cstdlib>
+#include <cstring>
+#include <cudaTypedefs.h>
 #include "conv_kernel.cuh"
 
 namespace sf {
@@ -37,39 +40,57 @@ __global__ void pack_weights_kernel(const void* __restrict__ w, int src_dtype, W
   }
 }
 
+int env_int(const char* name) {
+  const char* v = getenv(name);
+  return v ? atoi(v) : 0;
+}
+
+// Launch plan: output channels per lane (CPL), row-segment length R, band
+// height TH (one row segment per warp), channels per chunk (cc) and stages.
+// SF_CONV_CC / SF_CONV_TH / SF_CONV_NSTAGE (environment) pin one of them for
+// tuning sweeps.
 bool make_plan(int K, int S, int P, int C, int H, int W, int Co, int Ho, int Wo, int esz, bool lif, Plan& pl) {
-  (void)C; (void)H; (void)P;
+  (void)H; (void)P; (void)lif;
+  // A 4-D tensor map needs 16-byte row pitch and box extents <= 256.
+  const bool tmap_ok = (W * esz) % 16 == 0 && W <= 256 && env_int("SF_CONV_NO_TMA") == 0;
+  const int force_cc = env_int("SF_CONV_CC"), force_th = env_int("SF_CONV_TH"), force_ns = env_int("SF_CONV_NSTAGE");
   pl.CPL = Co <= 32 ? 1 : (Co <= 64 ? 2 : 4);
-  pl.PPW = (lif && pl.CPL == 4) ? 4 : 8;
-  const int ipass = pl.CPL == 4 ? 1 : 2;
-  const int npix_cap = kNWarps * pl.PPW;
-  if (Wo > npix_cap) return false;
-  const int COB = 32 * pl.CPL;
-  for (int TH = std::min(Ho, npix_cap / Wo); TH >= 1; --TH) {
-    const int th_in = (TH - 1) * S + K;
-    const int slot_bytes = ((th_in * W * esz + 15) / 16) * 16 + 16;
-    const int stage_bytes = kCC * slot_bytes;
-    const int os = (ipass * kNWarps) | 1;
-    const int out_bytes = ((COB * os * 4 + 15) / 16) * 16;
-    const int mask_bytes = ((th_in * W * 4 + 15) / 16) * 16;
-    const int e0_bytes = kMaxStages * kCC;
-    const int bar_bytes = kMaxStages * 8;
-    const int fixed = out_bytes + mask_bytes + e0_bytes + bar_bytes + 64;
-    // As many stages as fit the L1-friendly budget (at least 2, within the hard limit).
-    int nstage = std::min(kMaxStages, (kSmemBudget - fixed) / stage_bytes);
-    if (nstage < 2) nstage = std::min(2, (kSmemLimit - fixed) / stage_bytes);
-    if (nstage < 2) continue;
-    pl.TH = TH;
-    pl.th_in = th_in;
-    pl.nstage = nstage;
-    pl.slot_elems = slot_bytes / esz;
-    pl.os = os;
-    pl.out_off = nstage * stage_bytes;
-    pl.mask_off = pl.out_off + out_bytes;
-    pl.e0_off = pl.mask_off + mask_bytes;
-    pl.bar_off = ((pl.e0_off + e0_bytes + 7) / 8) * 8;
-    pl.smem = pl.bar_off + bar_bytes;
-    return true;
+  pl.R = pl.CPL == 4 ? 4 : 8;
+  const int tpr = (Wo + pl.R - 1) / pl.R;
+  if (tpr > kNWarps) return false;
+  const int Wp = W + 2 + kMaskPadR;
+  const int th_max = std::min(Ho, kNWarps / tpr);
+  for (int cc = std::min(kCC, ((C + 7) / 8) * 8); cc >= 8; cc /= 2) {
+    if (force_cc && cc != force_cc) continue;
+    for (int TH = th_max; TH >= 1; --TH) {
+      if (force_th && TH != force_th) continue;
+      const int th_in = (TH - 1) * S + K;
+      // Tensor copies land densely (channel pitch th_in*W); bulk copies need
+      // 16 bytes of slack for the aligned-out byte range.
+      const int slot_bytes = tmap_ok ? th_in * W * esz : ((th_in * W * esz + 15) / 16) * 16 + 16;
+      const int stage_bytes = cc * slot_bytes;
+      const int mask_bytes = ((th_in * Wp * 8 + 15) / 16) * 16;
+      const int cb_bytes = ((kMaxStages * (kCC + 1) * 4 + 15) / 16) * 16;
+      const int bar_bytes = kMaxStages * 8;
+      const int fixed = mask_bytes + cb_bytes + bar_bytes + 64;
+      int nstage = std::min(kMaxStages, (kSmemLimit - fixed) / stage_bytes);
+      if (force_ns) {
+        if (force_ns > nstage) continue;
+        nstage = force_ns;
+      }
+      if (nstage < 2) continue;
+      pl.cc = cc;
+      pl.use_tmap = tmap_ok ? 1 : 0;
+      pl.TH = TH;
+      pl.th_in = th_in;
+      pl.nstage = nstage;
+      pl.slot_elems = slot_bytes / esz;
+      pl.mask_off = nstage * stage_bytes;
+      pl.cb_off = pl.mask_off + mask_bytes;
+      pl.bar_off = ((pl.cb_off + cb_bytes + 7) / 8) * 8;
+      pl.smem = pl.bar_off + bar_bytes;
+      return true;
+    }
   }
   return false;
 }
@@ -94,16 +115,50 @@ int num_sms_current_device() {
 namespace conv {
 namespace {
 
-sf_status dispatch(bool lif, int xdt, int wdt, int K, int S, const ConvParams& p, const Plan& pl, cudaStream_t st) {
-  if (xdt == SF_DTYPE_F32) return dispatch_f32(lif, wdt, K, S, p, pl, st);
-  if (xdt == SF_DTYPE_F16) return dispatch_f16(lif, wdt, K, S, p, pl, st);
-  if (xdt == SF_DTYPE_BF16) return dispatch_bf16(lif, wdt, K, S, p, pl, st);
+sf_status dispatch(bool lif, int xdt, int wdt, int K, int S, const ConvParams& p, const CUtensorMap& tm,
+                   const Plan& pl, cudaStream_t st) {
+  if (xdt == SF_DTYPE_F32) return dispatch_f32(lif, wdt, K, S, p, tm, pl, st);
+  if (xdt == SF_DTYPE_F16) return dispatch_f16(lif, wdt, K, S, p, tm, pl, st);
+  if (xdt == SF_DTYPE_BF16) return dispatch_bf16(lif, wdt, K, S, p, tm, pl, st);
   return SF_ERR_UNSUPPORTED;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// x viewed as 4-D (W, H, C, T*N), box (W, th_in, cc, 1), zero fill outside.
+sf_status encode_x_map(CUtensorMap* m, const void* x, int xdt, int W, int H, int C, long long nimg, int th_in,
+                       int cc) {
+  auto fn = tensor_map_encoder();
+  if (!fn) return SF_ERR_CUDA;
+  const CUtensorMapDataType dt = xdt == SF_DTYPE_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : xdt == SF_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                       : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const cuuint64_t esz = dtype_size(xdt);
+  const cuuint64_t dims[4] = {(cuuint64_t)W, (cuuint64_t)H, (cuuint64_t)C, (cuuint64_t)nimg};
+  const cuuint64_t strides[3] = {W * esz, (cuuint64_t)H * W * esz, (cuuint64_t)C * H * W * esz};
+  const cuuint32_t box[4] = {(cuuint32_t)W, (cuuint32_t)th_in, (cuuint32_t)cc, 1u};
+  const cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
+  const CUresult r = fn(m, dt, 4, const_cast<void*>(x), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? SF_OK : SF_ERR_CUDA;
 }
 
 sf_status conv_common(const void* x, const void* w_packed, const float* bias, void* y, int T, int N, int C,
                       int H, int W, int Co, int Ho, int Wo, int K, int S, int P, int xdt, int wdt, bool lif,
-                      ConvParams& p, Plan& pl) {
+                      ConvParams& p, Plan& pl, CUtensorMap& tm) {
   if (!x || !w_packed || !y) return SF_ERR_INVALID_ARG;
   if (T <= 0 || N <= 0 || C <= 0 || H <= 0 || W <= 0 || Co <= 0 || Ho <= 0 || Wo <= 0) return SF_ERR_INVALID_ARG;
   if (!((K == 1 && S == 1 && P == 0) || (K == 3 && S == 1 && P == 1) || (K == 3 && S == 2 && P == 1)))
@@ -130,14 +185,22 @@ sf_status conv_common(const void* x, const void* w_packed, const float* bias, vo
   p.n_units = (int)units;
   p.th_in = pl.th_in;
   p.slot_elems = pl.slot_elems;
-  p.nchunks = (C + kCC - 1) / kCC;
+  p.cc = pl.cc;
+  p.nchunks = (C + pl.cc - 1) / pl.cc;
   p.nstage = pl.nstage;
-  p.os = pl.os;
-  p.out_off = pl.out_off;
+  p.tpr = (Wo + pl.R - 1) / pl.R;
   p.mask_off = pl.mask_off;
-  p.e0_off = pl.e0_off;
+  p.cb_off = pl.cb_off;
+  p.Wp = W + 2 + kMaskPadR;
   p.bar_off = pl.bar_off;
   p.tau = 1.f; p.vth = 1.f; p.vreset = 0.f; p.hard_reset = 1; p.decay_input = 1;
+  p.use_tmap = pl.use_tmap;
+  p.box_bytes = (uint32_t)((size_t)W * pl.th_in * pl.cc * esz);
+  memset(&tm, 0, sizeof(tm));
+  if (pl.use_tmap) {
+    sf_status s = encode_x_map(&tm, x, xdt, W, H, C, (long long)T * N, pl.th_in, pl.cc);
+    if (s != SF_OK) return s;
+  }
   return SF_OK;
 }
 
@@ -180,10 +243,11 @@ extern "C" sf_status sf_sparse_conv2d(const void* x, const void* w_packed, const
   if (d->has_bias && !bias) return SF_ERR_INVALID_ARG;
   ConvParams p;
   Plan pl;
+  CUtensorMap tm;
   sf_status s = conv_common(x, w_packed, d->has_bias ? bias : nullptr, y, 1, d->n, d->c_in, d->h, d->w, d->c_out,
-                            d->h_out, d->w_out, d->kernel, d->stride, d->padding, d->x_dtype, d->w_dtype, false, p, pl);
+                            d->h_out, d->w_out, d->kernel, d->stride, d->padding, d->x_dtype, d->w_dtype, false, p, pl, tm);
   if (s != SF_OK) return s;
-  return dispatch(false, d->x_dtype, d->w_dtype, d->kernel, d->stride, p, pl, static_cast<cudaStream_t>(stream));
+  return dispatch(false, d->x_dtype, d->w_dtype, d->kernel, d->stride, p, tm, pl, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" sf_status sf_fused_conv_lif(const void* x, const void* w_packed, const float* bias, float* v_inout,
@@ -193,9 +257,10 @@ extern "C" sf_status sf_fused_conv_lif(const void* x, const void* w_packed, cons
   if (!(d->tau > 0.f)) return SF_ERR_INVALID_ARG;
   ConvParams p;
   Plan pl;
+  CUtensorMap tm;
   sf_status s = conv_common(x, w_packed, d->has_bias ? bias : nullptr, spikes_out, d->t_steps, d->n, d->c_in, d->h,
                             d->w, d->c_out, d->h_out, d->w_out, d->kernel, d->stride, d->padding, d->x_dtype,
-                            d->w_dtype, true, p, pl);
+                            d->w_dtype, true, p, pl, tm);
   if (s != SF_OK) return s;
   p.v = v_inout;
   p.tau = d->tau;
@@ -203,7 +268,7 @@ extern "C" sf_status sf_fused_conv_lif(const void* x, const void* w_packed, cons
   p.vreset = d->hard_reset ? d->v_reset : 0.f;
   p.hard_reset = d->hard_reset;
   p.decay_input = d->decay_input;
-  return dispatch(true, d->x_dtype, d->w_dtype, d->kernel, d->stride, p, pl, static_cast<cudaStream_t>(stream));
+  return dispatch(true, d->x_dtype, d->w_dtype, d->kernel, d->stride, p, tm, pl, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" sf_status sf_sparse_conv2d_status(void* stream) {
