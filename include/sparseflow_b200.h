@@ -111,8 +111,9 @@ sf_status sf_prescan2d_static_ws(const void* x, const sf_prescan_desc* d,
 /* Stage 2: gather-style sparse convolution (deterministic, atomic-free).    */
 /* ------------------------------------------------------------------------ */
 
-/* Packed layout: [c_in][kernel*kernel][c_out_pad] with c_out_pad =
- * round_up(c_out, 128), zero padded; element type w_dst_dtype (F32 or BF16). */
+/* Packed layout: [c_in][kernel*kernel][c_out_pad], zero padded, element type
+ * w_dst_dtype (F32 or BF16); c_out_pad = c_out rounded up to 32 (c_out <= 32),
+ * 64 (c_out <= 64) or a multiple of 128. */
 size_t sf_packed_weight_bytes(int32_t c_out, int32_t c_in, int32_t kernel, int32_t w_dst_dtype);
 sf_status sf_pack_weights(const void* w_oihw, int32_t w_src_dtype,
                           int32_t c_out, int32_t c_in, int32_t kernel,

@@ -21,6 +21,8 @@ template <> struct DT<float> {
   static __device__ __forceinline__ float to_f(float v) { return v; }
   static __device__ __forceinline__ float from_f(float v) { return v; }
   static __device__ __forceinline__ bool nonzero(float v) { return v != 0.0f; }
+  static __device__ __forceinline__ uint32_t nz_bit(float v) { return (__float_as_uint(v) << 1) != 0u; }
+  static __device__ __forceinline__ uint32_t not_one(float v) { return __float_as_uint(v) != 0x3f800000u; }
 };
 template <> struct DT<__half> {
   static __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
@@ -28,6 +30,8 @@ template <> struct DT<__half> {
   static __device__ __forceinline__ bool nonzero(__half v) {
     return (__half_as_ushort(v) & 0x7fffu) != 0u;
   }
+  static __device__ __forceinline__ uint32_t nz_bit(__half v) { return (__half_as_ushort(v) & 0x7fffu) != 0u; }
+  static __device__ __forceinline__ uint32_t not_one(__half v) { return __half_as_ushort(v) != 0x3c00u; }
 };
 template <> struct DT<__nv_bfloat16> {
   static __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
@@ -35,6 +39,10 @@ template <> struct DT<__nv_bfloat16> {
   static __device__ __forceinline__ bool nonzero(__nv_bfloat16 v) {
     return (__bfloat16_as_ushort(v) & 0x7fffu) != 0u;
   }
+  static __device__ __forceinline__ uint32_t nz_bit(__nv_bfloat16 v) {
+    return (__bfloat16_as_ushort(v) & 0x7fffu) != 0u;
+  }
+  static __device__ __forceinline__ uint32_t not_one(__nv_bfloat16 v) { return __bfloat16_as_ushort(v) != 0x3f80u; }
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -46,50 +46,60 @@ int env_int(const char* name) {
 }
 
 // Launch plan: output channels per lane (CPL), row-segment length R, band
-// height TH (one row segment per warp), channels per chunk (cc) and stages.
-// SF_CONV_CC / SF_CONV_TH / SF_CONV_NSTAGE (environment) pin one of them for
-// tuning sweeps.
-bool make_plan(int K, int S, int P, int C, int H, int W, int Co, int Ho, int Wo, int esz, bool lif, Plan& pl) {
+// height TH (one row segment per compute warp), channels per chunk (cc),
+// stages, and whether the packed weights live in shared memory. The
+// environment variables SF_CONV_CC / SF_CONV_TH / SF_CONV_NSTAGE /
+// SF_CONV_NO_WSMEM / SF_CONV_NO_TMA pin choices for tuning sweeps.
+bool make_plan(int K, int S, int P, int C, int H, int W, int Co, int Ho, int Wo, int esz, int wsz, bool lif,
+               Plan& pl) {
   (void)H; (void)P; (void)lif;
-  // A 4-D tensor map needs 16-byte row pitch and box extents <= 256.
-  const bool tmap_ok = (W * esz) % 16 == 0 && W <= 256 && env_int("SF_CONV_NO_TMA") == 0;
   const int force_cc = env_int("SF_CONV_CC"), force_th = env_int("SF_CONV_TH"), force_ns = env_int("SF_CONV_NSTAGE");
+  // A 4-D tensor map needs a 16-byte row pitch and box extents <= 256.
+  const bool tmap_ok = (W * esz) % 16 == 0 && W <= 256 && env_int("SF_CONV_NO_TMA") == 0;
   pl.CPL = Co <= 32 ? 1 : (Co <= 64 ? 2 : 4);
   pl.R = pl.CPL == 4 ? 4 : 8;
   const int tpr = (Wo + pl.R - 1) / pl.R;
-  if (tpr > kNWarps) return false;
-  const int Wp = W + 2 + kMaskPadR;
-  const int th_max = std::min(Ho, kNWarps / tpr);
-  for (int cc = std::min(kCC, ((C + 7) / 8) * 8); cc >= 8; cc /= 2) {
-    if (force_cc && cc != force_cc) continue;
-    for (int TH = th_max; TH >= 1; --TH) {
-      if (force_th && TH != force_th) continue;
-      const int th_in = (TH - 1) * S + K;
-      // Tensor copies land densely (channel pitch th_in*W); bulk copies need
-      // 16 bytes of slack for the aligned-out byte range.
-      const int slot_bytes = tmap_ok ? th_in * W * esz : ((th_in * W * esz + 15) / 16) * 16 + 16;
-      const int stage_bytes = cc * slot_bytes;
-      const int mask_bytes = ((th_in * Wp * 8 + 15) / 16) * 16;
-      const int cb_bytes = ((kMaxStages * (kCC + 1) * 4 + 15) / 16) * 16;
-      const int bar_bytes = kMaxStages * 8;
-      const int fixed = mask_bytes + cb_bytes + bar_bytes + 64;
-      int nstage = std::min(kMaxStages, (kSmemLimit - fixed) / stage_bytes);
-      if (force_ns) {
-        if (force_ns > nstage) continue;
-        nstage = force_ns;
+  const int tpu = std::min(tpr, kComputeWarps);  // wider rows are split into column blocks
+  const int th_max = std::min(Ho, kComputeWarps / tpu);
+  const int ncob = (Co + co_block(Co) - 1) / co_block(Co);
+  const int w_bytes = C * K * K * co_padded(Co) * wsz;
+  const bool ws_ok = ncob == 1 && env_int("SF_CONV_NO_WSMEM") == 0;
+  const int cb_bytes = ((kMaxStages * kCbStride * 4 + 127) / 128) * 128;
+  const int bar_bytes = (2 * kMaxStages + 1) * 8;
+  for (int wsmem = ws_ok ? 1 : 0; wsmem >= 0; --wsmem) {
+    const int w_region = wsmem ? ((w_bytes + 127) / 128) * 128 : 0;
+    for (int cc = std::min(kCC, ((C + 7) / 8) * 8); cc >= 8; cc /= 2) {
+      if (force_cc && cc != force_cc) continue;
+      for (int TH = th_max; TH >= 1; --TH) {
+        if (force_th && TH != force_th) continue;
+        const int th_in = (TH - 1) * S + K;
+        // Tensor copies land densely (channel pitch th_in*W); bulk copies need
+        // 16 bytes of slack for the aligned-out byte range.
+        const int slot_bytes = tmap_ok ? th_in * W * esz : ((th_in * W * esz + 15) / 16) * 16 + 16;
+        const int stage_bytes = ((cc * slot_bytes + 127) / 128) * 128;
+        const int fixed = w_region + cb_bytes + bar_bytes;
+        if (fixed >= kSmemLimit) continue;
+        int nstage = std::min(kMaxStages, (kSmemLimit - fixed) / stage_bytes);
+        if (force_ns) {
+          if (force_ns > nstage) continue;
+          nstage = force_ns;
+        }
+        if (nstage < 2) continue;
+        // Stage pitch must stay a whole number of slots.
+        if (stage_bytes != cc * slot_bytes) continue;
+        pl.wsmem = wsmem;
+        pl.cc = cc;
+        pl.use_tmap = tmap_ok ? 1 : 0;
+        pl.TH = TH;
+        pl.th_in = th_in;
+        pl.nstage = nstage;
+        pl.slot_elems = slot_bytes / esz;
+        pl.w_off = nstage * stage_bytes;
+        pl.cb_off = pl.w_off + w_region;
+        pl.bar_off = pl.cb_off + cb_bytes;
+        pl.smem = pl.bar_off + bar_bytes;
+        return true;
       }
-      if (nstage < 2) continue;
-      pl.cc = cc;
-      pl.use_tmap = tmap_ok ? 1 : 0;
-      pl.TH = TH;
-      pl.th_in = th_in;
-      pl.nstage = nstage;
-      pl.slot_elems = slot_bytes / esz;
-      pl.mask_off = nstage * stage_bytes;
-      pl.cb_off = pl.mask_off + mask_bytes;
-      pl.bar_off = ((pl.cb_off + cb_bytes + 7) / 8) * 8;
-      pl.smem = pl.bar_off + bar_bytes;
-      return true;
     }
   }
   return false;
@@ -167,7 +177,7 @@ sf_status conv_common(const void* x, const void* w_packed, const float* bias, vo
   const size_t esz = dtype_size(xdt);
   if (esz == 0 || (wdt != SF_DTYPE_F32 && wdt != SF_DTYPE_BF16)) return SF_ERR_INVALID_ARG;
   if (!aligned16(x) || !aligned16(w_packed)) return SF_ERR_ALIGNMENT;
-  if (!make_plan(K, S, P, C, H, W, Co, Ho, Wo, (int)esz, lif, pl)) return SF_ERR_UNSUPPORTED;
+  if (!make_plan(K, S, P, C, H, W, Co, Ho, Wo, (int)esz, (int)dtype_size(wdt), lif, pl)) return SF_ERR_UNSUPPORTED;
   p.x = x;
   p.wp = w_packed;
   p.bias = bias;
@@ -175,12 +185,15 @@ sf_status conv_common(const void* x, const void* w_packed, const float* bias, vo
   p.v = nullptr;
   if (cudaGetSymbolAddress(reinterpret_cast<void**>(&p.err), g_conv_error) != cudaSuccess) return SF_ERR_CUDA;
   p.T = T; p.N = N; p.C = C; p.H = H; p.W = W; p.Co = Co; p.Ho = Ho; p.Wo = Wo; p.P = P;
-  p.Co_pad = ((Co + 127) / 128) * 128;
+  p.Co_pad = co_padded(Co);
   p.TH = pl.TH;
   p.nbands = (Ho + pl.TH - 1) / pl.TH;
   const int COB = 32 * pl.CPL;
   p.ncob = (Co + COB - 1) / COB;
-  const long long units = (long long)N * p.nbands * p.ncob;
+  p.tpr = (Wo + pl.R - 1) / pl.R;
+  p.tpu = std::min(p.tpr, kComputeWarps);
+  p.ncolb = (p.tpr + p.tpu - 1) / p.tpu;
+  const long long units = (long long)N * p.nbands * p.ncolb * p.ncob;
   if (units >= (1ll << 31)) return SF_ERR_UNSUPPORTED;
   p.n_units = (int)units;
   p.th_in = pl.th_in;
@@ -188,10 +201,9 @@ sf_status conv_common(const void* x, const void* w_packed, const float* bias, vo
   p.cc = pl.cc;
   p.nchunks = (C + pl.cc - 1) / pl.cc;
   p.nstage = pl.nstage;
-  p.tpr = (Wo + pl.R - 1) / pl.R;
-  p.mask_off = pl.mask_off;
+  p.w_off = pl.w_off;
+  p.w_bytes = (uint32_t)((size_t)C * K * K * p.Co_pad * dtype_size(wdt));
   p.cb_off = pl.cb_off;
-  p.Wp = W + 2 + kMaskPadR;
   p.bar_off = pl.bar_off;
   p.tau = 1.f; p.vth = 1.f; p.vreset = 0.f; p.hard_reset = 1; p.decay_input = 1;
   p.use_tmap = pl.use_tmap;
@@ -214,7 +226,7 @@ using namespace sf::conv;
 extern "C" size_t sf_packed_weight_bytes(int32_t c_out, int32_t c_in, int32_t kernel, int32_t w_dst_dtype) {
   if (c_out <= 0 || c_in <= 0 || kernel <= 0) return 0;
   const size_t esz = dtype_size(w_dst_dtype);
-  const size_t co_pad = ((size_t)(c_out + 127) / 128) * 128;
+  const size_t co_pad = (size_t)co_padded(c_out);
   return (size_t)c_in * kernel * kernel * co_pad * esz;
 }
 
@@ -223,7 +235,7 @@ extern "C" sf_status sf_pack_weights(const void* w_oihw, int32_t w_src_dtype, in
   if (!w_oihw || !w_packed || c_out <= 0 || c_in <= 0 || kernel <= 0) return SF_ERR_INVALID_ARG;
   if (dtype_size(w_src_dtype) == 0) return SF_ERR_INVALID_ARG;
   if (w_dst_dtype != SF_DTYPE_F32 && w_dst_dtype != SF_DTYPE_BF16) return SF_ERR_UNSUPPORTED;
-  const int co_pad = ((c_out + 127) / 128) * 128;
+  const int co_pad = co_padded(c_out);
   const int KK = kernel * kernel;
   const size_t total = (size_t)c_in * KK * co_pad;
   const int blocks = (int)std::min<size_t>((total + 255) / 256, 4096);

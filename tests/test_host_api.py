@@ -155,4 +155,4 @@ def test_native_argument_checks_without_gpu():
     assert lib.sf_prescan2d(None, ctypes.byref(d), None, None, None, None, None, 0, None) == _lib.SF_ERR_INVALID_ARG
     cd = _lib.ConvDesc(1, 8, 8, 8, 8, 8, 8, 5, 1, 2, 0, 0, 0)
     assert lib.sf_sparse_conv2d(16, 16, None, 16, ctypes.byref(cd), None) == _lib.SF_ERR_UNSUPPORTED
-    assert lib.sf_packed_weight_bytes(64, 32, 3, 0) == 32 * 9 * 128 * 4
+    assert lib.sf_packed_weight_bytes(64, 32, 3, 0) == 32 * 9 * 64 * 4
