@@ -111,9 +111,9 @@ sf_status sf_prescan2d_static_ws(const void* x, const sf_prescan_desc* d,
 /* Stage 2: gather-style sparse convolution (deterministic, atomic-free).    */
 /* ------------------------------------------------------------------------ */
 
-/* Packed layout: [c_in][kernel*kernel][c_out_pad], zero padded, element type
- * w_dst_dtype (F32 or BF16); c_out_pad = c_out rounded up to 32 (c_out <= 32),
- * 64 (c_out <= 64) or a multiple of 128. */
+/* Packed layout: [c_out_pad / 32][c_in][kernel*kernel][32] (slices of 32
+ * output channels), c_out_pad = c_out rounded up to a multiple of 128, zero
+ * padded; element type w_dst_dtype (F32 or BF16). */
 size_t sf_packed_weight_bytes(int32_t c_out, int32_t c_in, int32_t kernel, int32_t w_dst_dtype);
 sf_status sf_pack_weights(const void* w_oihw, int32_t w_src_dtype,
                           int32_t c_out, int32_t c_in, int32_t kernel,
@@ -128,14 +128,20 @@ typedef struct sf_conv_desc {
   int32_t has_bias;            /* bias: fp32 [c_out] */
 } sf_conv_desc;
 
+/* Bytes of caller-owned device workspace sf_sparse_conv2d needs (the
+ * per-pixel nonzero-channel masks of x: ceil(c_in/64) 64-bit words per pixel,
+ * plus one flag word per image). No initialisation is required. */
+size_t sf_sparse_conv2d_workspace_size(const sf_conv_desc* d);
+
 /* y = conv2d(x, w) + bias, computed in fp32 over the nonzero input elements
- * only (exact zeros contribute nothing, so skipping them is exact).
- * x must be 16-byte aligned and readable up to the next 16-byte boundary past
- * its last element (the input rows are moved as 16-byte aligned ranges); any
- * allocation from cudaMalloc or the torch caching allocator that starts at x
- * satisfies this. The same holds for x of sf_fused_conv_lif. */
+ * only (exact zeros contribute nothing, so skipping them is exact). Two
+ * launches: a streaming pass writes the nonzero-channel masks of x into the
+ * workspace, then the gather kernel reads masks (and x itself only for
+ * images holding values other than 0 and 1). w_packed must be 16-byte
+ * aligned; x has no alignment requirement. */
 sf_status sf_sparse_conv2d(const void* x, const void* w_packed, const float* bias,
-                           void* y, const sf_conv_desc* d, void* stream);
+                           void* y, const sf_conv_desc* d,
+                           void* workspace, size_t workspace_bytes, void* stream);
 
 /* Reads back (synchronously on `stream`) the device error word shared by
  * sf_sparse_conv2d and sf_fused_conv_lif: SF_OK or SF_ERR_DEVICE_TIMEOUT.
@@ -157,11 +163,15 @@ typedef struct sf_lif_desc {
   int32_t has_bias;
 } sf_lif_desc;
 
+/* Workspace bytes of sf_fused_conv_lif (masks of all t_steps * n images). */
+size_t sf_fused_conv_lif_workspace_size(const sf_lif_desc* d);
+
 /* v_inout: fp32 [n, c_out, h_out, w_out], read as v[0] and overwritten with
- * the membrane state after the last step. */
+ * the membrane state after the last step. Supports 3x3/s1/p1 and 1x1/s1/p0. */
 sf_status sf_fused_conv_lif(const void* x, const void* w_packed, const float* bias,
                             float* v_inout, void* spikes_out,
-                            const sf_lif_desc* d, void* stream);
+                            const sf_lif_desc* d,
+                            void* workspace, size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

@@ -49,20 +49,8 @@ def output_hw(h: int, w: int, k: int, s: int, p: int, d: int = 1):
 
 
 def prepare_input(x: torch.Tensor) -> torch.Tensor:
-    """Contiguous, 16-byte aligned input whose byte size is a multiple of 16.
-
-    The bulk copies in the kernel move each channel's rows as 16-byte aligned
-    ranges, so the last range may extend up to 15 bytes past the last element;
-    inputs that do not meet that are copied (on the GPU) into a padded buffer.
-    """
-    x = x.contiguous()
-    nbytes = x.numel() * x.element_size()
-    if x.data_ptr() % 16 == 0 and nbytes % 16 == 0:
-        return x
-    pad = (-nbytes % 16) // x.element_size()
-    buf = torch.empty(x.numel() + pad, dtype=x.dtype, device=x.device)
-    buf[: x.numel()].copy_(x.reshape(-1))
-    return buf[: x.numel()].view(x.shape)
+    """The kernels read x in its own NCHW layout; only contiguity is required."""
+    return x.contiguous()
 
 
 def pack_weight(weight: torch.Tensor) -> torch.Tensor:

@@ -88,9 +88,12 @@ _SIGNATURES = {
     "sf_packed_weight_bytes": (ctypes.c_size_t, [ctypes.c_int32] * 4),
     "sf_pack_weights": (ctypes.c_int32, [_VP, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                          ctypes.c_int32, _VP, _VP]),
-    "sf_sparse_conv2d": (ctypes.c_int32, [_VP, _VP, _VP, _VP, ctypes.POINTER(ConvDesc), _VP]),
+    "sf_sparse_conv2d_workspace_size": (ctypes.c_size_t, [ctypes.POINTER(ConvDesc)]),
+    "sf_sparse_conv2d": (ctypes.c_int32, [_VP, _VP, _VP, _VP, ctypes.POINTER(ConvDesc), _VP, ctypes.c_size_t, _VP]),
     "sf_sparse_conv2d_status": (ctypes.c_int32, [_VP]),
-    "sf_fused_conv_lif": (ctypes.c_int32, [_VP, _VP, _VP, _VP, _VP, ctypes.POINTER(LifDesc), _VP]),
+    "sf_fused_conv_lif_workspace_size": (ctypes.c_size_t, [ctypes.POINTER(LifDesc)]),
+    "sf_fused_conv_lif": (ctypes.c_int32, [_VP, _VP, _VP, _VP, _VP, ctypes.POINTER(LifDesc), _VP, ctypes.c_size_t,
+                                           _VP]),
 }
 
 _lib = None
@@ -204,6 +207,26 @@ def pack_weights(weight: torch.Tensor, out_dtype: torch.dtype = torch.float32) -
     return out
 
 
+_ws_lock = threading.Lock()
+_workspaces: dict = {}
+
+
+def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """Per-(device, stream) scratch buffer for the conv entry points, grown on demand.
+
+    Calls on one stream run in order, so they can share it; another stream
+    gets its own.
+    """
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    key = (idx, torch.cuda.current_stream(device).cuda_stream)
+    with _ws_lock:
+        buf = _workspaces.get(key)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+            _workspaces[key] = buf
+    return buf
+
+
 def sparse_conv2d(x: torch.Tensor, w_packed: torch.Tensor, bias: Optional[torch.Tensor], y: torch.Tensor,
                   c_out: int, kernel: int, stride: int, padding: int) -> None:
     _require_cuda(x, w_packed, bias, y)
@@ -211,7 +234,11 @@ def sparse_conv2d(x: torch.Tensor, w_packed: torch.Tensor, bias: Optional[torch.
     _, co, ho, wo = y.shape
     desc = ConvDesc(n, c, h, w, co, ho, wo, kernel, stride, padding, sf_dtype(x.dtype), sf_dtype(w_packed.dtype),
                     int(bias is not None))
-    st = load().sf_sparse_conv2d(_ptr(x), _ptr(w_packed), _ptr(bias), _ptr(y), ctypes.byref(desc), _stream(x.device))
+    lib = load()
+    nbytes = lib.sf_sparse_conv2d_workspace_size(ctypes.byref(desc))
+    ws = workspace(x.device, nbytes)
+    st = lib.sf_sparse_conv2d(_ptr(x), _ptr(w_packed), _ptr(bias), _ptr(y), ctypes.byref(desc), _ptr(ws),
+                              ws.numel(), _stream(x.device))
     _check("sf_sparse_conv2d", st)
 
 
@@ -224,6 +251,9 @@ def fused_conv_lif(x5: torch.Tensor, w_packed: torch.Tensor, bias: Optional[torc
     desc = LifDesc(t, n, c, h, w, co, ho, wo, kernel, stride, padding, float(tau), float(v_threshold),
                    0.0 if v_reset is None else float(v_reset), int(v_reset is not None), int(bool(decay_input)),
                    sf_dtype(x5.dtype), sf_dtype(w_packed.dtype), int(bias is not None))
-    st = load().sf_fused_conv_lif(_ptr(x5), _ptr(w_packed), _ptr(bias), _ptr(v), _ptr(spikes), ctypes.byref(desc),
-                                  _stream(x5.device))
+    lib = load()
+    nbytes = lib.sf_fused_conv_lif_workspace_size(ctypes.byref(desc))
+    ws = workspace(x5.device, nbytes)
+    st = lib.sf_fused_conv_lif(_ptr(x5), _ptr(w_packed), _ptr(bias), _ptr(v), _ptr(spikes), ctypes.byref(desc),
+                               _ptr(ws), ws.numel(), _stream(x5.device))
     _check("sf_fused_conv_lif", st)

@@ -1,34 +1,35 @@
-// Stage 2: gather-style sparse convolution, and the same kernel with a fused
-// (BN-folded) bias + LIF epilogue run over all T steps.
+// Stage 2: gather-style sparse convolution from spike-event masks, and the
+// same kernel with a fused (BN-folded) bias + LIF epilogue over all T steps.
 //
 // Reference semantics: Kernels/conv2d.py:563-886 (3x3 s1/s2) and :236-460
 // (1x1) compute y = conv2d(x, w) + bias over active (tile, channel-group)
 // blocks; Ops/sparse_conv2d.py:819-834 (F.conv2d) is the exact result they
 // approximate. Ops/sparse_fused_conv_lif.py:271-293 defines the LIF update.
 //
-// B200 design: one persistent CTA per SM, warp-specialised.
+// Input: the per-pixel nonzero-channel masks written by events.cu (64-bit
+// words, [image][h][w][nw]) and, only for images flagged as holding values
+// other than 0/1, x itself.
+//
+// B200 design: one persistent CTA per SM, warp-specialised, no CTA-wide
+// barrier after set-up.
 //   * Warp 31 is the producer. A work unit is (image, band of TH output rows,
-//     block of up to 128 output channels); a chunk is cc <= 64 input channels
-//     of the band's input rows (band + halo). The producer fills a ring of
-//     shared-memory stages with ONE 4-D tensor TMA copy per chunk (box
-//     W x rows x channels; halo rows outside the image arrive as zeros), or
-//     with one bulk copy per channel when the row pitch is not 16-byte
-//     aligned. Stages hand over through full/empty mbarriers, so loads run
-//     ahead of compute and no CTA-wide barrier is needed.
+//     column block, block of 32*CPL output channels). For each unit (and time
+//     step) it copies the band's mask rows (band + halo; a few KB, contiguous
+//     in memory) into a ring of shared-memory stages with one bulk copy (TMA
+//     engine), handing stages over through full/empty mbarriers. When the
+//     output-channel block changes it also bulk-copies that block's packed
+//     weights into shared memory, after the consumers have drained the ring.
 //   * Warps 0..30 compute, each owning a segment of R output pixels of one
-//     row; lanes own CPL consecutive output channels. Per chunk a warp builds,
-//     in registers, the 64-bit nonzero-channel masks of the K x ((R-1)S+K)
-//     input pixels it reads (element-level sparsity: exact zeros are skipped,
-//     so results are exact), and learns whether every nonzero is 1.0 (binary
-//     spikes: then x is never read again). Each set bit (ascending channel) is
-//     an input event that feeds up to K taps of the segment, with one vector
-//     weight load per tap into register accumulators; tap/pixel pairing is
-//     resolved at compile time. No atomics, fixed order: bit-identical runs.
-//   * Weights sit in shared memory for the whole kernel when they fit (one
-//     bulk copy per CTA); otherwise they are read through L1/L2.
+//     row; lane l owns output channels (slice j) * 32 + l, j < CPL. A warp
+//     reads the K x ((R-1)S+K) masks its segment needs (lane = pixel),
+//     ballots which are nonzero, and walks their set bits (ascending channel):
+//     each is an input event feeding up to K taps of the segment, one weight
+//     load per tap and slice into register accumulators (tap/pixel pairing is
+//     resolved at compile time). Binary spikes add weights; other values are
+//     read from x and multiplied. No atomics, fixed order: bit-identical runs.
 //   * Epilogue: bias (or the LIF update with v held in registers across all T
-//     steps); lane pairs exchange halves by shuffle so every 16-byte store of
-//     the warp completes a 32-byte sector of an NCHW row.
+//     steps); lane pairs exchange half rows by shuffle so every 16-byte store
+//     of a warp completes 32-byte sectors of NCHW rows.
 #pragma once
 #include <algorithm>
 #include <cstdlib>
@@ -42,17 +43,12 @@ constexpr int kNWarps = 32;
 constexpr int kThreads = kNWarps * 32;
 constexpr int kComputeWarps = kNWarps - 1;
 constexpr int kProducerWarp = kNWarps - 1;
-constexpr int kCC = 64;  // max channels per chunk (one mask bit each); p.cc <= kCC is used
-constexpr int kMaxStages = 4;
+constexpr int kMaxStages = 8;
 constexpr int kSmemLimit = 227 * 1024;
 
-// Output-channel block of one unit (32 lanes x CPL) and the padded C_out of
-// the packed weights.
-inline int co_block(int co) { return co <= 32 ? 32 : (co <= 64 ? 64 : 128); }
-inline int co_padded(int co) {
-  const int b = co_block(co);
-  return ((co + b - 1) / b) * b;
-}
+// Packed weights: [slice][C_in][k*k][32], slices of 32 output channels,
+// padded to a multiple of four slices (128 channels) with zeros.
+inline int co_slices_padded(int co) { return ((co + 127) / 128) * 4; }
 
 // Optional phase timing (builds with -DSF_CONV_PHASE_PROFILE only): thread 0
 // accumulates cycles per phase in registers and adds them to g_conv_phase.
@@ -77,85 +73,35 @@ struct ConvParams {
   void* y;   // conv output or spikes
   float* v;  // LIF membrane state [N, Co, Ho, Wo]
   uint32_t* err;
+  const unsigned long long* masks;  // [T*N][H][W][nw]
+  const uint32_t* flags;            // [T*N]: bit 0 set when values other than 0/1 occur
+  int nw;
   float tau, vth, vreset;
   int hard_reset, decay_input;
   int T, N, C, H, W, Co, Ho, Wo, P;
-  int Co_pad;
-  int TH, nbands, ncob, n_units, tpr;  // tpr: row segments per output row (whole image)
-  int tpu, ncolb;                     // row segments per unit, column blocks per band
+  int TH, nbands, ncolb, ncob, n_units, tpr, tpu;  // tpr: row segments per output row; tpu: per unit
+  int units_per_cta;
   int th_in;
-  int slot_elems;
-  int cc;  // channels per chunk
-  int nchunks;
+  int slot_words;  // 64-bit words per mask stage
   int nstage;
-  int use_tmap;        // 1: one 4-D tensor copy per chunk; 0: one bulk copy per channel
-  uint32_t box_bytes;  // bytes of one tensor copy
-  uint32_t w_bytes;    // packed weight bytes staged in shared memory (WSMEM kernels)
-  int w_off, cb_off, bar_off;  // byte offsets in dynamic smem
+  uint32_t w_cob_bytes;  // bytes of one output-channel block of packed weights (WSMEM kernels)
+  int w_off, bar_off;    // byte offsets in dynamic smem
 };
 
 struct Plan {
-  int CPL, R, TH, th_in, nstage, slot_elems, cc, use_tmap, wsmem;
-  int w_off, cb_off, bar_off, smem;
+  int CPL, R, TH, th_in, nstage, slot_words, wsmem;
+  int w_off, bar_off, smem;
 };
 
-// Per-stage table in shared memory: kCC channel base offsets, then a uniform
-// flag and the uniform base (element index of channel 0, halo row 0).
-constexpr int kCbStride = kCC + 2;
-
-template <typename WT, int CPL, bool SMEM>
-struct WVec;
-template <bool SMEM>
-struct WVec<float, 1, SMEM> {
-  static __device__ __forceinline__ void ld(const float* p, float (&w)[1]) { w[0] = SMEM ? *p : __ldg(p); }
-};
-template <bool SMEM>
-struct WVec<float, 2, SMEM> {
-  static __device__ __forceinline__ void ld(const float* p, float (&w)[2]) {
-    const float2 v = SMEM ? *reinterpret_cast<const float2*>(p) : __ldg(reinterpret_cast<const float2*>(p));
-    w[0] = v.x;
-    w[1] = v.y;
-  }
-};
-template <bool SMEM>
-struct WVec<float, 4, SMEM> {
-  static __device__ __forceinline__ void ld(const float* p, float (&w)[4]) {
-    const float4 v = SMEM ? *reinterpret_cast<const float4*>(p) : __ldg(reinterpret_cast<const float4*>(p));
-    w[0] = v.x;
-    w[1] = v.y;
-    w[2] = v.z;
-    w[3] = v.w;
-  }
-};
-__device__ __forceinline__ float bf16_lo(uint32_t u) { return __uint_as_float(u << 16); }
-__device__ __forceinline__ float bf16_hi(uint32_t u) { return __uint_as_float(u & 0xffff0000u); }
-template <bool SMEM>
-struct WVec<__nv_bfloat16, 1, SMEM> {
-  static __device__ __forceinline__ void ld(const __nv_bfloat16* p, float (&w)[1]) {
+template <typename WT, bool SMEM>
+__device__ __forceinline__ float ldw(const WT* p) {
+  if constexpr (sizeof(WT) == 4) {
+    return SMEM ? *reinterpret_cast<const float*>(p) : __ldg(reinterpret_cast<const float*>(p));
+  } else {
     const unsigned short* q = reinterpret_cast<const unsigned short*>(p);
-    w[0] = __uint_as_float((uint32_t)(SMEM ? *q : __ldg(q)) << 16);
+    return __uint_as_float((uint32_t)(SMEM ? *q : __ldg(q)) << 16);
   }
-};
-template <bool SMEM>
-struct WVec<__nv_bfloat16, 2, SMEM> {
-  static __device__ __forceinline__ void ld(const __nv_bfloat16* p, float (&w)[2]) {
-    const unsigned int* q = reinterpret_cast<const unsigned int*>(p);
-    const uint32_t u = SMEM ? *q : __ldg(q);
-    w[0] = bf16_lo(u);
-    w[1] = bf16_hi(u);
-  }
-};
-template <bool SMEM>
-struct WVec<__nv_bfloat16, 4, SMEM> {
-  static __device__ __forceinline__ void ld(const __nv_bfloat16* p, float (&w)[4]) {
-    const uint2* q = reinterpret_cast<const uint2*>(p);
-    const uint2 u = SMEM ? *q : __ldg(q);
-    w[0] = bf16_lo(u.x);
-    w[1] = bf16_hi(u.x);
-    w[2] = bf16_lo(u.y);
-    w[3] = bf16_hi(u.y);
-  }
-};
+}
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
@@ -209,72 +155,55 @@ __device__ __forceinline__ void load_run(const float* src, float (&v)[R], int nv
   for (int j = 0; j < R; ++j) v[j] = (j < nvalid) ? src[j] : 0.f;
 }
 
-// Writes a warp's tile (lane owns channels lane*CPL + j, R pixels each) to
-// rows base + co * co_stride. For fp32 with R = 8 and CPL <= 2, aligned full
-// segments go out as lane-pair sector stores: lanes 2m and 2m+1 exchange half
-// rows so that each 16-byte store instruction completes 16 32-byte sectors.
-template <typename T, int CPL, int R>
-__device__ __forceinline__ void store_tile(T* base, size_t co_stride, int co_lim, int lane, int nvalid,
-                                           const float (&v)[CPL][R]) {
-  if constexpr (sizeof(T) == 4 && R == 8 && CPL <= 2) {
-    const bool pairable = nvalid == R && (reinterpret_cast<uintptr_t>(base) & 15u) == 0 && (co_stride & 3u) == 0;
-    if (pairable) {
+// Writes one slice of a warp's tile: lane l holds R pixels of channel
+// co0 + l at base + l * co_stride. For fp32 with R = 8, aligned full rows go
+// out as lane-pair stores: lanes 2m and 2m+1 swap half rows so each 16-byte
+// store instruction completes sixteen 32-byte sectors.
+template <typename T, int R>
+__device__ __forceinline__ void store_slice(T* base, size_t co_stride, int co_lim, int lane, int nvalid,
+                                            const float (&v)[R]) {
+  if constexpr (sizeof(T) == 4 && R == 8) {
+    if (nvalid == R && (reinterpret_cast<uintptr_t>(base) & 15u) == 0 && (co_stride & 3u) == 0) {
       const int h = lane & 1;
-      // Send the half the partner stores: the even lane sends pixels 4..7,
-      // the odd lane pixels 0..3.
-      float recv[CPL][4];
+      float recv[4];
 #pragma unroll
-      for (int j = 0; j < CPL; ++j)
+      for (int i = 0; i < 4; ++i) recv[i] = __shfl_xor_sync(0xffffffffu, h ? v[i] : v[4 + i], 1);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) recv[j][i] = __shfl_xor_sync(0xffffffffu, h ? v[j][i] : v[j][4 + i], 1);
-      // Pair m owns channels 2*CPL*m .. 2*CPL*m + 2*CPL - 1 (even lane's CPL
-      // first); store q writes channel 2*CPL*m + q, even lane pixels 0..3,
-      // odd lane pixels 4..7.
-#pragma unroll
-      for (int q = 0; q < 2 * CPL; ++q) {
-        const int co = (lane >> 1) * 2 * CPL + q;
-        const bool own = (q < CPL) ? (h == 0) : (h == 1);
-        const int j = q % CPL;
+      for (int q = 0; q < 2; ++q) {
+        const int co = (lane & ~1) + q;  // store q writes channel 2m + q: even lane pixels 0..3, odd 4..7
         float4 out;
-        if (own)
-          out = h ? make_float4(v[j][4], v[j][5], v[j][6], v[j][7]) : make_float4(v[j][0], v[j][1], v[j][2], v[j][3]);
+        if (q == h)
+          out = h ? make_float4(v[4], v[5], v[6], v[7]) : make_float4(v[0], v[1], v[2], v[3]);
         else
-          out = make_float4(recv[j][0], recv[j][1], recv[j][2], recv[j][3]);
+          out = make_float4(recv[0], recv[1], recv[2], recv[3]);
         if (co < co_lim) *reinterpret_cast<float4*>(reinterpret_cast<float*>(base) + co * co_stride + h * 4) = out;
       }
       return;
     }
   }
-#pragma unroll
-  for (int j = 0; j < CPL; ++j) {
-    const int co = lane * CPL + j;
-    if (co < co_lim) store_run<T, R>(base + co * co_stride, v[j], nvalid);
-  }
+  if (lane < co_lim) store_run<T, R>(base + lane * co_stride, v, nvalid);
 }
 
 template <int K, int S, int CPL, int R, typename XT, typename WT, bool LIF, bool WSMEM>
-__global__ void __launch_bounds__(kThreads, 1)
-    sparse_conv_kernel(const ConvParams p, const __grid_constant__ CUtensorMap tmap) {
+__global__ void __launch_bounds__(kThreads, 1) sparse_conv_kernel(const ConvParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
   constexpr int KK = K * K;
-  constexpr int COB = 32 * CPL;
-  constexpr int ESZ = (int)sizeof(XT);
   constexpr int QN = (R - 1) * S + K;  // input columns a row segment reads
   constexpr int NPOS = K * QN;         // input pixels a row segment reads
   constexpr int ROUNDS = (NPOS + 31) / 32;
 
-  XT* stages = reinterpret_cast<XT*>(smem);
+  unsigned long long* stages = reinterpret_cast<unsigned long long*>(smem);
   const WT* wsm = reinterpret_cast<const WT*>(smem + p.w_off);
-  int* cbtab = reinterpret_cast<int*>(smem + p.cb_off);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.bar_off);
   uint64_t* empty = full + kMaxStages;
   uint64_t* wbar = empty + kMaxStages;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const XT* __restrict__ x = static_cast<const XT*>(p.x);
   const int T = LIF ? p.T : 1;
-  const int chunks_per_unit = T * p.nchunks;
-  const int stage_elems = p.cc * p.slot_elems;
+  const int u_begin = blockIdx.x * p.units_per_cta;
+  const int u_end = min(p.n_units, u_begin + p.units_per_cta);
+  const int upc = p.n_units / p.ncob;  // units per output-channel block
+  const size_t wslice = (size_t)p.C * KK * 32;  // elements of one 32-channel weight slice
 
   if (tid == 0) {
     for (int s = 0; s < p.nstage; ++s) {
@@ -287,77 +216,45 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();  // the only CTA-wide barrier
 
   if (warp == kProducerWarp) {
-    if (WSMEM && lane == 0) {
-      mbar_arrive_expect_tx(wbar, p.w_bytes);
-      bulk_g2s(smem + p.w_off, p.wp, p.w_bytes, wbar);
-    }
-    for (int g = 0;; ++g) {
-      const int ul = g / chunks_per_unit;
-      const int u = blockIdx.x + ul * gridDim.x;
-      if (u >= p.n_units) break;
-      const int s = g % p.nstage;
-      if (g >= p.nstage) {
-        if (!mbar_wait_bounded(&empty[s], (uint32_t)(((g / p.nstage) - 1) & 1))) {
-          if (lane == 0) atomicExch(p.err, 1u);
-          return;
+    if (lane == 0) {
+      int g = 0, cur_cob = -1;
+      for (int u = u_begin; u < u_end; ++u) {
+        const int cob = u / upc;
+        const int rest = u - cob * upc;
+        const int n = rest / (p.nbands * p.ncolb);
+        const int band = (rest - n * p.nbands * p.ncolb) / p.ncolb;
+        if (WSMEM && cob != cur_cob) {
+          // Drain: every stage handed out so far must be released before the
+          // weights in shared memory change.
+          for (int q = max(0, g - p.nstage); q < g; ++q) {
+            if (!mbar_wait_bounded(&empty[q % p.nstage], (uint32_t)((q / p.nstage) & 1))) {
+              atomicExch(p.err, 1u);
+              return;
+            }
+          }
+          mbar_arrive_expect_tx(wbar, p.w_cob_bytes);
+          bulk_g2s(smem + p.w_off, static_cast<const WT*>(p.wp) + (size_t)cob * CPL * wslice, p.w_cob_bytes, wbar);
+          cur_cob = cob;
         }
-      }
-      const int rem = g - ul * chunks_per_unit;
-      const int t = rem / p.nchunks;
-      const int k = rem - t * p.nchunks;
-      const int nb = u / p.ncob / p.ncolb;
-      const int band = nb % p.nbands;
-      const int n = nb / p.nbands;
-      const int ihs = band * p.TH * S - p.P;
-      const int ih_lo = max(0, ihs);
-      const int ih_hi = min(p.H, ihs + p.th_in);
-      const int c0 = k * p.cc;
-      const int cc = min(p.cc, p.C - c0);
-      const int img = LIF ? t * p.N + n : n;
-      int* cbs = cbtab + s * kCbStride;
-      if (p.use_tmap) {
-        // Box (W, th_in rows from ihs, cc channels, 1 image); rows outside the
-        // image and channels past C arrive as zeros.
-        if (lane == 0) {
-          cbs[kCC] = 1;
-          cbs[kCC + 1] = 0;
-          mbar_arrive_expect_tx(&full[s], p.box_bytes);
-          tma_load_4d(stages + (size_t)s * stage_elems, &tmap, 0, ihs, c0, img, &full[s]);
+        const int ihs = band * p.TH * S - p.P;
+        const int ih_lo = max(0, ihs);
+        const int ih_hi = min(p.H, ihs + p.th_in);
+        for (int t = 0; t < T; ++t, ++g) {
+          const int s = g % p.nstage;
+          if (g >= p.nstage) {
+            if (!mbar_wait_bounded(&empty[s], (uint32_t)(((g / p.nstage) - 1) & 1))) {
+              atomicExch(p.err, 1u);
+              return;
+            }
+          }
+          const size_t img = (size_t)(LIF ? t * p.N + n : n);
+          const size_t w0 = ((img * p.H + ih_lo) * p.W) * p.nw;
+          const size_t w1 = w0 + (size_t)(ih_hi - ih_lo) * p.W * p.nw;
+          const size_t a0 = (w0 * 8) & ~(size_t)15, a1 = (w1 * 8 + 15) & ~(size_t)15;
+          mbar_arrive_expect_tx(&full[s], (uint32_t)(a1 - a0));
+          bulk_g2s(stages + (size_t)s * p.slot_words, reinterpret_cast<const char*>(p.masks) + a0, (uint32_t)(a1 - a0),
+                   &full[s]);
         }
-        continue;
-      }
-      size_t a0[2] = {0, 0};
-      uint32_t bytes[2] = {0, 0};
-      int e0[2] = {-1, -1};
-      const int row_shift = (ih_lo - ihs) * p.W;  // halo row 0 sits row_shift elements before the copied rows
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const int ci = lane + 32 * hh;
-        if (ci < cc) {
-          const size_t start = (((size_t)img * p.C + c0 + ci) * p.H + ih_lo) * (size_t)p.W * ESZ;
-          const size_t end = start + (size_t)(ih_hi - ih_lo) * p.W * ESZ;
-          a0[hh] = start & ~(size_t)15;
-          bytes[hh] = (uint32_t)(((end + 15) & ~(size_t)15) - a0[hh]);
-          e0[hh] = (int)((start - a0[hh]) / ESZ);
-          cbs[ci] = ci * p.slot_elems + e0[hh] - row_shift;
-        }
-      }
-      const uint32_t total = __reduce_add_sync(0xffffffffu, bytes[0] + bytes[1]);
-      const int e0_first = __shfl_sync(0xffffffffu, e0[0], 0);
-      const bool uniform =
-          __all_sync(0xffffffffu, (e0[0] < 0 || e0[0] == e0_first) && (e0[1] < 0 || e0[1] == e0_first));
-      if (lane == 0) {
-        cbs[kCC] = uniform ? 1 : 0;
-        cbs[kCC + 1] = e0_first - row_shift;
-        mbar_arrive_expect_tx(&full[s], total);
-      }
-      __syncwarp();
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const int ci = lane + 32 * hh;
-        if (ci < cc)
-          bulk_g2s(stages + (size_t)s * stage_elems + (size_t)ci * p.slot_elems,
-                   reinterpret_cast<const char*>(x) + a0[hh], bytes[hh], &full[s]);
       }
     }
     return;
@@ -368,32 +265,32 @@ __global__ void __launch_bounds__(kThreads, 1)
   long long ph_t0 = clock64();
   long long ph_acc[5] = {0, 0, 0, 0, 0};
 #endif
-  if (WSMEM) {
-    if (!mbar_wait_bounded(wbar, 0)) {
-      if (lane == 0) atomicExch(p.err, 1u);
-      return;
-    }
-  }
+  const XT* __restrict__ x = static_cast<const XT*>(p.x);
   const WT* __restrict__ wglob = static_cast<const WT*>(p.wp);
-
   float acc[R][CPL];
   float vreg[LIF ? CPL : 1][LIF ? R : 1];
-  int g = 0;
+  int g = 0, cur_cob = -1, wloads = 0;
 
-  for (int ul = 0;; ++ul) {
-    const int u = blockIdx.x + ul * gridDim.x;
-    if (u >= p.n_units) break;
-    const int cob = u % p.ncob;
-    const int colb = (u / p.ncob) % p.ncolb;
-    const int nb = u / p.ncob / p.ncolb;
-    const int band = nb % p.nbands;
-    const int n = nb / p.nbands;
+  for (int u = u_begin; u < u_end; ++u) {
+    const int cob = u / upc;
+    const int rest = u - cob * upc;
+    const int n = rest / (p.nbands * p.ncolb);
+    const int rb = rest - n * p.nbands * p.ncolb;
+    const int band = rb / p.ncolb;
+    const int colb = rb - band * p.ncolb;
+    if (WSMEM && cob != cur_cob) {
+      if (!mbar_wait_bounded(wbar, (uint32_t)(wloads & 1))) {
+        if (lane == 0) atomicExch(p.err, 1u);
+        return;
+      }
+      ++wloads;
+      cur_cob = cob;
+    }
     const int r0 = band * p.TH;
     const int rows_out = min(p.TH, p.Ho - r0);
     const int ihs = r0 * S - p.P;
     const int ih_lo = max(0, ihs);
     const int ih_hi = min(p.H, ihs + p.th_in);
-    const int co_base = cob * COB;
     const size_t hw_out = (size_t)p.Ho * p.Wo;
 
     // This warp's row segment.
@@ -403,160 +300,118 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool active = tr < rows_out && segi < p.tpr;
     const int nvalid = min(R, p.Wo - seg0);
     const int orow = r0 + tr;
-    const int hl0 = tr * S;
-    const int col0 = seg0 * S - p.P;  // input column of position qq = 0
+    const int ih0 = ihs + tr * S;     // input row of tap row 0
+    const int col0 = seg0 * S - p.P;  // input column of position 0
+    const WT* wbase = (WSMEM ? wsm : wglob + (size_t)cob * CPL * wslice) + lane;
 
-    if (LIF && active) {
+    if constexpr (LIF) {
+      if (active) {
 #pragma unroll
-      for (int j = 0; j < CPL; ++j) {
-        const int co = co_base + lane * CPL + j;
-        float tmp[R];
-        if (co < p.Co) {
-          load_run<R>(p.v + ((size_t)n * p.Co + co) * hw_out + (size_t)orow * p.Wo + seg0, tmp, nvalid);
-        } else {
+        for (int j = 0; j < CPL; ++j) {
+          const int co = (cob * CPL + j) * 32 + lane;
+          if (co < p.Co) {
+            load_run<R>(p.v + ((size_t)n * p.Co + co) * hw_out + (size_t)orow * p.Wo + seg0, vreg[j], nvalid);
+          } else {
 #pragma unroll
-          for (int i = 0; i < R; ++i) tmp[i] = 0.f;
+            for (int i = 0; i < R; ++i) vreg[j][i] = 0.f;
+          }
         }
-#pragma unroll
-        for (int i = 0; i < R; ++i) vreg[j][i] = tmp[i];
       }
     }
 
-    for (int t = 0; t < T; ++t) {
+    for (int t = 0; t < T; ++t, ++g) {
+      const int s = g % p.nstage;
+      const size_t img = (size_t)(LIF ? t * p.N + n : n);
+      SF_PHASE(4);
+      if (!mbar_wait_bounded(&full[s], (uint32_t)((g / p.nstage) & 1))) {
+        if (lane == 0) atomicExch(p.err, 1u);
+        return;
+      }
+      SF_PHASE(0);
+      const unsigned long long* st = stages + (size_t)s * p.slot_words;
+      const int e0 = (int)((((img * p.H + ih_lo) * p.W) * p.nw) & 1);  // word offset of the aligned copy
+      const bool binary = (__ldg(p.flags + img) & 1u) == 0u;
+
 #pragma unroll
       for (int i = 0; i < R; ++i)
 #pragma unroll
         for (int j = 0; j < CPL; ++j) acc[i][j] = 0.f;
 
-      for (int k = 0; k < p.nchunks; ++k, ++g) {
-        const int s = g % p.nstage;
-        SF_PHASE(4);
-        if (!mbar_wait_bounded(&full[s], (uint32_t)((g / p.nstage) & 1))) {
-          if (lane == 0) atomicExch(p.err, 1u);
-          return;
-        }
-        SF_PHASE(0);
-        const XT* st = stages + (size_t)s * stage_elems;
-        const int* cb = cbtab + s * kCbStride;
-        const bool uni = cb[kCC] != 0;
-        const int u0 = cb[kCC + 1];
-        const int c0 = k * p.cc;
-        const int cc = min(p.cc, p.C - c0);
-
-        // Nonzero-channel masks of this segment's input pixels (lane = pixel),
-        // built 32 channels at a time with constant shifts; `bad` records a
-        // nonzero that is not exactly 1.
+      for (int wd = 0; wd < p.nw; ++wd) {
+        // Masks of this segment's input pixels (lane = pixel) and which are nonzero.
         unsigned long long mk[ROUNDS];
-        uint32_t bad = 0u;
+        uint32_t nzpos[ROUNDS];
 #pragma unroll
         for (int rd = 0; rd < ROUNDS; ++rd) {
           const int pos = rd * 32 + lane;
           const int kh = pos / QN;
           const int qq = pos - kh * QN;
-          const int ih = ihs + hl0 + kh;
+          const int ih = ih0 + kh;
           const int iw = col0 + qq;
-          uint32_t half_m[2] = {0u, 0u};
-          if (active && pos < NPOS && iw >= 0 && iw < p.W && ih >= ih_lo && ih < ih_hi) {
-            const int off = (hl0 + kh) * p.W + iw;
+          unsigned long long m = 0ull;
+          if (active && pos < NPOS && iw >= 0 && iw < p.W && ih >= ih_lo && ih < ih_hi)
+            m = st[e0 + ((ih - ih_lo) * p.W + iw) * p.nw + wd];
+          mk[rd] = m;
+          nzpos[rd] = __ballot_sync(0xffffffffu, m != 0ull);
+        }
+        SF_PHASE(1);
+        // Events: each set bit of a nonzero position feeds up to K taps.
+        auto gather = [&](auto binary_tag) {
+          constexpr bool BIN = decltype(binary_tag)::value;
 #pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-              if (hh * 32 < cc) {
-                uint32_t mm = 0u;
-                if (uni) {
-                  const XT* src = st + u0 + off + hh * 32 * p.slot_elems;
+          for (int pos = 0; pos < NPOS; ++pos) {
+            const int kh = pos / QN;
+            const int qq = pos - kh * QN;
+            if (((nzpos[pos / 32] >> (pos % 32)) & 1u) == 0u) continue;
+            unsigned long long m = shfl64(mk[pos / 32], pos % 32);
+            while (m) {
+              const int ci = __ffsll((long long)m) - 1;
+              m &= m - 1ull;
+              const int c = wd * 64 + ci;
+              const WT* wc = wbase + ((size_t)c * KK + kh * K) * 32;
+              float xv = 1.f;
+              if constexpr (!BIN)
+                xv = DT<XT>::to_f(__ldg(x + ((img * p.C + c) * p.H + (ih0 + kh)) * p.W + (col0 + qq)));
 #pragma unroll
-                  for (int q = 0; q < 32; ++q) {
-                    if (hh * 32 + q < cc) {
-                      const XT v = src[q * p.slot_elems];
-                      const uint32_t nzb = DT<XT>::nz_bit(v);
-                      mm |= nzb << q;
-                      bad |= nzb & DT<XT>::not_one(v);
-                    }
-                  }
-                } else {
-#pragma unroll 8
-                  for (int q = 0; q < 32; ++q) {
-                    if (hh * 32 + q < cc) {
-                      const XT v = st[cb[hh * 32 + q] + off];
-                      const uint32_t nzb = DT<XT>::nz_bit(v);
-                      mm |= nzb << q;
-                      bad |= nzb & DT<XT>::not_one(v);
-                    }
+              for (int kw = 0; kw < K; ++kw) {
+                const int d = qq - kw;
+                if (d >= 0 && d % S == 0 && d / S < R) {
+#pragma unroll
+                  for (int j = 0; j < CPL; ++j) {
+                    const float w = ldw<WT, WSMEM>(wc + j * wslice + kw * 32);
+                    if constexpr (BIN)
+                      acc[d / S][j] += w;
+                    else
+                      acc[d / S][j] = fmaf(xv, w, acc[d / S][j]);
                   }
                 }
-                half_m[hh] = mm;
               }
             }
           }
-          mk[rd] = ((unsigned long long)half_m[1] << 32) | half_m[0];
-        }
-        const bool binary = !__any_sync(0xffffffffu, bad != 0u);
-        uint32_t nzpos[ROUNDS];
-#pragma unroll
-        for (int rd = 0; rd < ROUNDS; ++rd) nzpos[rd] = __ballot_sync(0xffffffffu, mk[rd] != 0ull);
-        SF_PHASE(1);
-
-        // Gather over the segment's input events.
+        };
         if (active) {
-          const WT* wchunk = (WSMEM ? wsm : wglob) + (size_t)c0 * KK * p.Co_pad + co_base + lane * CPL;
-          const int xrow0 = u0 + hl0 * p.W + col0;
-          auto gather = [&](auto binary_tag) {
-            constexpr bool BIN = decltype(binary_tag)::value;
-#pragma unroll
-            for (int pos = 0; pos < NPOS; ++pos) {
-              const int kh = pos / QN;
-              const int qq = pos - kh * QN;
-              if (((nzpos[pos / 32] >> (pos % 32)) & 1u) == 0u) continue;
-              unsigned long long m = shfl64(mk[pos / 32], pos % 32);
-              while (m) {
-                const int ci = __ffsll((long long)m) - 1;
-                m &= m - 1ull;
-                const WT* wc = wchunk + ((size_t)ci * KK + kh * K) * p.Co_pad;
-                float xv = 1.f;
-                if constexpr (!BIN) {
-                  const int bse = uni ? ci * p.slot_elems + xrow0 : cb[ci] + hl0 * p.W + col0;
-                  xv = DT<XT>::to_f(st[bse + kh * p.W + qq]);
-                }
-#pragma unroll
-                for (int kw = 0; kw < K; ++kw) {
-                  const int d = qq - kw;
-                  if (d >= 0 && d % S == 0 && d / S < R) {
-                    float w[CPL];
-                    WVec<WT, CPL, WSMEM>::ld(wc + kw * p.Co_pad, w);
-#pragma unroll
-                    for (int j = 0; j < CPL; ++j) {
-                      if constexpr (BIN)
-                        acc[d / S][j] += w[j];
-                      else
-                        acc[d / S][j] = fmaf(xv, w[j], acc[d / S][j]);
-                    }
-                  }
-                }
-              }
-            }
-          };
           if (binary)
             gather(std::true_type{});
           else
             gather(std::false_type{});
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
-        SF_PHASE(2);
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      SF_PHASE(2);
 
       // Epilogue for (unit, t).
       if (active) {
-        const size_t img = (size_t)(LIF ? t * p.N + n : n);
-        float out[CPL][R];
 #pragma unroll
         for (int j = 0; j < CPL; ++j) {
-          const int co = co_base + lane * CPL + j;
+          const int co0 = (cob * CPL + j) * 32;
+          const int co = co0 + lane;
           const float b = (p.bias != nullptr && co < p.Co) ? __ldg(p.bias + co) : 0.f;
+          float out[R];
 #pragma unroll
           for (int i = 0; i < R; ++i) {
             float val = acc[i][j] + b;
-            if (LIF) {
+            if constexpr (LIF) {
               const float vp = vreg[j][i];
               const float vr = p.hard_reset ? p.vreset : 0.f;
               float vt;
@@ -568,19 +423,23 @@ __global__ void __launch_bounds__(kThreads, 1)
               vreg[j][i] = p.hard_reset ? (spk ? p.vreset : vt) : (vt - (spk ? p.vth : 0.f));
               val = spk ? 1.f : 0.f;
             }
-            out[j][i] = val;
+            out[i] = val;
           }
+          XT* ybase = static_cast<XT*>(p.y) + (img * p.Co + co0) * hw_out + (size_t)orow * p.Wo + seg0;
+          store_slice<XT, R>(ybase, hw_out, p.Co - co0, lane, nvalid, out);
         }
-        XT* ybase = static_cast<XT*>(p.y) + (img * p.Co + co_base) * hw_out + (size_t)orow * p.Wo + seg0;
-        store_tile<XT, CPL, R>(ybase, hw_out, p.Co - co_base, lane, nvalid, out);
       }
       SF_PHASE(3);
     }
 
     if constexpr (LIF) {
       if (active) {
-        float* vbase = p.v + ((size_t)n * p.Co + co_base) * hw_out + (size_t)orow * p.Wo + seg0;
-        store_tile<float, CPL, R>(vbase, hw_out, p.Co - co_base, lane, nvalid, vreg);
+#pragma unroll
+        for (int j = 0; j < CPL; ++j) {
+          const int co0 = (cob * CPL + j) * 32;
+          float* vb = p.v + ((size_t)n * p.Co + co0) * hw_out + (size_t)orow * p.Wo + seg0;
+          store_slice<float, R>(vb, hw_out, p.Co - co0, lane, nvalid, vreg[j]);
+        }
       }
     }
   }
@@ -591,57 +450,56 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 template <int K, int S, int CPL, int R, typename XT, typename WT, bool LIF, bool WSMEM>
-sf_status launch_conv(const ConvParams& p, const CUtensorMap& tmap, int smem, cudaStream_t st) {
+sf_status launch_conv(const ConvParams& p, int grid, int smem, cudaStream_t st) {
   auto kern = sparse_conv_kernel<K, S, CPL, R, XT, WT, LIF, WSMEM>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return SF_ERR_CUDA;
-  const int grid = std::max(1, std::min(p.n_units, num_sms_current_device()));
-  kern<<<grid, kThreads, smem, st>>>(p, tmap);
+  kern<<<grid, kThreads, smem, st>>>(p);
   return cudaGetLastError() == cudaSuccess ? SF_OK : SF_ERR_CUDA;
 }
 
 template <int K, int S, typename XT, typename WT, bool LIF, bool WSMEM>
-sf_status dispatch_cpl(const ConvParams& p, const CUtensorMap& tm, const Plan& pl, cudaStream_t st) {
-  if (pl.CPL == 1) return launch_conv<K, S, 1, 8, XT, WT, LIF, WSMEM>(p, tm, pl.smem, st);
-  if (pl.CPL == 2) return launch_conv<K, S, 2, 8, XT, WT, LIF, WSMEM>(p, tm, pl.smem, st);
-  return launch_conv<K, S, 4, 4, XT, WT, LIF, WSMEM>(p, tm, pl.smem, st);
+sf_status dispatch_cpl(const ConvParams& p, int grid, const Plan& pl, cudaStream_t st) {
+  if (pl.CPL == 1) return launch_conv<K, S, 1, 8, XT, WT, LIF, WSMEM>(p, grid, pl.smem, st);
+  if (pl.CPL == 2) return launch_conv<K, S, 2, 8, XT, WT, LIF, WSMEM>(p, grid, pl.smem, st);
+  return launch_conv<K, S, 4, 4, XT, WT, LIF, WSMEM>(p, grid, pl.smem, st);
 }
 
 template <typename XT, typename WT, bool LIF, bool WSMEM>
-sf_status dispatch_geom(int K, int S, const ConvParams& p, const CUtensorMap& tm, const Plan& pl, cudaStream_t st) {
-  if (K == 3 && S == 1) return dispatch_cpl<3, 1, XT, WT, LIF, WSMEM>(p, tm, pl, st);
+sf_status dispatch_geom(int K, int S, const ConvParams& p, int grid, const Plan& pl, cudaStream_t st) {
+  if (K == 3 && S == 1) return dispatch_cpl<3, 1, XT, WT, LIF, WSMEM>(p, grid, pl, st);
   if constexpr (!LIF) {
-    if (K == 3 && S == 2) return dispatch_cpl<3, 2, XT, WT, LIF, WSMEM>(p, tm, pl, st);
+    if (K == 3 && S == 2) return dispatch_cpl<3, 2, XT, WT, LIF, WSMEM>(p, grid, pl, st);
   }
-  if (K == 1 && S == 1) return dispatch_cpl<1, 1, XT, WT, LIF, WSMEM>(p, tm, pl, st);
+  if (K == 1 && S == 1) return dispatch_cpl<1, 1, XT, WT, LIF, WSMEM>(p, grid, pl, st);
   return SF_ERR_UNSUPPORTED;
 }
 
 // Per input dtype: launches the kernel instantiation matching (LIF, weight
-// dtype, weights in shared memory, kernel/stride, channels per lane). Defined
+// dtype, weights in shared memory, kernel/stride, slices per lane). Defined
 // in conv_<dtype>.cu.
-sf_status dispatch_f32(bool lif, int wdt, int K, int S, const ConvParams& p, const CUtensorMap& tm, const Plan& pl,
+sf_status dispatch_f32(bool lif, int wdt, int K, int S, const ConvParams& p, int grid, const Plan& pl,
                        cudaStream_t st);
-sf_status dispatch_f16(bool lif, int wdt, int K, int S, const ConvParams& p, const CUtensorMap& tm, const Plan& pl,
+sf_status dispatch_f16(bool lif, int wdt, int K, int S, const ConvParams& p, int grid, const Plan& pl,
                        cudaStream_t st);
-sf_status dispatch_bf16(bool lif, int wdt, int K, int S, const ConvParams& p, const CUtensorMap& tm, const Plan& pl,
+sf_status dispatch_bf16(bool lif, int wdt, int K, int S, const ConvParams& p, int grid, const Plan& pl,
                         cudaStream_t st);
 
 template <typename XT, typename WT, bool LIF>
-sf_status dispatch_ws(int K, int S, const ConvParams& p, const CUtensorMap& tm, const Plan& pl, cudaStream_t st) {
-  if (pl.wsmem) return dispatch_geom<XT, WT, LIF, true>(K, S, p, tm, pl, st);
-  return dispatch_geom<XT, WT, LIF, false>(K, S, p, tm, pl, st);
+sf_status dispatch_ws(int K, int S, const ConvParams& p, int grid, const Plan& pl, cudaStream_t st) {
+  if (pl.wsmem) return dispatch_geom<XT, WT, LIF, true>(K, S, p, grid, pl, st);
+  return dispatch_geom<XT, WT, LIF, false>(K, S, p, grid, pl, st);
 }
 
 template <typename XT>
-sf_status dispatch_x(bool lif, int wdt, int K, int S, const ConvParams& p, const CUtensorMap& tm, const Plan& pl,
+sf_status dispatch_x(bool lif, int wdt, int K, int S, const ConvParams& p, int grid, const Plan& pl,
                      cudaStream_t st) {
   if (lif) {
-    if (wdt == SF_DTYPE_F32) return dispatch_ws<XT, float, true>(K, S, p, tm, pl, st);
-    if (wdt == SF_DTYPE_BF16) return dispatch_ws<XT, __nv_bfloat16, true>(K, S, p, tm, pl, st);
+    if (wdt == SF_DTYPE_F32) return dispatch_ws<XT, float, true>(K, S, p, grid, pl, st);
+    if (wdt == SF_DTYPE_BF16) return dispatch_ws<XT, __nv_bfloat16, true>(K, S, p, grid, pl, st);
   } else {
-    if (wdt == SF_DTYPE_F32) return dispatch_ws<XT, float, false>(K, S, p, tm, pl, st);
-    if (wdt == SF_DTYPE_BF16) return dispatch_ws<XT, __nv_bfloat16, false>(K, S, p, tm, pl, st);
+    if (wdt == SF_DTYPE_F32) return dispatch_ws<XT, float, false>(K, S, p, grid, pl, st);
+    if (wdt == SF_DTYPE_BF16) return dispatch_ws<XT, __nv_bfloat16, false>(K, S, p, grid, pl, st);
   }
   return SF_ERR_UNSUPPORTED;
 }

@@ -1,0 +1,122 @@
+// Stage 1 of the sparse convolution: spike-event extraction.
+//
+// One streaming pass over x (NCHW, images = T*N) writes, for every pixel, a
+// bitmask of its nonzero input channels: nw = ceil(C/64) 64-bit words per
+// pixel, layout [image][h][w][nw]. For fp32 spikes this is 1/32 of the bytes
+// of x, so the convolution stage never has to stage x itself. The pass also
+// raises flags[image] when a nonzero value other than 1.0 occurs; only then
+// does the convolution read x values (binary spikes need none).
+//
+// This is the element-granular form of the reference's stage-1 metadata
+// (Kernels/_prescan_common.py:32-189 builds per-tile channel-group bits); the
+// tile-group metadata itself is produced bit-exactly by prescan.cu.
+#include "events.cuh"
+
+namespace sf {
+namespace {
+
+constexpr int kEvThreads = 256;
+
+template <typename T, int VEC>
+struct alignas(sizeof(T) * VEC) EVec {
+  T v[VEC];
+};
+
+template <typename XT, int VEC>
+__global__ void __launch_bounds__(kEvThreads) spike_masks_kernel(const XT* __restrict__ x, int C, int HW, int nw,
+                                                                 unsigned long long* __restrict__ masks,
+                                                                 uint32_t* __restrict__ flags) {
+  const int img = blockIdx.z;
+  const int word = blockIdx.y;
+  const int pix0 = (blockIdx.x * kEvThreads + threadIdx.x) * VEC;
+  const int c0 = word * 64;
+  const int cn = min(64, C - c0);
+  uint32_t lo[VEC], hi[VEC];
+  uint32_t bad = 0u;
+#pragma unroll
+  for (int e = 0; e < VEC; ++e) lo[e] = hi[e] = 0u;
+  if (pix0 < HW) {
+    const XT* src = x + ((size_t)img * C + c0) * HW + pix0;
+    int c = 0;
+    // Eight channels per step keep eight 16-byte loads in flight per thread.
+#pragma unroll 1
+    for (; c + 8 <= cn; c += 8) {
+      EVec<XT, VEC> r[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) r[u] = *reinterpret_cast<const EVec<XT, VEC>*>(src + (size_t)(c + u) * HW);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int cc = c + u;
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) {
+          const uint32_t nz = DT<XT>::nz_bit(r[u].v[e]);
+          bad |= nz & DT<XT>::not_one(r[u].v[e]);
+          if (cc < 32)
+            lo[e] |= nz << cc;
+          else
+            hi[e] |= nz << (cc - 32);
+        }
+      }
+    }
+    for (; c < cn; ++c) {
+      const EVec<XT, VEC> r = *reinterpret_cast<const EVec<XT, VEC>*>(src + (size_t)c * HW);
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) {
+        const uint32_t nz = DT<XT>::nz_bit(r.v[e]);
+        bad |= nz & DT<XT>::not_one(r.v[e]);
+        if (c < 32)
+          lo[e] |= nz << c;
+        else
+          hi[e] |= nz << (c - 32);
+      }
+    }
+    unsigned long long* dst = masks + ((size_t)img * HW + pix0) * nw + word;
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) dst[(size_t)e * nw] = ((unsigned long long)hi[e] << 32) | lo[e];
+  }
+  if (__syncthreads_or(bad != 0u) && threadIdx.x == 0) atomicOr(&flags[img], 1u);
+}
+
+template <typename XT>
+sf_status launch(const void* x, int nimg, int C, int HW, unsigned long long* masks, uint32_t* flags,
+                 cudaStream_t st) {
+  const int nw = (C + 63) / 64;
+  constexpr int V = 16 / (int)sizeof(XT);
+  const bool vec = aligned16(x) && HW % V == 0;
+  const int per_block = kEvThreads * (vec ? V : 1);
+  const dim3 grid((HW + per_block - 1) / per_block, nw, nimg);
+  if (grid.z > 65535u || grid.y > 65535u) return SF_ERR_UNSUPPORTED;
+  if (vec)
+    spike_masks_kernel<XT, V><<<grid, kEvThreads, 0, st>>>(static_cast<const XT*>(x), C, HW, nw, masks, flags);
+  else
+    spike_masks_kernel<XT, 1><<<grid, kEvThreads, 0, st>>>(static_cast<const XT*>(x), C, HW, nw, masks, flags);
+  return cudaGetLastError() == cudaSuccess ? SF_OK : SF_ERR_CUDA;
+}
+
+}  // namespace
+
+size_t event_workspace_bytes(long long nimg, int C, int HW) {
+  const size_t nw = (size_t)(C + 63) / 64;
+  const size_t mask_bytes = (size_t)nimg * HW * nw * 8;
+  return ((mask_bytes + 255) / 256) * 256 + (((size_t)nimg * 4 + 255) / 256) * 256;
+}
+
+sf_status extract_events(const void* x, int xdt, long long nimg, int C, int HW, void* workspace,
+                         size_t workspace_bytes, EventBuffers& out, cudaStream_t st) {
+  if (workspace_bytes < event_workspace_bytes(nimg, C, HW)) return SF_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return SF_ERR_ALIGNMENT;
+  const size_t nw = (size_t)(C + 63) / 64;
+  out.masks = static_cast<unsigned long long*>(workspace);
+  out.flags = reinterpret_cast<uint32_t*>(static_cast<char*>(workspace) +
+                                          (((size_t)nimg * HW * nw * 8 + 255) / 256) * 256);
+  out.nw = (int)nw;
+  if (cudaMemsetAsync(out.flags, 0, (size_t)nimg * 4, st) != cudaSuccess) return SF_ERR_CUDA;
+  switch (xdt) {
+    case SF_DTYPE_F32: return launch<float>(x, (int)nimg, C, HW, out.masks, out.flags, st);
+    case SF_DTYPE_F16: return launch<__half>(x, (int)nimg, C, HW, out.masks, out.flags, st);
+    case SF_DTYPE_BF16: return launch<__nv_bfloat16>(x, (int)nimg, C, HW, out.masks, out.flags, st);
+  }
+  return SF_ERR_INVALID_ARG;
+}
+
+}  // namespace sf
