@@ -111,9 +111,11 @@ sf_status sf_prescan2d_static_ws(const void* x, const sf_prescan_desc* d,
 /* Stage 2: gather-style sparse convolution (deterministic, atomic-free).    */
 /* ------------------------------------------------------------------------ */
 
-/* Packed layout: [c_out_pad / 32][c_in][kernel*kernel][32] (slices of 32
- * output channels), c_out_pad = c_out rounded up to a multiple of 128, zero
- * padded; element type w_dst_dtype (F32 or BF16). */
+/* Packed layout: [block][c_in][kernel*kernel][32][cpl], where block b holds
+ * output channels b*32*cpl + j*32 + lane (j < cpl), zero padded past c_out;
+ * cpl (1, 2 or 4) is the widest block whose weights fit in 160 KB, chosen by
+ * the library from (c_out, c_in, kernel, dtype); element type w_dst_dtype
+ * (F32 or BF16). Use sf_packed_weight_bytes for the size. */
 size_t sf_packed_weight_bytes(int32_t c_out, int32_t c_in, int32_t kernel, int32_t w_dst_dtype);
 sf_status sf_pack_weights(const void* w_oihw, int32_t w_src_dtype,
                           int32_t c_out, int32_t c_in, int32_t kernel,

@@ -109,6 +109,24 @@ __device__ __forceinline__ void tma_load_4d(void* dst_smem, const CUtensorMap* m
       : "memory");
 }
 
+// 4-D tiled tensor store (TMA) from shared memory, bulk-group completion.
+// Elements outside the tensor are not written. c0 * element size must be a
+// multiple of 16 bytes and stays >= 0.
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src_smem, int c0, int c1, int c2,
+                                             int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src_smem)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until the shared-memory sources of all committed bulk stores have been read.
+__device__ __forceinline__ void bulk_wait_group_read0() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_group0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 __device__ __forceinline__ uint64_t ld_acquire_u64(const uint64_t* p) {
   uint64_t v;
   asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");

@@ -23,13 +23,16 @@
 //     row; lane l owns output channels (slice j) * 32 + l, j < CPL. A warp
 //     reads the K x ((R-1)S+K) masks its segment needs (lane = pixel),
 //     ballots which are nonzero, and walks their set bits (ascending channel):
-//     each is an input event feeding up to K taps of the segment, one weight
-//     load per tap and slice into register accumulators (tap/pixel pairing is
-//     resolved at compile time). Binary spikes add weights; other values are
+//     each is an input event feeding up to K taps of the segment, one vector
+//     weight load (the lane's CPL channels) per tap into register accumulators
+//     (tap/pixel pairing is resolved at compile time). Binary spikes add weights; other values are
 //     read from x and multiplied. No atomics, fixed order: bit-identical runs.
 //   * Epilogue: bias (or the LIF update with v held in registers across all T
-//     steps); lane pairs exchange half rows by shuffle so every 16-byte store
-//     of a warp completes 32-byte sectors of NCHW rows.
+//     steps); the warp's [channels x R pixels] tile goes to a shared-memory
+//     slot and leaves with one asynchronous TMA tensor store, so output
+//     traffic overlaps the next unit. Where the row pitch rules TMA out, lane
+//     pairs exchange half rows by shuffle so every 16-byte store completes
+//     32-byte sectors of NCHW rows.
 #pragma once
 #include <algorithm>
 #include <cstdlib>
@@ -42,13 +45,37 @@ namespace conv {
 constexpr int kNWarps = 32;
 constexpr int kThreads = kNWarps * 32;
 constexpr int kComputeWarps = kNWarps - 1;
+#ifndef SF_CONV_ROWS_PER_WARP
+#define SF_CONV_ROWS_PER_WARP 1
+#endif
+// Output rows each compute warp accumulates (non-LIF kernels). Two rows read
+// each input event for more outputs per visit (2.5 instead of 3.75 visits per
+// event for 3x3 s1), but the doubled accumulator file spills at the 64
+// registers a 1024-thread CTA allows and measured 30% slower; one row is the
+// default.
+constexpr int kRowsPerWarp = SF_CONV_ROWS_PER_WARP;
 constexpr int kProducerWarp = kNWarps - 1;
 constexpr int kMaxStages = 8;
 constexpr int kSmemLimit = 227 * 1024;
 
-// Packed weights: [slice][C_in][k*k][32], slices of 32 output channels,
-// padded to a multiple of four slices (128 channels) with zeros.
-inline int co_slices_padded(int co) { return ((co + 127) / 128) * 4; }
+// Weights live in shared memory when one output-channel block fits this.
+constexpr size_t kWsmemMax = 160 * 1024;
+
+// 32-channel slices per lane (CPL) of the packed weight blocks: the widest
+// block (<= the layer) whose weights fit shared memory, else the widest block.
+inline int weight_block_cpl(int C, int K, int Co, int wsz) {
+  const int slices = (Co + 31) / 32;
+  for (int cpl = 4; cpl >= 1; cpl /= 2) {
+    if (cpl > 1 && cpl > slices) continue;
+    if ((size_t)C * K * K * 32 * cpl * wsz <= kWsmemMax) return cpl;
+  }
+  return slices >= 4 ? 4 : (slices >= 2 ? 2 : 1);
+}
+
+// Packed weights: [block][C_in][k*k][32 lanes][CPL], block b holding output
+// channels b*32*CPL + j*32 + lane; zero padded past C_out. A lane reads its
+// CPL channels of one (channel, tap) with one vector load.
+inline int weight_blocks(int Co, int cpl) { return ((Co + 31) / 32 + cpl - 1) / cpl; }
 
 // Optional phase timing (builds with -DSF_CONV_PHASE_PROFILE only): thread 0
 // accumulates cycles per phase in registers and adds them to g_conv_phase.
@@ -85,23 +112,68 @@ struct ConvParams {
   int slot_words;  // 64-bit words per mask stage
   int nstage;
   uint32_t w_cob_bytes;  // bytes of one output-channel block of packed weights (WSMEM kernels)
-  int w_off, bar_off;    // byte offsets in dynamic smem
+  int tma_store;         // 1: epilogue tiles leave through TMA tensor stores (y map)
+  int w_off, stg_off, bar_off;  // byte offsets in dynamic smem
 };
 
 struct Plan {
-  int CPL, R, TH, th_in, nstage, slot_words, wsmem;
-  int w_off, bar_off, smem;
+  int CPL, R, TH, th_in, nstage, slot_words, wsmem, tma_store;
+  int w_off, stg_off, bar_off, smem;
 };
 
-template <typename WT, bool SMEM>
-__device__ __forceinline__ float ldw(const WT* p) {
-  if constexpr (sizeof(WT) == 4) {
-    return SMEM ? *reinterpret_cast<const float*>(p) : __ldg(reinterpret_cast<const float*>(p));
-  } else {
-    const unsigned short* q = reinterpret_cast<const unsigned short*>(p);
-    return __uint_as_float((uint32_t)(SMEM ? *q : __ldg(q)) << 16);
+template <typename WT, int CPL, bool SMEM>
+struct WVec;
+template <bool SMEM>
+struct WVec<float, 1, SMEM> {
+  static __device__ __forceinline__ void ld(const float* p, float (&w)[1]) { w[0] = SMEM ? *p : __ldg(p); }
+};
+template <bool SMEM>
+struct WVec<float, 2, SMEM> {
+  static __device__ __forceinline__ void ld(const float* p, float (&w)[2]) {
+    const float2 v = SMEM ? *reinterpret_cast<const float2*>(p) : __ldg(reinterpret_cast<const float2*>(p));
+    w[0] = v.x;
+    w[1] = v.y;
   }
-}
+};
+template <bool SMEM>
+struct WVec<float, 4, SMEM> {
+  static __device__ __forceinline__ void ld(const float* p, float (&w)[4]) {
+    const float4 v = SMEM ? *reinterpret_cast<const float4*>(p) : __ldg(reinterpret_cast<const float4*>(p));
+    w[0] = v.x;
+    w[1] = v.y;
+    w[2] = v.z;
+    w[3] = v.w;
+  }
+};
+__device__ __forceinline__ float bf16_lo(uint32_t u) { return __uint_as_float(u << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t u) { return __uint_as_float(u & 0xffff0000u); }
+template <bool SMEM>
+struct WVec<__nv_bfloat16, 1, SMEM> {
+  static __device__ __forceinline__ void ld(const __nv_bfloat16* p, float (&w)[1]) {
+    const unsigned short* q = reinterpret_cast<const unsigned short*>(p);
+    w[0] = __uint_as_float((uint32_t)(SMEM ? *q : __ldg(q)) << 16);
+  }
+};
+template <bool SMEM>
+struct WVec<__nv_bfloat16, 2, SMEM> {
+  static __device__ __forceinline__ void ld(const __nv_bfloat16* p, float (&w)[2]) {
+    const unsigned int* q = reinterpret_cast<const unsigned int*>(p);
+    const uint32_t u = SMEM ? *q : __ldg(q);
+    w[0] = bf16_lo(u);
+    w[1] = bf16_hi(u);
+  }
+};
+template <bool SMEM>
+struct WVec<__nv_bfloat16, 4, SMEM> {
+  static __device__ __forceinline__ void ld(const __nv_bfloat16* p, float (&w)[4]) {
+    const uint2* q = reinterpret_cast<const uint2*>(p);
+    const uint2 u = SMEM ? *q : __ldg(q);
+    w[0] = bf16_lo(u.x);
+    w[1] = bf16_hi(u.x);
+    w[2] = bf16_lo(u.y);
+    w[3] = bf16_hi(u.y);
+  }
+};
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
@@ -184,12 +256,15 @@ __device__ __forceinline__ void store_slice(T* base, size_t co_stride, int co_li
   if (lane < co_lim) store_run<T, R>(base + lane * co_stride, v, nvalid);
 }
 
-template <int K, int S, int CPL, int R, typename XT, typename WT, bool LIF, bool WSMEM>
-__global__ void __launch_bounds__(kThreads, 1) sparse_conv_kernel(const ConvParams p) {
+template <int K, int S, int CPL, int R, int B, typename XT, typename WT, bool LIF, bool WSMEM>
+__global__ void __launch_bounds__(kThreads, 1)
+    sparse_conv_kernel(const ConvParams p, const __grid_constant__ CUtensorMap ymap) {
   extern __shared__ __align__(128) unsigned char smem[];
   constexpr int KK = K * K;
   constexpr int QN = (R - 1) * S + K;  // input columns a row segment reads
-  constexpr int NPOS = K * QN;         // input pixels a row segment reads
+  constexpr int HH = (B - 1) * S + K;  // input rows a warp tile (B output rows) reads
+  constexpr int NPOS = HH * QN;        // input pixels a warp tile reads
+  static_assert(!LIF || B == 1, "LIF keeps one output row per warp (register budget)");
   constexpr int ROUNDS = (NPOS + 31) / 32;
 
   unsigned long long* stages = reinterpret_cast<unsigned long long*>(smem);
@@ -203,7 +278,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_conv_kernel(const ConvPara
   const int u_begin = blockIdx.x * p.units_per_cta;
   const int u_end = min(p.n_units, u_begin + p.units_per_cta);
   const int upc = p.n_units / p.ncob;  // units per output-channel block
-  const size_t wslice = (size_t)p.C * KK * 32;  // elements of one 32-channel weight slice
+  const size_t wblock = (size_t)p.C * KK * 32 * CPL;  // elements of one packed weight block
 
   if (tid == 0) {
     for (int s = 0; s < p.nstage; ++s) {
@@ -233,7 +308,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_conv_kernel(const ConvPara
             }
           }
           mbar_arrive_expect_tx(wbar, p.w_cob_bytes);
-          bulk_g2s(smem + p.w_off, static_cast<const WT*>(p.wp) + (size_t)cob * CPL * wslice, p.w_cob_bytes, wbar);
+          bulk_g2s(smem + p.w_off, static_cast<const WT*>(p.wp) + (size_t)cob * wblock, p.w_cob_bytes, wbar);
           cur_cob = cob;
         }
         const int ihs = band * p.TH * S - p.P;
@@ -267,17 +342,36 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_conv_kernel(const ConvPara
 #endif
   const XT* __restrict__ x = static_cast<const XT*>(p.x);
   const WT* __restrict__ wglob = static_cast<const WT*>(p.wp);
-  float acc[R][CPL];
+  float acc[B * R][CPL];
   float vreg[LIF ? CPL : 1][LIF ? R : 1];
   int g = 0, cur_cob = -1, wloads = 0;
 
+  // This warp's place in every unit: row tile tr (output rows tr*B .. +B-1)
+  // of the band, segment si of the column block.
+  const int tr = warp / p.tpu;
+  const int si = warp - tr * p.tpu;
+  // Unit coordinates of u_begin; advanced with carries below.
+  int cob = u_begin / upc;
+  int rest0 = u_begin - cob * upc;
+  int n = rest0 / (p.nbands * p.ncolb);
+  rest0 -= n * p.nbands * p.ncolb;
+  int band = rest0 / p.ncolb;
+  int colb = rest0 - band * p.ncolb;
+  const size_t hw_out = (size_t)p.Ho * p.Wo;
+
   for (int u = u_begin; u < u_end; ++u) {
-    const int cob = u / upc;
-    const int rest = u - cob * upc;
-    const int n = rest / (p.nbands * p.ncolb);
-    const int rb = rest - n * p.nbands * p.ncolb;
-    const int band = rb / p.ncolb;
-    const int colb = rb - band * p.ncolb;
+    if (u > u_begin) {
+      if (++colb == p.ncolb) {
+        colb = 0;
+        if (++band == p.nbands) {
+          band = 0;
+          if (++n == p.N) {
+            n = 0;
+            ++cob;
+          }
+        }
+      }
+    }
     if (WSMEM && cob != cur_cob) {
       if (!mbar_wait_bounded(wbar, (uint32_t)(wloads & 1))) {
         if (lane == 0) atomicExch(p.err, 1u);
@@ -291,18 +385,17 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_conv_kernel(const ConvPara
     const int ihs = r0 * S - p.P;
     const int ih_lo = max(0, ihs);
     const int ih_hi = min(p.H, ihs + p.th_in);
-    const size_t hw_out = (size_t)p.Ho * p.Wo;
 
     // This warp's row segment.
-    const int tr = warp / p.tpu;
-    const int segi = colb * p.tpu + (warp - tr * p.tpu);
+    const int segi = colb * p.tpu + si;
     const int seg0 = segi * R;
-    const bool active = tr < rows_out && segi < p.tpr;
+    const bool active = tr * B < rows_out && segi < p.tpr;
+    const int nrows = min(B, rows_out - tr * B);
     const int nvalid = min(R, p.Wo - seg0);
-    const int orow = r0 + tr;
-    const int ih0 = ihs + tr * S;     // input row of tap row 0
+    const int orow = r0 + tr * B;
+    const int ih0 = ihs + tr * B * S;  // input row of the tile's first input row
     const int col0 = seg0 * S - p.P;  // input column of position 0
-    const WT* wbase = (WSMEM ? wsm : wglob + (size_t)cob * CPL * wslice) + lane;
+    const WT* wbase = (WSMEM ? wsm : wglob + (size_t)cob * wblock) + lane * CPL;
 
     if constexpr (LIF) {
       if (active) {
@@ -333,7 +426,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_conv_kernel(const ConvPara
       const bool binary = (__ldg(p.flags + img) & 1u) == 0u;
 
 #pragma unroll
-      for (int i = 0; i < R; ++i)
+      for (int i = 0; i < B * R; ++i)
 #pragma unroll
         for (int j = 0; j < CPL; ++j) acc[i][j] = 0.f;
 
@@ -344,9 +437,9 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_conv_kernel(const ConvPara
 #pragma unroll
         for (int rd = 0; rd < ROUNDS; ++rd) {
           const int pos = rd * 32 + lane;
-          const int kh = pos / QN;
-          const int qq = pos - kh * QN;
-          const int ih = ih0 + kh;
+          const int hh = pos / QN;
+          const int qq = pos - hh * QN;
+          const int ih = ih0 + hh;
           const int iw = col0 + qq;
           unsigned long long m = 0ull;
           if (active && pos < NPOS && iw >= 0 && iw < p.W && ih >= ih_lo && ih < ih_hi)
@@ -360,36 +453,52 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_conv_kernel(const ConvPara
           constexpr bool BIN = decltype(binary_tag)::value;
 #pragma unroll
           for (int pos = 0; pos < NPOS; ++pos) {
-            const int kh = pos / QN;
-            const int qq = pos - kh * QN;
+            const int hh = pos / QN;
+            const int qq = pos - hh * QN;
             if (((nzpos[pos / 32] >> (pos % 32)) & 1u) == 0u) continue;
-            unsigned long long m = shfl64(mk[pos / 32], pos % 32);
-            while (m) {
-              const int ci = __ffsll((long long)m) - 1;
-              m &= m - 1ull;
-              const int c = wd * 64 + ci;
-              const WT* wc = wbase + ((size_t)c * KK + kh * K) * 32;
-              float xv = 1.f;
-              if constexpr (!BIN)
-                xv = DT<XT>::to_f(__ldg(x + ((img * p.C + c) * p.H + (ih0 + kh)) * p.W + (col0 + qq)));
+            const unsigned long long m64 = shfl64(mk[pos / 32], pos % 32);
+            const WT* wrow = wbase + (size_t)wd * 64 * KK * 32 * CPL;
 #pragma unroll
-              for (int kw = 0; kw < K; ++kw) {
-                const int d = qq - kw;
-                if (d >= 0 && d % S == 0 && d / S < R) {
+            for (int hw = 0; hw < 2; ++hw) {
+              uint32_t m = hw ? (uint32_t)(m64 >> 32) : (uint32_t)m64;
+              while (m) {
+                const int ci = __ffs(m) - 1 + 32 * hw;
+                m &= m - 1u;
+                const WT* wc = wrow + (size_t)ci * (KK * 32 * CPL);
+                float xv = 1.f;
+                if constexpr (!BIN)
+                  xv = DT<XT>::to_f(
+                      __ldg(x + ((img * p.C + wd * 64 + ci) * p.H + (ih0 + hh)) * p.W + (col0 + qq)));
 #pragma unroll
-                  for (int j = 0; j < CPL; ++j) {
-                    const float w = ldw<WT, WSMEM>(wc + j * wslice + kw * 32);
-                    if constexpr (BIN)
-                      acc[d / S][j] += w;
-                    else
-                      acc[d / S][j] = fmaf(xv, w, acc[d / S][j]);
+                for (int kh = 0; kh < K; ++kh) {
+                  const int rb = hh - kh;  // S * (output row within the tile)
+                  if (rb >= 0 && rb % S == 0 && rb / S < B) {
+#pragma unroll
+                    for (int kw = 0; kw < K; ++kw) {
+                      const int d = qq - kw;
+                      if (d >= 0 && d % S == 0 && d / S < R) {
+                        float w[CPL];
+                        WVec<WT, CPL, WSMEM>::ld(wc + (kh * K + kw) * 32 * CPL, w);
+#pragma unroll
+                        for (int j = 0; j < CPL; ++j) {
+                          if constexpr (BIN)
+                            acc[(rb / S) * R + d / S][j] += w[j];
+                          else
+                            acc[(rb / S) * R + d / S][j] = fmaf(xv, w[j], acc[(rb / S) * R + d / S][j]);
+                        }
+                      }
+                    }
                   }
                 }
               }
             }
           }
         };
+#ifdef SF_CONV_EXPERIMENT_NO_GATHER
+        if (false) {
+#else
         if (active) {
+#endif
           if (binary)
             gather(std::true_type{});
           else
@@ -401,32 +510,63 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_conv_kernel(const ConvPara
       SF_PHASE(2);
 
       // Epilogue for (unit, t).
+#ifdef SF_CONV_EXPERIMENT_NO_EPILOGUE
+      if (false) {
+#else
       if (active) {
+#endif
 #pragma unroll
-        for (int j = 0; j < CPL; ++j) {
-          const int co0 = (cob * CPL + j) * 32;
-          const int co = co0 + lane;
-          const float b = (p.bias != nullptr && co < p.Co) ? __ldg(p.bias + co) : 0.f;
-          float out[R];
+        for (int b = 0; b < B; ++b) {
+          if (b >= nrows) break;
+          float out[CPL][R];
 #pragma unroll
-          for (int i = 0; i < R; ++i) {
-            float val = acc[i][j] + b;
-            if constexpr (LIF) {
-              const float vp = vreg[j][i];
-              const float vr = p.hard_reset ? p.vreset : 0.f;
-              float vt;
-              if (p.decay_input)
-                vt = vp + (val - (vp - vr)) / p.tau;
-              else
-                vt = vp - (vp - vr) / p.tau + val;
-              const bool spk = vt >= p.vth;
-              vreg[j][i] = p.hard_reset ? (spk ? p.vreset : vt) : (vt - (spk ? p.vth : 0.f));
-              val = spk ? 1.f : 0.f;
+          for (int j = 0; j < CPL; ++j) {
+            const int co = (cob * CPL + j) * 32 + lane;
+            const float bias_v = (p.bias != nullptr && co < p.Co) ? __ldg(p.bias + co) : 0.f;
+#pragma unroll
+            for (int i = 0; i < R; ++i) {
+              float val = acc[b * R + i][j] + bias_v;
+              if constexpr (LIF) {
+                const float vp = vreg[j][i];
+                const float vr = p.hard_reset ? p.vreset : 0.f;
+                float vt;
+                if (p.decay_input)
+                  vt = vp + (val - (vp - vr)) / p.tau;
+                else
+                  vt = vp - (vp - vr) / p.tau + val;
+                const bool spk = vt >= p.vth;
+                vreg[j][i] = p.hard_reset ? (spk ? p.vreset : vt) : (vt - (spk ? p.vth : 0.f));
+                val = spk ? 1.f : 0.f;
+              }
+              out[j][i] = val;
             }
-            out[i] = val;
           }
-          XT* ybase = static_cast<XT*>(p.y) + (img * p.Co + co0) * hw_out + (size_t)orow * p.Wo + seg0;
-          store_slice<XT, R>(ybase, hw_out, p.Co - co0, lane, nvalid, out);
+          if (p.tma_store) {
+            // Tile [32*CPL channels][R pixels] through this warp's staging
+            // slot; one TMA tensor store writes it (clipped at the edges).
+            XT* stg = reinterpret_cast<XT*>(smem + p.stg_off) + (size_t)warp * (32 * CPL * R);
+            if (lane == 0) bulk_wait_group_read0();  // previous tile has left the slot
+            __syncwarp();
+#pragma unroll
+            for (int j = 0; j < CPL; ++j) {
+              XT* row = stg + (size_t)(j * 32 + lane) * R;
+#pragma unroll
+              for (int i = 0; i < R; ++i) row[i] = DT<XT>::from_f(out[j][i]);
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_4d(&ymap, stg, seg0, orow + b, cob * CPL * 32, (int)img);
+              bulk_commit_group();
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < CPL; ++j) {
+              const int co0 = (cob * CPL + j) * 32;
+              XT* ybase = static_cast<XT*>(p.y) + (img * p.Co + co0) * hw_out + (size_t)(orow + b) * p.Wo + seg0;
+              store_slice<XT, R>(ybase, hw_out, p.Co - co0, lane, nvalid, out[j]);
+            }
+          }
         }
       }
       SF_PHASE(3);
@@ -443,63 +583,67 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_conv_kernel(const ConvPara
       }
     }
   }
+  if (p.tma_store && lane == 0) bulk_wait_group0();  // stores complete before the CTA leaves
 #ifdef SF_CONV_PHASE_PROFILE
   if (tid == 0)
     for (int i = 0; i < 5; ++i) atomicAdd(&g_conv_phase[i], (unsigned long long)ph_acc[i]);
 #endif
 }
 
-template <int K, int S, int CPL, int R, typename XT, typename WT, bool LIF, bool WSMEM>
-sf_status launch_conv(const ConvParams& p, int grid, int smem, cudaStream_t st) {
-  auto kern = sparse_conv_kernel<K, S, CPL, R, XT, WT, LIF, WSMEM>;
+template <int K, int S, int CPL, int R, int B, typename XT, typename WT, bool LIF, bool WSMEM>
+sf_status launch_conv(const ConvParams& p, const CUtensorMap& ymap, int grid, int smem, cudaStream_t st) {
+  auto kern = sparse_conv_kernel<K, S, CPL, R, B, XT, WT, LIF, WSMEM>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return SF_ERR_CUDA;
-  kern<<<grid, kThreads, smem, st>>>(p);
+  kern<<<grid, kThreads, smem, st>>>(p, ymap);
   return cudaGetLastError() == cudaSuccess ? SF_OK : SF_ERR_CUDA;
 }
 
 template <int K, int S, typename XT, typename WT, bool LIF, bool WSMEM>
-sf_status dispatch_cpl(const ConvParams& p, int grid, const Plan& pl, cudaStream_t st) {
-  if (pl.CPL == 1) return launch_conv<K, S, 1, 8, XT, WT, LIF, WSMEM>(p, grid, pl.smem, st);
-  if (pl.CPL == 2) return launch_conv<K, S, 2, 8, XT, WT, LIF, WSMEM>(p, grid, pl.smem, st);
-  return launch_conv<K, S, 4, 4, XT, WT, LIF, WSMEM>(p, grid, pl.smem, st);
+sf_status dispatch_cpl(const ConvParams& p, const CUtensorMap& ym, int grid, const Plan& pl, cudaStream_t st) {
+  constexpr int B = LIF ? 1 : kRowsPerWarp;  // output rows per warp
+  if (pl.CPL == 1) return launch_conv<K, S, 1, 8, B, XT, WT, LIF, WSMEM>(p, ym, grid, pl.smem, st);
+  if (pl.CPL == 2) return launch_conv<K, S, 2, 8, B, XT, WT, LIF, WSMEM>(p, ym, grid, pl.smem, st);
+  return launch_conv<K, S, 4, 4, B, XT, WT, LIF, WSMEM>(p, ym, grid, pl.smem, st);
 }
 
 template <typename XT, typename WT, bool LIF, bool WSMEM>
-sf_status dispatch_geom(int K, int S, const ConvParams& p, int grid, const Plan& pl, cudaStream_t st) {
-  if (K == 3 && S == 1) return dispatch_cpl<3, 1, XT, WT, LIF, WSMEM>(p, grid, pl, st);
+sf_status dispatch_geom(int K, int S, const ConvParams& p, const CUtensorMap& ym, int grid, const Plan& pl,
+                        cudaStream_t st) {
+  if (K == 3 && S == 1) return dispatch_cpl<3, 1, XT, WT, LIF, WSMEM>(p, ym, grid, pl, st);
   if constexpr (!LIF) {
-    if (K == 3 && S == 2) return dispatch_cpl<3, 2, XT, WT, LIF, WSMEM>(p, grid, pl, st);
+    if (K == 3 && S == 2) return dispatch_cpl<3, 2, XT, WT, LIF, WSMEM>(p, ym, grid, pl, st);
   }
-  if (K == 1 && S == 1) return dispatch_cpl<1, 1, XT, WT, LIF, WSMEM>(p, grid, pl, st);
+  if (K == 1 && S == 1) return dispatch_cpl<1, 1, XT, WT, LIF, WSMEM>(p, ym, grid, pl, st);
   return SF_ERR_UNSUPPORTED;
 }
 
 // Per input dtype: launches the kernel instantiation matching (LIF, weight
 // dtype, weights in shared memory, kernel/stride, slices per lane). Defined
 // in conv_<dtype>.cu.
-sf_status dispatch_f32(bool lif, int wdt, int K, int S, const ConvParams& p, int grid, const Plan& pl,
-                       cudaStream_t st);
-sf_status dispatch_f16(bool lif, int wdt, int K, int S, const ConvParams& p, int grid, const Plan& pl,
-                       cudaStream_t st);
-sf_status dispatch_bf16(bool lif, int wdt, int K, int S, const ConvParams& p, int grid, const Plan& pl,
-                        cudaStream_t st);
+sf_status dispatch_f32(bool lif, int wdt, int K, int S, const ConvParams& p, const CUtensorMap& ym, int grid,
+                       const Plan& pl, cudaStream_t st);
+sf_status dispatch_f16(bool lif, int wdt, int K, int S, const ConvParams& p, const CUtensorMap& ym, int grid,
+                       const Plan& pl, cudaStream_t st);
+sf_status dispatch_bf16(bool lif, int wdt, int K, int S, const ConvParams& p, const CUtensorMap& ym, int grid,
+                        const Plan& pl, cudaStream_t st);
 
 template <typename XT, typename WT, bool LIF>
-sf_status dispatch_ws(int K, int S, const ConvParams& p, int grid, const Plan& pl, cudaStream_t st) {
-  if (pl.wsmem) return dispatch_geom<XT, WT, LIF, true>(K, S, p, grid, pl, st);
-  return dispatch_geom<XT, WT, LIF, false>(K, S, p, grid, pl, st);
+sf_status dispatch_ws(int K, int S, const ConvParams& p, const CUtensorMap& ym, int grid, const Plan& pl,
+                      cudaStream_t st) {
+  if (pl.wsmem) return dispatch_geom<XT, WT, LIF, true>(K, S, p, ym, grid, pl, st);
+  return dispatch_geom<XT, WT, LIF, false>(K, S, p, ym, grid, pl, st);
 }
 
 template <typename XT>
-sf_status dispatch_x(bool lif, int wdt, int K, int S, const ConvParams& p, int grid, const Plan& pl,
-                     cudaStream_t st) {
+sf_status dispatch_x(bool lif, int wdt, int K, int S, const ConvParams& p, const CUtensorMap& ym, int grid,
+                     const Plan& pl, cudaStream_t st) {
   if (lif) {
-    if (wdt == SF_DTYPE_F32) return dispatch_ws<XT, float, true>(K, S, p, grid, pl, st);
-    if (wdt == SF_DTYPE_BF16) return dispatch_ws<XT, __nv_bfloat16, true>(K, S, p, grid, pl, st);
+    if (wdt == SF_DTYPE_F32) return dispatch_ws<XT, float, true>(K, S, p, ym, grid, pl, st);
+    if (wdt == SF_DTYPE_BF16) return dispatch_ws<XT, __nv_bfloat16, true>(K, S, p, ym, grid, pl, st);
   } else {
-    if (wdt == SF_DTYPE_F32) return dispatch_ws<XT, float, false>(K, S, p, grid, pl, st);
-    if (wdt == SF_DTYPE_BF16) return dispatch_ws<XT, __nv_bfloat16, false>(K, S, p, grid, pl, st);
+    if (wdt == SF_DTYPE_F32) return dispatch_ws<XT, float, false>(K, S, p, ym, grid, pl, st);
+    if (wdt == SF_DTYPE_BF16) return dispatch_ws<XT, __nv_bfloat16, false>(K, S, p, ym, grid, pl, st);
   }
   return SF_ERR_UNSUPPORTED;
 }

@@ -3,6 +3,7 @@
 // planning, weight packing. The kernels are in events.cu and conv_kernel.cuh.
 #include <cstdlib>
 #include <cstring>
+#include <cudaTypedefs.h>
 #include "conv_kernel.cuh"
 #include "events.cuh"
 
@@ -14,19 +15,21 @@ namespace {
 // sf_sparse_conv2d_status); a static device word, so no allocation is needed.
 __device__ uint32_t g_conv_error = 0;
 
-// [co][ci][kk] (any dtype) -> [slice][ci][kk][32] (fp32 or bf16), zero padded.
+// [co][ci][kk] (any dtype) -> [block][ci][kk][32][cpl] (fp32 or bf16), zero padded.
 template <typename WT>
 __global__ void pack_weights_kernel(const void* __restrict__ w, int src_dtype, WT* __restrict__ out, int Co, int Ci,
-                                    int KK, int slices) {
-  const size_t total = (size_t)slices * Ci * KK * 32;
+                                    int KK, int blocks, int cpl) {
+  const size_t total = (size_t)blocks * Ci * KK * 32 * cpl;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
-    const int l = (int)(i & 31);
-    size_t r = i >> 5;
+    const int j = (int)(i % cpl);
+    size_t r = i / cpl;
+    const int l = (int)(r & 31);
+    r >>= 5;
     const int t = (int)(r % KK);
     r /= KK;
     const int ci = (int)(r % Ci);
-    const int sl = (int)(r / Ci);
-    const int co = sl * 32 + l;
+    const int b = (int)(r / Ci);
+    const int co = (b * cpl + j) * 32 + l;
     float v = 0.f;
     if (co < Co) {
       const size_t src = ((size_t)co * Ci + ci) * KK + t;
@@ -49,47 +52,57 @@ int env_int(const char* name) {
   return v ? atoi(v) : 0;
 }
 
-// Launch plan: 32-channel slices per lane (CPL), row-segment length R, band
-// height TH (one row segment per compute warp), mask stages, and whether a
-// block of packed weights lives in shared memory. SF_CONV_CPL / SF_CONV_TH /
-// SF_CONV_NSTAGE / SF_CONV_NO_WSMEM (environment) pin choices for tuning.
-bool make_plan(int K, int S, int C, int W, int Co, int Ho, int Wo, int nw, int wsz, Plan& pl) {
-  const int force_cpl = env_int("SF_CONV_CPL"), force_th = env_int("SF_CONV_TH"), force_ns = env_int("SF_CONV_NSTAGE");
-  const int slices = (Co + 31) / 32;
+// Launch plan: 32-channel slices per lane (CPL, fixed by the weight packing),
+// row-segment length R, band height TH (one row segment per compute warp),
+// mask stages, and whether a block of packed weights lives in shared memory.
+// SF_CONV_TH / SF_CONV_NSTAGE / SF_CONV_NO_WSMEM (environment) pin choices for
+// tuning.
+bool make_plan(int K, int S, int C, int W, int Co, int Ho, int Wo, int nw, int wsz, int esz, bool y_tma_ok,
+               bool lif, Plan& pl) {
+  const int B = lif ? 1 : kRowsPerWarp;  // output rows per compute warp (matches the kernel)
+  const int force_th = env_int("SF_CONV_TH"), force_ns = env_int("SF_CONV_NSTAGE");
   const int bar_bytes = (2 * kMaxStages + 1) * 8;
-  for (int wsmem = env_int("SF_CONV_NO_WSMEM") ? 0 : 1; wsmem >= 0; --wsmem) {
-    for (int cpl = 4; cpl >= 1; cpl /= 2) {
-      if (force_cpl && cpl != force_cpl) continue;
-      if (!force_cpl && cpl > 1 && cpl > slices) continue;  // no wider block than the layer
-      const int R = cpl == 4 ? 4 : 8;
-      const int tpr = (Wo + R - 1) / R;
-      const int tpu = std::min(tpr, kComputeWarps);
-      const size_t w_bytes = (size_t)C * K * K * 32 * cpl * wsz;
-      const int w_region = wsmem ? (int)std::min<size_t>(((w_bytes + 127) / 128) * 128, 1u << 30) : 0;
-      for (int TH = std::min(Ho, kComputeWarps / tpu); TH >= 1; --TH) {
-        if (force_th && TH != force_th) continue;
-        const int th_in = (TH - 1) * S + K;
-        const int slot_words = ((th_in * W * nw + 2) + 1) & ~1;
-        const int stage_bytes = slot_words * 8;
-        const long long fixed = (long long)w_region + bar_bytes;
-        if (fixed + 2ll * stage_bytes > kSmemLimit) continue;
-        int nstage = (int)std::min<long long>(kMaxStages, (kSmemLimit - fixed) / stage_bytes);
-        if (force_ns) {
-          if (force_ns > nstage) continue;
-          nstage = force_ns;
-        }
-        pl.CPL = cpl;
-        pl.R = R;
-        pl.wsmem = wsmem;
-        pl.TH = TH;
-        pl.th_in = th_in;
-        pl.nstage = nstage;
-        pl.slot_words = slot_words;
-        pl.w_off = nstage * stage_bytes;
-        pl.bar_off = pl.w_off + w_region;
-        pl.smem = pl.bar_off + bar_bytes;
-        return true;
+  const int cpl = weight_block_cpl(C, K, Co, wsz);
+  const size_t w_bytes = (size_t)C * K * K * 32 * cpl * wsz;
+  const bool ws_ok = w_bytes <= kWsmemMax && env_int("SF_CONV_NO_WSMEM") == 0;
+  const int R = cpl == 4 ? 4 : 8;
+  // TMA tensor stores need 16-byte row pitch and 16-byte tile rows.
+  // Off unless SF_CONV_TMA_STORE=1: plain sector-complete stores measured faster.
+  const bool tma_ok = y_tma_ok && (Wo * esz) % 16 == 0 && (R * esz) % 16 == 0 && env_int("SF_CONV_TMA_STORE") == 1;
+  for (int combo = 0; combo < 4; ++combo) {
+    const int wsmem = (combo < 2) ? (ws_ok ? 1 : -1) : 0;  // prefer weights in smem, then TMA stores
+    const int tma = (combo % 2 == 0) ? (tma_ok ? 1 : -1) : 0;
+    if (wsmem < 0 || tma < 0) continue;
+    const int tpr = (Wo + R - 1) / R;
+    const int tpu = std::min(tpr, kComputeWarps);
+    const int w_region = wsmem ? (int)(((w_bytes + 127) / 128) * 128) : 0;
+    const int stg_region = tma ? kComputeWarps * 32 * cpl * R * esz : 0;
+    for (int TH = std::min(Ho, B * (kComputeWarps / tpu)); TH >= 1; --TH) {
+      if (force_th && TH != force_th) continue;
+      const int th_in = (TH - 1) * S + K;
+      // 128-byte aligned stages keep every region after them 128-byte aligned.
+      const int slot_words = ((th_in * W * nw + 2) + 15) & ~15;
+      const int stage_bytes = slot_words * 8;
+      const long long fixed = (long long)w_region + stg_region + bar_bytes;
+      if (fixed + 2ll * stage_bytes > kSmemLimit) continue;
+      int nstage = (int)std::min<long long>(kMaxStages, (kSmemLimit - fixed) / stage_bytes);
+      if (force_ns) {
+        if (force_ns > nstage) continue;
+        nstage = force_ns;
       }
+      pl.CPL = cpl;
+      pl.R = R;
+      pl.wsmem = wsmem;
+      pl.tma_store = tma;
+      pl.TH = TH;
+      pl.th_in = th_in;
+      pl.nstage = nstage;
+      pl.slot_words = slot_words;
+      pl.w_off = nstage * stage_bytes;
+      pl.stg_off = pl.w_off + w_region;
+      pl.bar_off = pl.stg_off + stg_region;
+      pl.smem = pl.bar_off + bar_bytes;
+      return true;
     }
   }
   return false;
@@ -115,12 +128,43 @@ int num_sms_current_device() {
 namespace conv {
 namespace {
 
-sf_status dispatch(bool lif, int xdt, int wdt, int K, int S, const ConvParams& p, int grid, const Plan& pl,
-                   cudaStream_t st) {
-  if (xdt == SF_DTYPE_F32) return dispatch_f32(lif, wdt, K, S, p, grid, pl, st);
-  if (xdt == SF_DTYPE_F16) return dispatch_f16(lif, wdt, K, S, p, grid, pl, st);
-  if (xdt == SF_DTYPE_BF16) return dispatch_bf16(lif, wdt, K, S, p, grid, pl, st);
+sf_status dispatch(bool lif, int xdt, int wdt, int K, int S, const ConvParams& p, const CUtensorMap& ym, int grid,
+                   const Plan& pl, cudaStream_t st) {
+  if (xdt == SF_DTYPE_F32) return dispatch_f32(lif, wdt, K, S, p, ym, grid, pl, st);
+  if (xdt == SF_DTYPE_F16) return dispatch_f16(lif, wdt, K, S, p, ym, grid, pl, st);
+  if (xdt == SF_DTYPE_BF16) return dispatch_bf16(lif, wdt, K, S, p, ym, grid, pl, st);
   return SF_ERR_UNSUPPORTED;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// y viewed as 4-D (W_out, H_out, C_out, T*N), box (R, 1, 32*CPL, 1).
+sf_status encode_y_map(CUtensorMap* m, void* y, int xdt, int Wo, int Ho, int Co, long long nimg, int R, int cpl) {
+  auto fn = tensor_map_encoder();
+  if (!fn) return SF_ERR_CUDA;
+  const CUtensorMapDataType dt = xdt == SF_DTYPE_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : xdt == SF_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                       : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const cuuint64_t esz = dtype_size(xdt);
+  const cuuint64_t dims[4] = {(cuuint64_t)Wo, (cuuint64_t)Ho, (cuuint64_t)Co, (cuuint64_t)nimg};
+  const cuuint64_t strides[3] = {Wo * esz, (cuuint64_t)Ho * Wo * esz, (cuuint64_t)Co * Ho * Wo * esz};
+  const cuuint32_t box[4] = {(cuuint32_t)R, 1u, (cuuint32_t)(32 * cpl), 1u};
+  const cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
+  const CUresult r = fn(m, dt, 4, y, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? SF_OK : SF_ERR_CUDA;
 }
 
 sf_status check_geometry(int T, int N, int C, int H, int W, int Co, int Ho, int Wo, int K, int S, int P, int xdt,
@@ -145,7 +189,9 @@ sf_status run_conv(const void* x, const void* w_packed, const float* bias, void*
   if (!aligned16(w_packed)) return SF_ERR_ALIGNMENT;
   const int nw = (C + 63) / 64;
   Plan pl;
-  if (!make_plan(K, S, C, W, Co, Ho, Wo, nw, (int)dtype_size(wdt), pl)) return SF_ERR_UNSUPPORTED;
+  const bool y_tma_ok = aligned16(y) && tensor_map_encoder() != nullptr;
+  if (!make_plan(K, S, C, W, Co, Ho, Wo, nw, (int)dtype_size(wdt), (int)dtype_size(xdt), y_tma_ok, lif, pl))
+    return SF_ERR_UNSUPPORTED;
 
   EventBuffers ev;
   s = extract_events(x, xdt, (long long)T * N, C, H * W, workspace, ws_bytes, ev, st);
@@ -191,9 +237,17 @@ sf_status run_conv(const void* x, const void* w_packed, const float* bias, void*
   p.nstage = pl.nstage;
   p.w_cob_bytes = (uint32_t)((size_t)C * K * K * 32 * pl.CPL * dtype_size(wdt));
   p.w_off = pl.w_off;
+  p.stg_off = pl.stg_off;
   p.bar_off = pl.bar_off;
+  p.tma_store = pl.tma_store;
+  CUtensorMap ym;
+  memset(&ym, 0, sizeof(ym));
+  if (pl.tma_store) {
+    s = encode_y_map(&ym, y, xdt, Wo, Ho, Co, (long long)T * N, pl.R, pl.CPL);
+    if (s != SF_OK) return s;
+  }
   const int grid_used = (p.n_units + p.units_per_cta - 1) / p.units_per_cta;
-  return dispatch(lif, xdt, wdt, K, S, p, grid_used, pl, st);
+  return dispatch(lif, xdt, wdt, K, S, p, ym, grid_used, pl, st);
 }
 
 }  // namespace
@@ -205,7 +259,9 @@ using namespace sf::conv;
 
 extern "C" size_t sf_packed_weight_bytes(int32_t c_out, int32_t c_in, int32_t kernel, int32_t w_dst_dtype) {
   if (c_out <= 0 || c_in <= 0 || kernel <= 0) return 0;
-  return (size_t)co_slices_padded(c_out) * 32 * c_in * kernel * kernel * dtype_size(w_dst_dtype);
+  const int wsz = (int)dtype_size(w_dst_dtype);
+  const int cpl = weight_block_cpl(c_in, kernel, c_out, wsz);
+  return (size_t)weight_blocks(c_out, cpl) * cpl * 32 * c_in * kernel * kernel * wsz;
 }
 
 extern "C" sf_status sf_pack_weights(const void* w_oihw, int32_t w_src_dtype, int32_t c_out, int32_t c_in,
@@ -213,17 +269,18 @@ extern "C" sf_status sf_pack_weights(const void* w_oihw, int32_t w_src_dtype, in
   if (!w_oihw || !w_packed || c_out <= 0 || c_in <= 0 || kernel <= 0) return SF_ERR_INVALID_ARG;
   if (dtype_size(w_src_dtype) == 0) return SF_ERR_INVALID_ARG;
   if (w_dst_dtype != SF_DTYPE_F32 && w_dst_dtype != SF_DTYPE_BF16) return SF_ERR_UNSUPPORTED;
-  const int slices = co_slices_padded(c_out);
+  const int cpl = weight_block_cpl(c_in, kernel, c_out, (int)dtype_size(w_dst_dtype));
+  const int blocks_w = weight_blocks(c_out, cpl);
   const int KK = kernel * kernel;
-  const size_t total = (size_t)slices * c_in * KK * 32;
+  const size_t total = (size_t)blocks_w * c_in * KK * 32 * cpl;
   const int blocks = (int)std::min<size_t>((total + 255) / 256, 4096);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (w_dst_dtype == SF_DTYPE_F32)
     pack_weights_kernel<float><<<blocks, 256, 0, st>>>(w_oihw, w_src_dtype, static_cast<float*>(w_packed), c_out,
-                                                       c_in, KK, slices);
+                                                       c_in, KK, blocks_w, cpl);
   else
     pack_weights_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(
-        w_oihw, w_src_dtype, static_cast<__nv_bfloat16*>(w_packed), c_out, c_in, KK, slices);
+        w_oihw, w_src_dtype, static_cast<__nv_bfloat16*>(w_packed), c_out, c_in, KK, blocks_w, cpl);
   return cudaGetLastError() == cudaSuccess ? SF_OK : SF_ERR_CUDA;
 }
 
