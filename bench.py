@@ -51,10 +51,14 @@ METRIC = "sparse conv3x3 GB/s (layer1.x.conv2 shape, 99% spike sparsity)"
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-extra", action="store_true", help="skip the C2/C3/prescan side measurements")
+    ap.add_argument("--only-timed", action="store_true",
+                    help="run only the warm-up and timed steps (no cuDNN, e2e, extras or CPU baseline); for ncu")
+    ap.add_argument("--images", type=int, default=T_STEPS * N_BATCH,
+                    help="T*N images per step (multiple of 16); smaller values make an ncu-sized case")
     return ap.parse_args()
 
 
@@ -295,9 +299,10 @@ def main():
     from sparseflow_b200.Ops.sparse_conv2d import SparseConv2d
 
     hbm_peak, _, peak_kind = peaks()
-    n_img = T_STEPS * N_BATCH
+    n_img = args.images
+    n_batch = n_img // T_STEPS
     g = torch.Generator(device=dev).manual_seed(1000 + rank)
-    x = (torch.rand(T_STEPS, N_BATCH, C, H, W, device=dev, generator=g) < DENSITY).float()
+    x = (torch.rand(T_STEPS, n_batch, C, H, W, device=dev, generator=g) < DENSITY).float()
     conv = make_conv(C, C, 3, 1, 1, True, 1, device=dev)
     mod = SparseConv2d.from_dense(conv, block_size=16)
     mod.set_inference_mode(True)
@@ -313,6 +318,14 @@ def main():
     ms_step = ms_total / args.steps
     value = world * step_bytes * args.steps / (ms_total / 1e3) / 1e9
     achieved = step_bytes / (ms_step / 1e3) / 1e9
+    if args.only_timed:
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+                              "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+                              "images": n_img, "only_timed": True, "clocks": clocks}))
+        if dist is not None:
+            dist.destroy_process_group()
+        return
 
     # cuDNN dense on the same input (fp32, torch defaults: TF32 allowed for convs).
     x4 = x.reshape(n_img, C, H, W)
@@ -327,7 +340,7 @@ def main():
     # End to end through the module: pinned host spikes in, output back to host, every step.
     e2e_steps = max(2, min(args.steps, 5))
     x_host = x.cpu().pin_memory()
-    y_host = torch.empty((T_STEPS, N_BATCH, C, H, W), dtype=torch.float32).pin_memory()
+    y_host = torch.empty((T_STEPS, n_batch, C, H, W), dtype=torch.float32).pin_memory()
     x_dev = torch.empty_like(x)
 
     def e2e_step():
@@ -363,8 +376,8 @@ def main():
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded Bernoulli spikes, kaiming weights)",
-            "config": {"workload": "C5 cell: SparseConv2d 3x3/s1/p1 C64->64, T16 N64 56x56, Bernoulli(0.01) "
-                                   "fp32 spikes, block 16 (per GPU)", "global_batch": N_BATCH * world,
+            "config": {"workload": f"C5 cell: SparseConv2d 3x3/s1/p1 C64->64, T16 N{n_batch} 56x56, Bernoulli(0.01) "
+                                   "fp32 spikes, block 16 (per GPU)", "global_batch": n_batch * world,
                        "seq_len": T_STEPS, "parallelism": f"N-shard x{world}",
                        "l2": "inputs (822 MB) and outputs larger than L2; no flush"},
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": x.numel() * 4,
@@ -372,12 +385,15 @@ def main():
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
-                         else "fallback 6650 GB/s", "kernel": "sparse_conv_kernel<3,1,2,16,float,float,false>",
-                         "algorithmic_bytes_per_launch": step_bytes},
+                         else "fallback 6650 GB/s",
+                         "kernel": "one sf_sparse_conv2d call = spike_masks_kernel<float,4> + "
+                                   "sparse_conv_kernel<3,1,2,8,1,float,float,false,true>",
+                         "algorithmic_bytes_per_launch": step_bytes,
+                         "bytes_model": "x read once + y written once + weights + bias"},
             "speedup_vs_cudnn": {"cudnn_default_ms": round(cud_ms, 4), "cudnn_fp32_no_tf32_ms": round(cud32_ms, 4),
                                  "ours_ms": round(ms_step, 4), "vs_default": round(cud_ms / ms_step, 2),
                                  "vs_fp32": round(cud32_ms / ms_step, 2)},
-            "gpu_launches": args.steps,
+            "gpu_launches": 2 * args.steps,  # spike_masks_kernel + sparse_conv_kernel per step (+1 memset)
             "clocks": clocks,
             "cpu_baseline": cpu,
             "extra": extra,

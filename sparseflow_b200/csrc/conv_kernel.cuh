@@ -42,7 +42,12 @@
 namespace sf {
 namespace conv {
 
-constexpr int kNWarps = 32;
+#ifndef SF_CONV_NWARPS
+#define SF_CONV_NWARPS 32
+#endif
+// Warps per CTA (one CTA per SM): the last is the producer, the rest compute.
+// 24 and 16 warps (more registers per thread) measured slower.
+constexpr int kNWarps = SF_CONV_NWARPS;
 constexpr int kThreads = kNWarps * 32;
 constexpr int kComputeWarps = kNWarps - 1;
 #ifndef SF_CONV_ROWS_PER_WARP
