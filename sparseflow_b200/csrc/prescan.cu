@@ -1,4 +1,4 @@
-// Stage 1: receptive-field prescan (single pass over x, HBM-bound).
+// Stage 1: receptive-field prescan (HBM-bound).
 //
 // Semantics follow Kernels/_prescan_common.py:32-189 of the reference:
 //   group_max[n,ih,iw,g] = amax_{c in g} |half(x)|             (:32-45)
@@ -8,15 +8,25 @@
 //   ag_mask  = sum_g active_g << g ; class ZERO/SPARSE/DENSEISH (:48-109)
 // and Kernels/conv2d.py:113-123 (ids of non-ZERO tiles, ascending).
 //
-// B200 design: one CTA per (image, tile row). The CTA streams the tile row's
-// receptive-field rows of every channel once with 16-byte vector loads, folds
-// them into a per-input-pixel group bitmap in shared memory (plus a NaN bitmap:
-// a NaN anywhere in a pooling window makes the reference's max NaN and the
-// comparison false), then ORs each tile's receptive-field rectangle with one
-// warp per tile. Active tile ids are compacted in global order with a
-// decoupled look-back scan over CTAs that take logical indices from a ticket
-// counter, so no second launch and no host sync is needed.
+// B200 design, NCHW input with the full workspace (three launches, no
+// inter-CTA waits):
+//   group_bits_kernel   streams x once (eight 16-byte loads in flight per
+//                       thread) and writes per pixel {active groups, NaN
+//                       groups}: 8 bytes per pixel, 3 % of fp32 x for C=64;
+//   pool_tiles_kernel   per (image, run of tile rows): ORs every tile's
+//                       receptive-field window of those words (a NaN anywhere
+//                       in the window clears the group, as the reference's
+//                       max-pool of a NaN compares false);
+//   compact_ids_kernel  writes active ids in ascending order from per-row
+//                       counts, each block summing the counts before it.
+// NHWC input, or a workspace of only the look-back words (the static-workspace
+// entry point), uses one kernel: a CTA per (image, tile row) folds channels
+// for its receptive-field rows into shared memory, pools its tiles and
+// compacts ids with a decoupled look-back over CTAs that take logical indices
+// from a ticket counter.
 #include <cmath>
+#include <algorithm>
+#include <cstring>
 #include "common.cuh"
 
 namespace sf {
@@ -42,6 +52,8 @@ struct PrescanParams {
   uint32_t group_full;  // (1<<G)-1
   float thr;            // half(threshold) as float
   int max_rows_in;
+  const uint2* bits;    // two-pass path: per-pixel {active groups, NaN groups}, else nullptr
+  int32_t* row_count;   // two-pass path: non-ZERO tiles per tile row (for the compaction kernel)
 };
 
 template <typename T>
@@ -142,6 +154,63 @@ __device__ void fold_nhwc(const PrescanParams& p, int n, int ih_lo, int rows_in,
   }
 }
 
+// Two-pass path, pass 1 (NCHW): one streaming read of x. Each thread owns
+// VEC consecutive pixels of one image and walks all channels with eight
+// 16-byte loads in flight, writing per pixel {bit g: some channel of group g
+// is active, bit g: some channel of group g is NaN}. `cut` is the least float
+// f with |half(f)| > half(threshold), so `|v| >= cut` is the reference's
+// half-precision comparison (NaN compares false) without a conversion.
+template <typename T, int VEC>
+__global__ void __launch_bounds__(256) group_bits_kernel(const T* __restrict__ x, int C, int HW, int gs, float cut,
+                                                         uint2* __restrict__ bits) {
+  const int img = blockIdx.y;
+  const int pix0 = (blockIdx.x * 256 + threadIdx.x) * VEC;
+  if (pix0 >= HW) return;
+  uint32_t a[VEC], nn[VEC];
+#pragma unroll
+  for (int e = 0; e < VEC; ++e) a[e] = nn[e] = 0u;
+  const T* src = x + (size_t)img * C * HW + pix0;
+  // Group bit of channel c, advanced with a counter (no division per channel).
+  uint32_t bit = 1u;
+  int in_group = 0;
+  int c = 0;
+#pragma unroll 1
+  for (; c + 8 <= C; c += 8) {
+    Vec<VEC, T> r[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) r[u] = *reinterpret_cast<const Vec<VEC, T>*>(src + (size_t)(c + u) * HW);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) {
+        const float v = DT<T>::to_f(r[u].v[e]);
+        a[e] |= fabsf(v) >= cut ? bit : 0u;
+        nn[e] |= v != v ? bit : 0u;
+      }
+      if (++in_group == gs) {
+        in_group = 0;
+        bit <<= 1;
+      }
+    }
+  }
+  for (; c < C; ++c) {
+    const Vec<VEC, T> r = *reinterpret_cast<const Vec<VEC, T>*>(src + (size_t)c * HW);
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) {
+      const float v = DT<T>::to_f(r.v[e]);
+      a[e] |= fabsf(v) >= cut ? bit : 0u;
+      nn[e] |= v != v ? bit : 0u;
+    }
+    if (++in_group == gs) {
+      in_group = 0;
+      bit <<= 1;
+    }
+  }
+  uint2* dst = bits + (size_t)img * HW + pix0;
+#pragma unroll
+  for (int e = 0; e < VEC; ++e) dst[e] = make_uint2(a[e], nn[e]);
+}
+
 template <typename T, int VEC, bool NHWC>
 __global__ void __launch_bounds__(256) prescan2d_kernel(PrescanParams p) {
   extern __shared__ __align__(16) uint32_t smem[];
@@ -218,32 +287,40 @@ __global__ void __launch_bounds__(256) prescan2d_kernel(PrescanParams p) {
         const bool f = gw < p.GW && s_cls[gw] != SF_TILE_ZERO;
         local += __popc(__ballot_sync(0xffffffffu, f));
       }
-      // Decoupled look-back over logical blocks.
+      // Decoupled look-back over logical blocks, 32 predecessors per step:
+      // lane l inspects block j - l. Status words are {tag | flag << 32 |
+      // count}, flag 1 = this block's own count, 2 = inclusive prefix.
       const uint64_t tag = (uint64_t)((epoch + 1u) & 0x3fffffffu) << 34;
-      if (lane == 0) {
-        int excl = 0;
-        if (b == 0) {
-          st_release_u64(&p.status[0], tag | (2ull << 32) | (uint32_t)local);
-        } else {
-          st_release_u64(&p.status[b], tag | (1ull << 32) | (uint32_t)local);
-          int j = b - 1;
-          bool failed = false;
-          while (j >= 0) {
-            uint64_t w = 0;
-            uint32_t spins = 0;
-            while (true) {
-              w = ld_acquire_u64(&p.status[j]);
-              if ((w & ~((1ull << 34) - 1)) == tag && ((w >> 32) & 3ull) != 0ull) break;
-              if (++spins > kSpinLimit) { failed = true; break; }
-            }
-            if (failed) break;
-            excl += (int)(uint32_t)(w & 0xffffffffull);
-            if (((w >> 32) & 3ull) == 2ull) break;
-            --j;
+      if (lane == 0)
+        st_release_u64(&p.status[b], tag | ((b == 0 ? 2ull : 1ull) << 32) | (uint32_t)local);
+      int excl = 0;
+      bool failed = false;
+      for (int j = b - 1; j >= 0 && !failed; j -= 32) {
+        const int idx = j - lane;
+        uint64_t w = 0;
+        uint32_t flag = 2u;  // before block 0: an inclusive prefix of 0
+        uint32_t spins = 0;
+        while (true) {
+          if (idx >= 0) {
+            w = ld_acquire_u64(&p.status[idx]);
+            flag = ((w & ~((1ull << 34) - 1)) == tag) ? (uint32_t)((w >> 32) & 3ull) : 0u;
           }
-          if (failed) atomicExch(&p.ws->error, 1u);
-          st_release_u64(&p.status[b], tag | (2ull << 32) | (uint32_t)(excl + local));
+          if (__all_sync(0xffffffffu, flag != 0u)) break;
+          if (++spins > kSpinLimit) {
+            failed = true;
+            break;
+          }
         }
+        if (failed) break;
+        const uint32_t incl = __ballot_sync(0xffffffffu, flag == 2u);
+        const int stop = incl ? __ffs(incl) - 1 : 31;  // nearest inclusive predecessor
+        const uint32_t v = (lane <= stop && idx >= 0) ? (uint32_t)(w & 0xffffffffull) : 0u;
+        excl += (int)__reduce_add_sync(0xffffffffu, v);
+        if (incl) break;
+      }
+      if (lane == 0) {
+        if (failed) atomicExch(&p.ws->error, 1u);
+        if (b > 0) st_release_u64(&p.status[b], tag | (2ull << 32) | (uint32_t)(excl + local));
         s_excl = excl;
         if (b == p.N * p.GH - 1 && p.active_count != nullptr) *p.active_count = excl + local;
       }
@@ -272,6 +349,145 @@ __global__ void __launch_bounds__(256) prescan2d_kernel(PrescanParams p) {
   }
 }
 
+// Two-pass path, pass 2: one CTA per (image, run of tile rows). It stages
+// the run's receptive-field rows of group words in shared memory once (no
+// halo re-reads between tile rows), ORs every tile's window with one warp per
+// tile, and writes ag_mask, tile_class and each tile row's non-ZERO count.
+constexpr int kPoolThreads = 256;
+
+__global__ void __launch_bounds__(kPoolThreads) pool_tiles_kernel(PrescanParams p, int rows_per_cta) {
+  extern __shared__ __align__(16) uint32_t smem[];
+  __shared__ int s_cnt[64];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int chunks = (p.GH + rows_per_cta - 1) / rows_per_cta;
+  const int n = blockIdx.x / chunks;
+  const int gh0 = (blockIdx.x - n * chunks) * rows_per_cta;
+  const int gh1 = min(p.GH, gh0 + rows_per_cta);
+  const int oh0 = gh0 * p.BH;
+  const int oh1 = min(gh1 * p.BH, p.Ho);
+  const int ih_lo = max(0, oh0 * p.S - p.P);
+  const int ih_hi = min(p.H, (oh1 - 1) * p.S - p.P + p.K);
+  const int rows_in = max(0, ih_hi - ih_lo);
+  uint32_t* act = smem;
+  uint32_t* nanm = smem + p.max_rows_in * p.W;
+  const uint2* src = p.bits + ((size_t)n * p.H + ih_lo) * p.W;
+  const int total = rows_in * p.W;
+  for (int base = tid; base < total; base += 4 * kPoolThreads) {
+    uint2 v[4];  // four independent loads in flight per thread
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = base + u * kPoolThreads;
+      v[u] = i < total ? src[i] : make_uint2(0u, 0u);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = base + u * kPoolThreads;
+      if (i < total) {
+        act[i] = v[u].x;
+        nanm[i] = v[u].y;
+      }
+    }
+  }
+  if (tid < 64) s_cnt[tid] = 0;
+  __syncthreads();
+  const int ntiles = (gh1 - gh0) * p.GW;
+  for (int t = warp; t < ntiles; t += kPoolThreads / 32) {
+    const int ghl = t / p.GW;
+    const int gw = t - ghl * p.GW;
+    const int toh0 = (gh0 + ghl) * p.BH;
+    const int toh1 = min(toh0 + p.BH, p.Ho);
+    const int r_lo = max(0, toh0 * p.S - p.P) - ih_lo;
+    const int r_hi = min(p.H, (toh1 - 1) * p.S - p.P + p.K) - ih_lo;
+    const int ow0 = gw * p.BW;
+    const int ow1 = min(ow0 + p.BW, p.Wo);
+    const int iw_lo = max(0, ow0 * p.S - p.P);
+    const int iw_hi = min(p.W, (ow1 - 1) * p.S - p.P + p.K);
+    uint32_t a = 0, nn = 0;
+    for (int r = r_lo; r < r_hi; ++r)
+      for (int c = iw_lo + lane; c < iw_hi; c += 32) {
+        a |= act[r * p.W + c];
+        nn |= nanm[r * p.W + c];
+      }
+    a = __reduce_or_sync(0xffffffffu, a);
+    nn = __reduce_or_sync(0xffffffffu, nn);
+    if (lane == 0) {
+      const uint32_t m = a & ~nn & p.group_full;
+      const int cls = (m == 0u) ? SF_TILE_ZERO : ((m == p.group_full) ? SF_TILE_DENSEISH : SF_TILE_SPARSE);
+      const size_t tile = ((size_t)n * p.GH + gh0 + ghl) * p.GW + gw;
+      p.ag_mask[tile] = (int32_t)m;
+      p.tile_class[tile] = cls;
+      if (cls != SF_TILE_ZERO) atomicAdd(&s_cnt[ghl], 1);
+    }
+  }
+  __syncthreads();
+  if (p.row_count != nullptr && tid < gh1 - gh0) p.row_count[(size_t)n * p.GH + gh0 + tid] = s_cnt[tid];
+}
+
+// Two-pass path, compaction: block k owns tile rows [k*R, k*R + R) (R*GW <=
+// 1024 tiles). It sums the non-ZERO counts of all earlier tile rows, scans its
+// own tiles' classes, and writes their ids in ascending order; no block waits
+// on another.
+constexpr int kCompactThreads = 256;
+constexpr int kCompactTiles = 1024;
+
+__global__ void __launch_bounds__(kCompactThreads) compact_ids_kernel(const int32_t* __restrict__ tile_class,
+                                                                      const int32_t* __restrict__ row_count,
+                                                                      int nrows, int GW, int rows_per_block,
+                                                                      int32_t* __restrict__ active_ids,
+                                                                      int32_t* __restrict__ active_count) {
+  __shared__ int s_warp[kCompactThreads / 32];
+  __shared__ int s_base;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int row0 = blockIdx.x * rows_per_block;
+  const int row1 = min(nrows, row0 + rows_per_block);
+  // 1) Non-ZERO tiles before this block.
+  int before = 0;
+  for (int r = tid; r < row0; r += 8 * kCompactThreads) {
+    int v[8];  // eight independent loads in flight per thread
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v[u] = (r + u * kCompactThreads < row0) ? row_count[r + u * kCompactThreads] : 0;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) before += v[u];
+  }
+  before = __reduce_add_sync(0xffffffffu, before);
+  if (lane == 0) s_warp[warp] = before;
+  __syncthreads();
+  if (tid == 0) {
+    int t = 0;
+    for (int w = 0; w < kCompactThreads / 32; ++w) t += s_warp[w];
+    s_base = t;
+  }
+  __syncthreads();
+  // 2) Scan this block's tiles: thread tid owns tiles t0 .. t0+3.
+  constexpr int kPer = kCompactTiles / kCompactThreads;
+  const long long first = (long long)row0 * GW;
+  const long long last = (long long)row1 * GW;
+  const long long t0 = first + (long long)tid * kPer;
+  bool f[kPer];
+  int cnt = 0;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    f[i] = (t0 + i < last) && tile_class[t0 + i] != SF_TILE_ZERO;
+    cnt += f[i] ? 1 : 0;
+  }
+  int incl = cnt;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  __syncthreads();  // s_warp reuse
+  if (lane == 31) s_warp[warp] = incl;
+  __syncthreads();
+  int off = s_base;
+  for (int w = 0; w < warp; ++w) off += s_warp[w];
+  off += incl - cnt;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i)
+    if (f[i]) active_ids[off++] = (int32_t)(t0 + i);
+  if (blockIdx.x == gridDim.x - 1 && tid == kCompactThreads - 1) *active_count = off;
+}
+
 uint16_t half_bits_rne_from_double(double v) {
   // Exact double -> IEEE binary16 rounding (round to nearest, ties to even).
   __half h = __double2half(v);
@@ -291,6 +507,57 @@ float half_bits_to_float(uint16_t b) {
 }
 
 int rows_in_max(const sf_prescan_desc* d) { return (d->block_h - 1) * d->stride + d->kernel; }
+
+// Least non-negative float f with float(half_rn(f)) > thr (rounding to half
+// is monotonic, so |v| >= f <=> |half(v)| > thr); NaN when no float qualifies.
+float half_compare_cut(float thr) {
+  auto above = [thr](uint32_t bits) {
+    float f;
+    std::memcpy(&f, &bits, 4);
+    return __half2float(__float2half_rn(f)) > thr;
+  };
+  uint32_t lo = 0u, hi = 0x7f800000u;  // +0 .. +inf
+  if (!above(hi)) return NAN;
+  if (above(lo)) return 0.f;
+  while (hi - lo > 1u) {  // invariant: !above(lo), above(hi)
+    const uint32_t mid = lo + (hi - lo) / 2u;
+    if (above(mid))
+      hi = mid;
+    else
+      lo = mid;
+  }
+  float f;
+  std::memcpy(&f, &hi, 4);
+  return f;
+}
+
+// Offset and size of the per-pixel group words of the two-pass path.
+size_t status_region_bytes(const sf_prescan_desc* d) {
+  const size_t blocks = (size_t)d->n * ((d->h_out + d->block_h - 1) / d->block_h);
+  return ((16 + 8 * blocks + 255) / 256) * 256;
+}
+size_t tile_rows(const sf_prescan_desc* d) { return (size_t)d->n * ((d->h_out + d->block_h - 1) / d->block_h); }
+// Per-pixel group words, then one count per tile row.
+size_t bits_region_bytes(const sf_prescan_desc* d) {
+  return (((size_t)d->n * d->h * d->w * 8 + 255) / 256) * 256 + ((4 * tile_rows(d) + 255) / 256) * 256;
+}
+bool two_pass_ok(const sf_prescan_desc* d) {
+  return d->layout == SF_LAYOUT_NCHW && d->n <= 65535;
+}
+
+template <typename T>
+sf_status launch_bits(const void* x, const sf_prescan_desc* d, float cut, uint2* bits, cudaStream_t st) {
+  constexpr int V = 16 / sizeof(T);
+  const int HW = d->h * d->w;
+  if (aligned16(x) && HW % V == 0) {
+    const dim3 grid((HW + 256 * V - 1) / (256 * V), d->n);
+    group_bits_kernel<T, V><<<grid, 256, 0, st>>>(static_cast<const T*>(x), d->c, HW, d->group_size, cut, bits);
+  } else {
+    const dim3 grid((HW + 255) / 256, d->n);
+    group_bits_kernel<T, 1><<<grid, 256, 0, st>>>(static_cast<const T*>(x), d->c, HW, d->group_size, cut, bits);
+  }
+  return cudaGetLastError() == cudaSuccess ? SF_OK : SF_ERR_CUDA;
+}
 
 template <typename T>
 sf_status launch_t(const PrescanParams& p, int layout, int vec, size_t smem, cudaStream_t st) {
@@ -339,10 +606,16 @@ static sf_status validate_prescan(const sf_prescan_desc* d) {
   return SF_OK;
 }
 
-extern "C" size_t sf_prescan2d_workspace_size(const sf_prescan_desc* d) {
-  if (validate_prescan(d) != SF_OK) return 0;
+// Look-back words only: the one-pass kernel (and sf_prescan2d_static_ws).
+static size_t prescan_min_workspace(const sf_prescan_desc* d) {
   const size_t blocks = (size_t)d->n * ((d->h_out + d->block_h - 1) / d->block_h);
   return 16 + 8 * blocks;
+}
+
+extern "C" size_t sf_prescan2d_workspace_size(const sf_prescan_desc* d) {
+  if (validate_prescan(d) != SF_OK) return 0;
+  if (two_pass_ok(d)) return status_region_bytes(d) + bits_region_bytes(d);
+  return prescan_min_workspace(d);
 }
 
 extern "C" sf_status sf_prescan2d(const void* x, const sf_prescan_desc* d, int32_t* ag_mask,
@@ -352,7 +625,7 @@ extern "C" sf_status sf_prescan2d(const void* x, const sf_prescan_desc* d, int32
   if (s != SF_OK) return s;
   if (!x || !ag_mask || !tile_class) return SF_ERR_INVALID_ARG;
   if ((active_ids == nullptr) != (active_count == nullptr)) return SF_ERR_INVALID_ARG;
-  if (!workspace || workspace_bytes < sf_prescan2d_workspace_size(d)) return SF_ERR_WORKSPACE;
+  if (!workspace || workspace_bytes < prescan_min_workspace(d)) return SF_ERR_WORKSPACE;
   if ((reinterpret_cast<uintptr_t>(workspace) & 7u) != 0) return SF_ERR_ALIGNMENT;
 
   PrescanParams p;
@@ -372,6 +645,27 @@ extern "C" sf_status sf_prescan2d(const void* x, const sf_prescan_desc* d, int32
   p.group_full = (p.G == 32) ? 0xffffffffu : ((1u << p.G) - 1u);
   p.thr = half_bits_to_float(half_bits_rne_from_double(d->threshold));
   p.max_rows_in = rows_in_max(d);
+  p.bits = nullptr;
+  p.row_count = nullptr;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // With the full workspace (sf_prescan2d_workspace_size), NCHW inputs take
+  // two passes: a streaming channel fold, then tile pooling from its output.
+  // A workspace of only the look-back words selects the one-pass kernel.
+  if (two_pass_ok(d) && workspace_bytes >= status_region_bytes(d) + bits_region_bytes(d) &&
+      (reinterpret_cast<uintptr_t>(workspace) & 255u) == 0) {
+    uint2* bits = reinterpret_cast<uint2*>(static_cast<char*>(workspace) + status_region_bytes(d));
+    const float cut = half_compare_cut(p.thr);
+    sf_status s1 = SF_ERR_INVALID_ARG;
+    switch (d->dtype) {
+      case SF_DTYPE_F32: s1 = launch_bits<float>(x, d, cut, bits, st); break;
+      case SF_DTYPE_F16: s1 = launch_bits<__half>(x, d, cut, bits, st); break;
+      case SF_DTYPE_BF16: s1 = launch_bits<__nv_bfloat16>(x, d, cut, bits, st); break;
+    }
+    if (s1 != SF_OK) return s1;
+    p.bits = bits;
+    p.row_count = reinterpret_cast<int32_t*>(reinterpret_cast<char*>(bits) +
+                                             (((size_t)d->n * d->h * d->w * 8 + 255) / 256) * 256);
+  }
 
   const size_t esz = dtype_size(d->dtype);
   const int V = (int)(16 / esz);
@@ -381,7 +675,6 @@ extern "C" sf_status sf_prescan2d(const void* x, const sf_prescan_desc* d, int32
     if (d->layout == SF_LAYOUT_NHWC && d->c % V == 0) vec = V;
   }
   const size_t smem = 2ull * p.max_rows_in * p.W * 4ull;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   // Opt in to large dynamic shared memory once per instantiation.
   if (smem > 48 * 1024) {
     cudaError_t e = cudaSuccess;
@@ -394,12 +687,33 @@ extern "C" sf_status sf_prescan2d(const void* x, const sf_prescan_desc* d, int32
     if (d->dtype == SF_DTYPE_BF16) { SF_ATTR(__nv_bfloat16, 8, false) SF_ATTR(__nv_bfloat16, 1, false) SF_ATTR(__nv_bfloat16, 8, true) SF_ATTR(__nv_bfloat16, 1, true) }
 #undef SF_ATTR
   }
-  switch (d->dtype) {
-    case SF_DTYPE_F32: return launch_t<float>(p, d->layout, vec, smem, st);
-    case SF_DTYPE_F16: return launch_t<__half>(p, d->layout, vec, smem, st);
-    case SF_DTYPE_BF16: return launch_t<__nv_bfloat16>(p, d->layout, vec, smem, st);
+  if (p.bits != nullptr) {
+    // Tile rows per pooling CTA: as many as 48 KB of staged rows allow (<= 64).
+    int rpc = 1;
+    while (rpc < 64 && rpc < p.GH && 2ull * ((size_t)((rpc + 1) * p.BH - 1) * p.S + p.K) * p.W * 4 <= 48 * 1024)
+      ++rpc;
+    p.max_rows_in = std::min(p.H, (rpc * p.BH - 1) * p.S + p.K);
+    const size_t psmem = 2ull * p.max_rows_in * p.W * 4;
+    const int chunks = (p.GH + rpc - 1) / rpc;
+    if (psmem > 48 * 1024 &&
+        cudaFuncSetAttribute(pool_tiles_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)psmem) != cudaSuccess)
+      return SF_ERR_CUDA;
+    pool_tiles_kernel<<<p.N * chunks, kPoolThreads, psmem, st>>>(p, rpc);
+    if (cudaGetLastError() != cudaSuccess) return SF_ERR_CUDA;
+    if (active_ids == nullptr) return SF_OK;
+    const int nrows = p.N * p.GH;
+    const int rows_per_block = std::max(1, kCompactTiles / p.GW);
+    compact_ids_kernel<<<(nrows + rows_per_block - 1) / rows_per_block, kCompactThreads, 0, st>>>(
+        tile_class, p.row_count, nrows, p.GW, rows_per_block, active_ids, active_count);
+    return cudaGetLastError() == cudaSuccess ? SF_OK : SF_ERR_CUDA;
   }
-  return SF_ERR_INVALID_ARG;
+  sf_status s2 = SF_ERR_INVALID_ARG;
+  switch (d->dtype) {
+    case SF_DTYPE_F32: s2 = launch_t<float>(p, d->layout, vec, smem, st); break;
+    case SF_DTYPE_F16: s2 = launch_t<__half>(p, d->layout, vec, smem, st); break;
+    case SF_DTYPE_BF16: s2 = launch_t<__nv_bfloat16>(p, d->layout, vec, smem, st); break;
+  }
+  return s2;
 }
 
 extern "C" sf_status sf_prescan2d_status(void* workspace, void* stream) {
@@ -454,8 +768,9 @@ sf_status static_ws_for_current_device(void** out) {
 extern "C" sf_status sf_prescan2d_static_ws(const void* x, const sf_prescan_desc* d, int32_t* ag_mask,
                                             int32_t* tile_class, int32_t* active_ids, int32_t* active_count,
                                             void* stream) {
-  const size_t need = sf_prescan2d_workspace_size(d);
-  if (need == 0) return validate_prescan(d) != SF_OK ? validate_prescan(d) : SF_ERR_INVALID_ARG;
+  const sf_status v = validate_prescan(d);
+  if (v != SF_OK) return v;
+  const size_t need = prescan_min_workspace(d);
   if (need > kStaticWsBytes) return SF_ERR_WORKSPACE;  // more than SF_PRESCAN_STATIC_MAX_ROWS tile rows
   void* ws = nullptr;
   sf_status s = static_ws_for_current_device(&ws);

@@ -104,3 +104,51 @@ def test_prescan_full_size_properties():
     for img in (0, 777):
         oag, _, _ = oracle.prescan2d(x[img:img + 1].cpu().numpy(), 0, 56, 56, 3, 1, 1, 8, 16, 16, 1e-6)
         np.testing.assert_array_equal(ag[img * 28:(img + 1) * 28], oag)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("n,c,h,w,k,s,p,bh,bw,gs", [
+    (3, 40, 30, 26, 3, 1, 1, 8, 8, 16),      # ragged channels, width not a multiple of the vector
+    (2, 64, 56, 56, 3, 2, 1, 8, 16, 16),     # stride 2
+    (4, 256, 14, 14, 1, 1, 0, 8, 8, 16),     # 1x1, 16 groups
+])
+def test_prescan_one_pass_and_two_pass_agree(dtype, n, c, h, w, k, s, p, bh, bw, gs):
+    """The full workspace selects the two-pass path (streaming channel fold, then tile
+    pooling); a workspace of only the look-back words selects the one-pass kernel.
+    Both must give identical metadata, including at the half-precision threshold
+    boundary and with NaNs."""
+    import ctypes
+    from sparseflow_b200 import _lib
+    g = torch.Generator().manual_seed(n * 1000 + c)
+    x = torch.zeros(n, c, h, w)
+    m = torch.rand(n, c, h, w, generator=g)
+    edge = torch.tensor([1e-6, 1.0133e-6, 1.0133e-6 * (1 + 2 ** -11), 1.02e-6, 5.96e-8, -2e-6, 0.5, 1.0])
+    pick = torch.randint(0, len(edge), (n, c, h, w), generator=g)
+    x = torch.where(m < 0.02, edge[pick], x)
+    x[0, 0, 0, 0] = float("nan")
+    x[-1, c - 1, h // 2, w // 3] = float("nan")
+    xd = x.to(dtype).cuda()
+    ho, wo = (h + 2 * p - k) // s + 1, (w + 2 * p - k) // s + 1
+    d = _lib.prescan_desc(n, c, h, w, ho, wo, k, s, p, bh, bw, gs, 1e-6, dtype, 0)
+    lib = _lib.load()
+    nt = n * (-(-ho // bh)) * (-(-wo // bw))
+    full = lib.sf_prescan2d_workspace_size(ctypes.byref(d))
+    minimal = 16 + 8 * n * (-(-ho // bh))
+    assert full > minimal
+    outs = []
+    for nbytes in (full, minimal):
+        ws = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+        ag = torch.empty(nt, dtype=torch.int32, device="cuda")
+        tc = torch.empty_like(ag)
+        ids = torch.full_like(ag, -1)
+        cnt = torch.zeros(1, dtype=torch.int32, device="cuda")
+        _lib.prescan2d(xd, d, ag, tc, ids, cnt, ws)
+        torch.cuda.synchronize()
+        assert _lib.prescan_status(ws) == 0
+        cn = int(cnt.item())
+        outs.append((ag.cpu().numpy(), tc.cpu().numpy(), ids[:cn].cpu().numpy()))
+    for a, b in zip(outs[0], outs[1]):
+        np.testing.assert_array_equal(a, b)
+    oag, otc, oids = oracle.prescan2d(xd.float().cpu().numpy(), 0, ho, wo, k, s, p, bh, bw, gs, 1e-6)
+    np.testing.assert_array_equal(outs[0][0], oag)
+    np.testing.assert_array_equal(outs[0][2], oids)

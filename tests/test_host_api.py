@@ -149,7 +149,11 @@ def test_native_argument_checks_without_gpu():
     from sparseflow_b200 import _lib
     lib = _lib.load()
     d = _lib.prescan_desc(2, 64, 32, 32, 32, 32, 3, 1, 1, 8, 8, 16, 1e-6, torch.float32, 0)
-    assert lib.sf_prescan2d_workspace_size(ctypes.byref(d)) == 16 + 8 * 2 * 4
+    # NCHW: look-back words, 8 bytes of group words per input pixel and one
+    # count per tile row, each region rounded to 256 bytes.
+    assert lib.sf_prescan2d_workspace_size(ctypes.byref(d)) == 256 + 2 * 32 * 32 * 8 + 256
+    d_nhwc = _lib.prescan_desc(2, 64, 32, 32, 32, 32, 3, 1, 1, 8, 8, 16, 1e-6, torch.float32, 1)
+    assert lib.sf_prescan2d_workspace_size(ctypes.byref(d_nhwc)) == 16 + 8 * 2 * 4
     bad = _lib.prescan_desc(2, 64, 32, 32, 31, 32, 3, 1, 1, 8, 8, 16, 1e-6, torch.float32, 0)
     assert lib.sf_prescan2d_workspace_size(ctypes.byref(bad)) == 0
     assert lib.sf_prescan2d(None, ctypes.byref(d), None, None, None, None, None, 0, None) == _lib.SF_ERR_INVALID_ARG
