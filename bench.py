@@ -277,7 +277,46 @@ def extras(dev, hbm_peak, steps):
     b3 = 4 * x3.numel() * 2 + 4 * 64 * 128 * 28 * 28 * 2 + 4 * 128 * 128 * 9
     out["c3_fused_conv_bn_lif"] = {"GBps": round(b3 / ms / 1e6, 1), "frac_of_measured_hbm": round(b3 / ms / 1e6 / hbm_peak, 3),
                                    "ms": round(ms, 4)}
+    del x3
+    out["c4_spiking_resnet50"] = c4_resnet(dev)
     return out
+
+
+def c4_resnet(dev, iters=3):
+    """C4: Spiking-ResNet50 inference, T16 N128 3x32x32 N(0,1) direct-encoded, random init;
+    the same model timed dense and after sparseflow_b200.optimize (img/s = N / s per forward)."""
+    import copy
+    import sparseflow_b200
+    from sparseflow_b200.snn import spiking_resnet50
+    from sparseflow_b200.Ops.lif_node import reset_net
+    from sparseflow_b200.Ops.sparse_conv2d import SparseConv2d
+    torch.manual_seed(5)
+    T, N = 16, 128
+    dense = spiking_resnet50().to(dev).eval()
+    img = torch.randn(N, 3, 32, 32, generator=torch.Generator().manual_seed(6)).to(dev)
+    x = img.unsqueeze(0).repeat(T, 1, 1, 1, 1)
+    sparse = copy.deepcopy(dense)
+    sparseflow_b200.optimize(sparse, sample_input=x[:, :2], verbose=False)
+    n_sparse = sum(isinstance(m, SparseConv2d) for m in sparse.modules())
+
+    def run(model):
+        reset_net(model)
+        return model(x)
+    res = {}
+    with torch.no_grad():
+        for name, model in (("dense", dense), ("sparse", sparse)):
+            ms = cuda_time(lambda: run(model), iters, 2) / iters
+            res[name] = ms
+        reset_net(dense)
+        reset_net(sparse)
+        ref = dense(x)
+        reset_net(sparse)
+        got = sparse(x)
+        err = float((got - ref).abs().max() / ref.abs().max().clamp_min(1e-12))
+    return {"img_per_s_sparse": round(N / (res["sparse"] / 1e3), 1), "img_per_s_dense": round(N / (res["dense"] / 1e3), 1),
+            "ms_sparse": round(res["sparse"], 2), "ms_dense": round(res["dense"], 2), "sparse_layers": n_sparse,
+            "logits_rel_err_vs_dense": err,
+            "note": "same random-init model and input; LIF nodes are torch elementwise ops in both"}
 
 
 def main():
