@@ -28,7 +28,7 @@ from ._prescan_common import prescan2d
 
 FALLBACK_RATIO = SPARSE_DENSE_RATIO_THRESHOLD
 
-SUPPORTED_PATTERNS = ((1, 1, 0), (3, 1, 1), (3, 2, 1))
+SUPPORTED_PATTERNS = ((1, 1, 0), (1, 2, 0), (3, 1, 1), (3, 2, 1))
 
 
 def _select_tile_sizes(h: int, w: int):

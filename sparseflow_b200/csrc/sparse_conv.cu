@@ -8,6 +8,10 @@
 #include "events.cuh"
 
 namespace sf {
+namespace pw {
+sf_status run_pointwise(const void* x, const void* w_packed, const float* bias, void* y, int N, int C, int H,
+                        int W, int Co, int Ho, int Wo, int S, int xdt, int wdt, cudaStream_t st);
+}  // namespace pw
 namespace conv {
 namespace {
 
@@ -172,7 +176,8 @@ sf_status encode_y_map(CUtensorMap* m, void* y, int xdt, int Wo, int Ho, int Co,
 sf_status check_geometry(int T, int N, int C, int H, int W, int Co, int Ho, int Wo, int K, int S, int P, int xdt,
                          int wdt) {
   if (T <= 0 || N <= 0 || C <= 0 || H <= 0 || W <= 0 || Co <= 0 || Ho <= 0 || Wo <= 0) return SF_ERR_INVALID_ARG;
-  if (!((K == 1 && S == 1 && P == 0) || (K == 3 && S == 1 && P == 1) || (K == 3 && S == 2 && P == 1)))
+  if (!((K == 1 && S == 1 && P == 0) || (K == 1 && S == 2 && P == 0) || (K == 3 && S == 1 && P == 1) ||
+        (K == 3 && S == 2 && P == 1)))
     return SF_ERR_UNSUPPORTED;
   if ((H + 2 * P - K) / S + 1 != Ho || (W + 2 * P - K) / S + 1 != Wo) return SF_ERR_INVALID_ARG;
   if (dtype_size(xdt) == 0 || (wdt != SF_DTYPE_F32 && wdt != SF_DTYPE_BF16)) return SF_ERR_INVALID_ARG;
@@ -189,6 +194,15 @@ sf_status run_conv(const void* x, const void* w_packed, const float* bias, void*
   if (!x || !w_packed || !y) return SF_ERR_INVALID_ARG;
   if (!workspace) return SF_ERR_WORKSPACE;
   if (!aligned16(w_packed)) return SF_ERR_ALIGNMENT;
+  // 1x1 stride 2: one pass over x with masks built in shared memory
+  // (pointwise.cu). For stride 1 that kernel measured slower than the two
+  // stages (0.74 vs 0.54 ms on the C2 cell; both issue-bound), so it runs
+  // only when SF_CONV_PW=1 asks for it.
+  if (!lif && K == 1 && (S == 2 || env_int("SF_CONV_PW") == 1)) {
+    s = pw::run_pointwise(x, w_packed, bias, y, T * N, C, H, W, Co, Ho, Wo, S, xdt, wdt, st);
+    if (s != SF_ERR_UNSUPPORTED) return s;
+  }
+  if (K == 1 && S != 1) return SF_ERR_UNSUPPORTED;
   const int nw = (C + 63) / 64;
   Plan pl;
   const bool y_tma_ok = aligned16(y) && tensor_map_encoder() != nullptr;

@@ -54,6 +54,14 @@ GRID = [
     (1, 64, 20, 250, 32, 3, 1, 1, 0.01),
     (3, 512, 7, 7, 512, 1, 1, 0, 0.01),
     (2, 48, 12, 12, 256, 3, 1, 1, 0.0),
+    # 1x1 (one-pass pointwise kernel): H*W not a multiple of 4, real values, ragged C and C_out,
+    # stride 2 (the downsample), more channels than one mask word row holds
+    (2, 40, 13, 30, 24, 1, 1, 0, 0.1),
+    (3, 3, 17, 9, 8, 1, 1, 0, 1.0),
+    (2, 64, 15, 15, 96, 1, 2, 0, 0.1),
+    (2, 256, 28, 28, 512, 1, 2, 0, 0.02),
+    (1, 1000, 7, 7, 40, 1, 1, 0, 0.05),
+    (2, 64, 56, 56, 256, 1, 1, 0, 1.0),
 ]
 
 
@@ -148,3 +156,20 @@ def test_conv_metadata_buffers_match_prescan():
     np.testing.assert_array_equal(agb.cpu().numpy(), oag)
     assert stats["zero_tiles"] == int((otc == 0).sum())
     assert ms > 0 and meta["backend"] == "sparse_b200"
+
+
+@pytest.mark.parametrize("s", [1, 2])
+def test_conv1x1_one_pass_matches_two_stage(monkeypatch, s):
+    """The one-pass 1x1 kernel and the two-stage (mask pass + gather) path give the same result."""
+    from sparseflow_b200.Kernels.conv2d import sparse_conv2d_forward
+    g = torch.Generator().manual_seed(21)
+    x = (torch.rand(4, 128, 28, 28, generator=g) < 0.03).float().cuda()
+    wt = (torch.randn(64, 128, 1, 1, generator=g) * 0.1).cuda()
+    y1, _ = sparse_conv2d_forward(x, wt, None, kernel_size=1, stride=1, padding=0)
+    monkeypatch.setenv("SF_CONV_PW", "1")
+    y2, _ = sparse_conv2d_forward(x, wt, None, kernel_size=1, stride=1, padding=0)
+    torch.testing.assert_close(y1, y2, rtol=1e-6, atol=1e-6)
+    if s == 2:
+        monkeypatch.delenv("SF_CONV_PW")
+        y3, _ = sparse_conv2d_forward(x, wt, None, kernel_size=1, stride=2, padding=0)
+        torch.testing.assert_close(y3, y1[:, :, ::2, ::2], rtol=1e-6, atol=1e-6)
