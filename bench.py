@@ -316,7 +316,7 @@ def c4_resnet(dev, iters=3):
     return {"img_per_s_sparse": round(N / (res["sparse"] / 1e3), 1), "img_per_s_dense": round(N / (res["dense"] / 1e3), 1),
             "ms_sparse": round(res["sparse"], 2), "ms_dense": round(res["dense"], 2), "sparse_layers": n_sparse,
             "logits_rel_err_vs_dense": err,
-            "note": "same random-init model and input; LIF nodes are torch elementwise ops in both"}
+            "note": "same random-init model and input; every LIF node is one sf_lif_multistep launch in both"}
 
 
 def main():

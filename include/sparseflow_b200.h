@@ -175,6 +175,28 @@ sf_status sf_fused_conv_lif(const void* x, const void* w_packed, const float* bi
                             const sf_lif_desc* d,
                             void* workspace, size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------------------------------ */
+/* Multi-step LIF neuron (the separate LIFNode after a BN, not fused into a  */
+/* convolution): the update of Ops/sparse_fused_conv_lif.py:271-293 applied  */
+/* over the leading time axis, v kept in registers across all steps.         */
+/* ------------------------------------------------------------------------ */
+typedef struct sf_lif_ms_desc {
+  int64_t numel;                    /* elements per time step (N*C*H*W) */
+  int32_t t_steps;
+  float tau, v_threshold, v_reset;  /* v_reset is used as 0 when hard_reset == 0 */
+  int32_t hard_reset;               /* 1: v = v_reset on spike; 0: v -= v_threshold */
+  int32_t decay_input;              /* 1: v += (x - (v - v_reset)) / tau; 0: v += x - (v - v_reset) / tau */
+  int32_t x_dtype;                  /* dtype of x */
+  int32_t s_dtype;                  /* dtype of spikes_out (values 0 / 1) */
+} sf_lif_ms_desc;
+
+/* x: [t_steps, numel]; v_inout: fp32 [numel], read as the state before step 0
+ * and overwritten with the state after the last step; spikes_out:
+ * [t_steps, numel]. Every pointer device memory, 16-byte alignment enables
+ * vector access. No workspace. */
+sf_status sf_lif_multistep(const void* x, float* v_inout, void* spikes_out, const sf_lif_ms_desc* d,
+                           void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -5,8 +5,9 @@ installed here, so models built for benchmarks and tests use this module: the
 same charge / fire / reset rule as spikingjelly's ``LIFNode`` with
 ``decay_input=True`` and the rule restated in Ops/sparse_fused_conv_lif.py:283-292
 of the reference, applied over the leading time axis of a [T, N, ...] input
-(``step_mode='m'``). It is plain tensor code: it is not part of the sparse
-convolution path, which consumes its output spikes.
+(``step_mode='m'``). On CUDA a multi-step call is one ``sf_lif_multistep``
+launch (v kept in registers across the steps); on CPU the same formula runs
+as tensor code.
 """
 from __future__ import annotations
 
@@ -51,7 +52,22 @@ class LIFNode(nn.Module):
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if self.step_mode == "s":
             return self._step(x)
+        if x.is_cuda:
+            return self._multistep_cuda(x)
         return torch.stack([self._step(x[t]) for t in range(x.shape[0])], 0)
+
+    def _multistep_cuda(self, x: torch.Tensor) -> torch.Tensor:
+        """All T steps in one sf_lif_multistep launch (v kept in registers across steps)."""
+        from .. import _lib
+        vr = 0.0 if self.v_reset is None else float(self.v_reset)
+        x = x.contiguous()
+        if self.v is None or self.v.shape != x.shape[1:] or self.v.device != x.device:
+            self.v = torch.full(x.shape[1:], vr, dtype=torch.float32, device=x.device)
+        else:
+            self.v = self.v.float().contiguous()
+        spikes = torch.empty_like(x)
+        _lib.lif_multistep(x, self.v, spikes, self.tau, self.v_threshold, self.v_reset, self.decay_input)
+        return spikes
 
     def extra_repr(self):
         return f"tau={self.tau}, v_threshold={self.v_threshold}, v_reset={self.v_reset}, step_mode={self.step_mode}"

@@ -75,6 +75,15 @@ class LifDesc(ctypes.Structure):
     ]
 
 
+class LifMsDesc(ctypes.Structure):
+    _fields_ = [
+        ("numel", ctypes.c_int64), ("t_steps", ctypes.c_int32),
+        ("tau", ctypes.c_float), ("v_threshold", ctypes.c_float), ("v_reset", ctypes.c_float),
+        ("hard_reset", ctypes.c_int32), ("decay_input", ctypes.c_int32),
+        ("x_dtype", ctypes.c_int32), ("s_dtype", ctypes.c_int32),
+    ]
+
+
 # Every symbol declared in include/sparseflow_b200.h, with its ctypes signature.
 _VP = ctypes.c_void_p
 _SIGNATURES = {
@@ -94,6 +103,7 @@ _SIGNATURES = {
     "sf_fused_conv_lif_workspace_size": (ctypes.c_size_t, [ctypes.POINTER(LifDesc)]),
     "sf_fused_conv_lif": (ctypes.c_int32, [_VP, _VP, _VP, _VP, _VP, ctypes.POINTER(LifDesc), _VP, ctypes.c_size_t,
                                            _VP]),
+    "sf_lif_multistep": (ctypes.c_int32, [_VP, _VP, _VP, ctypes.POINTER(LifMsDesc), _VP]),
 }
 
 _lib = None
@@ -257,3 +267,19 @@ def fused_conv_lif(x5: torch.Tensor, w_packed: torch.Tensor, bias: Optional[torc
     st = lib.sf_fused_conv_lif(_ptr(x5), _ptr(w_packed), _ptr(bias), _ptr(v), _ptr(spikes), ctypes.byref(desc),
                                _ptr(ws), ws.numel(), _stream(x5.device))
     _check("sf_fused_conv_lif", st)
+
+
+def lif_multistep(x: torch.Tensor, v: torch.Tensor, spikes: torch.Tensor, tau: float, v_threshold: float,
+                  v_reset: Optional[float], decay_input: bool) -> None:
+    """x, spikes: [T, ...] contiguous; v: fp32 [...] contiguous, updated in place."""
+    _require_cuda(x, v, spikes)
+    if v.dtype != torch.float32 or not (x.is_contiguous() and v.is_contiguous() and spikes.is_contiguous()):
+        raise ValueError("lif_multistep needs contiguous tensors and an fp32 membrane")
+    t = x.shape[0]
+    numel = x[0].numel() if t > 0 else v.numel()
+    if v.numel() != numel or spikes.shape != x.shape:
+        raise ValueError("shape mismatch between x, v and spikes")
+    desc = LifMsDesc(numel, t, float(tau), float(v_threshold), 0.0 if v_reset is None else float(v_reset),
+                     int(v_reset is not None), int(bool(decay_input)), sf_dtype(x.dtype), sf_dtype(spikes.dtype))
+    st = load().sf_lif_multistep(_ptr(x), _ptr(v), _ptr(spikes), ctypes.byref(desc), _stream(x.device))
+    _check("sf_lif_multistep", st)
