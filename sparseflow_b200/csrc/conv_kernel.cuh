@@ -502,7 +502,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #ifdef SF_CONV_EXPERIMENT_NO_GATHER
         if (false) {
 #else
-        if (active) {
+        // Warp-uniform skip of the unrolled position tests when no input
+        // pixel of this tile has an event in this channel word.
+        uint32_t nz_any = 0u;
+#pragma unroll
+        for (int rd = 0; rd < ROUNDS; ++rd) nz_any |= nzpos[rd];
+        if (active && nz_any != 0u) {
 #endif
           if (binary)
             gather(std::true_type{});

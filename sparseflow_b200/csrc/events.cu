@@ -22,59 +22,67 @@ struct alignas(sizeof(T) * VEC) EVec {
   T v[VEC];
 };
 
+// Thread g of channel word blockIdx.y owns VEC consecutive pixels of image
+// g / (HW / VEC): images are flattened into one index space so small feature
+// maps (8x8) still fill whole CTAs.
 template <typename XT, int VEC>
 __global__ void __launch_bounds__(kEvThreads) spike_masks_kernel(const XT* __restrict__ x, int C, int HW, int nw,
+                                                                 long long nimg,
                                                                  unsigned long long* __restrict__ masks,
                                                                  uint32_t* __restrict__ flags) {
-  const int img = blockIdx.z;
   const int word = blockIdx.y;
-  const int pix0 = (blockIdx.x * kEvThreads + threadIdx.x) * VEC;
+  const int vpi = HW / VEC;  // vectors per image
+  const long long gid = (long long)blockIdx.x * kEvThreads + threadIdx.x;
+  if (gid >= nimg * vpi) return;
+  const long long img = gid / vpi;
+  const int pix0 = (int)(gid - img * vpi) * VEC;
   const int c0 = word * 64;
   const int cn = min(64, C - c0);
   uint32_t lo[VEC], hi[VEC];
   uint32_t bad = 0u;
 #pragma unroll
   for (int e = 0; e < VEC; ++e) lo[e] = hi[e] = 0u;
-  if (pix0 < HW) {
-    const XT* src = x + ((size_t)img * C + c0) * HW + pix0;
-    int c = 0;
-    // Eight channels per step keep eight 16-byte loads in flight per thread.
+  const XT* src = x + ((size_t)img * C + c0) * HW + pix0;
+  int c = 0;
+  // Eight channels per step keep eight 16-byte loads in flight per thread.
 #pragma unroll 1
-    for (; c + 8 <= cn; c += 8) {
-      EVec<XT, VEC> r[8];
+  for (; c + 8 <= cn; c += 8) {
+    EVec<XT, VEC> r[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) r[u] = *reinterpret_cast<const EVec<XT, VEC>*>(src + (size_t)(c + u) * HW);
+    for (int u = 0; u < 8; ++u) r[u] = *reinterpret_cast<const EVec<XT, VEC>*>(src + (size_t)(c + u) * HW);
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int cc = c + u;
-#pragma unroll
-        for (int e = 0; e < VEC; ++e) {
-          const uint32_t nz = DT<XT>::nz_bit(r[u].v[e]);
-          bad |= nz & DT<XT>::not_one(r[u].v[e]);
-          if (cc < 32)
-            lo[e] |= nz << cc;
-          else
-            hi[e] |= nz << (cc - 32);
-        }
-      }
-    }
-    for (; c < cn; ++c) {
-      const EVec<XT, VEC> r = *reinterpret_cast<const EVec<XT, VEC>*>(src + (size_t)c * HW);
+    for (int u = 0; u < 8; ++u) {
+      const int cc = c + u;
 #pragma unroll
       for (int e = 0; e < VEC; ++e) {
-        const uint32_t nz = DT<XT>::nz_bit(r.v[e]);
-        bad |= nz & DT<XT>::not_one(r.v[e]);
-        if (c < 32)
-          lo[e] |= nz << c;
+        const uint32_t nz = DT<XT>::nz_bit(r[u].v[e]);
+        bad |= nz & DT<XT>::not_one(r[u].v[e]);
+        if (cc < 32)
+          lo[e] |= nz << cc;
         else
-          hi[e] |= nz << (c - 32);
+          hi[e] |= nz << (cc - 32);
       }
     }
-    unsigned long long* dst = masks + ((size_t)img * HW + pix0) * nw + word;
-#pragma unroll
-    for (int e = 0; e < VEC; ++e) dst[(size_t)e * nw] = ((unsigned long long)hi[e] << 32) | lo[e];
   }
-  if (__syncthreads_or(bad != 0u) && threadIdx.x == 0) atomicOr(&flags[img], 1u);
+  for (; c < cn; ++c) {
+    const EVec<XT, VEC> r = *reinterpret_cast<const EVec<XT, VEC>*>(src + (size_t)c * HW);
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) {
+      const uint32_t nz = DT<XT>::nz_bit(r.v[e]);
+      bad |= nz & DT<XT>::not_one(r.v[e]);
+      if (c < 32)
+        lo[e] |= nz << c;
+      else
+        hi[e] |= nz << (c - 32);
+    }
+  }
+  unsigned long long* dst = masks + ((size_t)img * HW + pix0) * nw + word;
+#pragma unroll
+  for (int e = 0; e < VEC; ++e) dst[(size_t)e * nw] = ((unsigned long long)hi[e] << 32) | lo[e];
+  // One atomic per image present in the warp that saw a value other than 0/1.
+  const unsigned same = __match_any_sync(__activemask(), img);
+  const unsigned any_bad = __ballot_sync(__activemask(), bad != 0u) & same;
+  if (any_bad != 0u && (threadIdx.x & 31) == __ffs(same) - 1) atomicOr(&flags[img], 1u);
 }
 
 template <typename XT>
@@ -83,13 +91,15 @@ sf_status launch(const void* x, int nimg, int C, int HW, unsigned long long* mas
   const int nw = (C + 63) / 64;
   constexpr int V = 16 / (int)sizeof(XT);
   const bool vec = aligned16(x) && HW % V == 0;
-  const int per_block = kEvThreads * (vec ? V : 1);
-  const dim3 grid((HW + per_block - 1) / per_block, nw, nimg);
-  if (grid.z > 65535u || grid.y > 65535u) return SF_ERR_UNSUPPORTED;
+  const long long threads = (long long)nimg * (HW / (vec ? V : 1));
+  const dim3 grid((unsigned)((threads + kEvThreads - 1) / kEvThreads), nw, 1);
+  if (grid.y > 65535u || (threads + kEvThreads - 1) / kEvThreads > 0x7fffffffll) return SF_ERR_UNSUPPORTED;
   if (vec)
-    spike_masks_kernel<XT, V><<<grid, kEvThreads, 0, st>>>(static_cast<const XT*>(x), C, HW, nw, masks, flags);
+    spike_masks_kernel<XT, V><<<grid, kEvThreads, 0, st>>>(static_cast<const XT*>(x), C, HW, nw, nimg, masks,
+                                                            flags);
   else
-    spike_masks_kernel<XT, 1><<<grid, kEvThreads, 0, st>>>(static_cast<const XT*>(x), C, HW, nw, masks, flags);
+    spike_masks_kernel<XT, 1><<<grid, kEvThreads, 0, st>>>(static_cast<const XT*>(x), C, HW, nw, nimg, masks,
+                                                            flags);
   return cudaGetLastError() == cudaSuccess ? SF_OK : SF_ERR_CUDA;
 }
 
