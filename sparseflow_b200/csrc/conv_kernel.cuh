@@ -184,6 +184,31 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// Packed fp32 pair arithmetic (sm_100 add/fma .f32x2): each half is rounded
+// exactly like a scalar add.rn.f32 / fma.rn.f32, one instruction for two.
+__device__ __forceinline__ void add_f32x2(float& a0, float& a1, float b0, float b1) {
+#ifdef SF_CONV_NO_F32X2
+  a0 += b0;
+  a1 += b1;
+#else
+  asm("{\n\t.reg .b64 ra, rb;\n\tmov.b64 ra, {%0, %1};\n\tmov.b64 rb, {%2, %3};\n\t"
+      "add.rn.f32x2 ra, ra, rb;\n\tmov.b64 {%0, %1}, ra;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(b0), "f"(b1));
+#endif
+}
+__device__ __forceinline__ void fma_f32x2(float& a0, float& a1, float x, float b0, float b1) {
+#ifdef SF_CONV_NO_F32X2
+  a0 = fmaf(x, b0, a0);
+  a1 = fmaf(x, b1, a1);
+#else
+  asm("{\n\t.reg .b64 ra, rb, rx;\n\tmov.b64 ra, {%0, %1};\n\tmov.b64 rb, {%2, %3};\n\t"
+      "mov.b64 rx, {%4, %4};\n\tfma.rn.f32x2 ra, rx, rb, ra;\n\tmov.b64 {%0, %1}, ra;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(b0), "f"(b1), "f"(x));
+#endif
+}
+
 __device__ __forceinline__ unsigned long long shfl64(unsigned long long v, int src) {
   const uint32_t lo = __shfl_sync(0xffffffffu, (uint32_t)v, src);
   const uint32_t hi = __shfl_sync(0xffffffffu, (uint32_t)(v >> 32), src);
@@ -484,12 +509,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                       if (d >= 0 && d % S == 0 && d / S < R) {
                         float w[CPL];
                         WVec<WT, CPL, WSMEM>::ld(wc + (kh * K + kw) * 32 * CPL, w);
+                        float(&a)[CPL] = acc[(rb / S) * R + d / S];
+                        // Pairs for fp32 weights (a float2 load feeds add.f32x2 directly);
+                        // bf16 weights measured faster with scalar adds.
+                        if constexpr (CPL % 2 == 0 && std::is_same<WT, float>::value) {
 #pragma unroll
-                        for (int j = 0; j < CPL; ++j) {
-                          if constexpr (BIN)
-                            acc[(rb / S) * R + d / S][j] += w[j];
-                          else
-                            acc[(rb / S) * R + d / S][j] = fmaf(xv, w[j], acc[(rb / S) * R + d / S][j]);
+                          for (int j = 0; j < CPL; j += 2) {
+                            if constexpr (BIN)
+                              add_f32x2(a[j], a[j + 1], w[j], w[j + 1]);
+                            else
+                              fma_f32x2(a[j], a[j + 1], xv, w[j], w[j + 1]);
+                          }
+                        } else {
+#pragma unroll
+                          for (int j = 0; j < CPL; ++j) {
+                            if constexpr (BIN)
+                              a[j] += w[j];
+                            else
+                              a[j] = fmaf(xv, w[j], a[j]);
+                          }
                         }
                       }
                     }
