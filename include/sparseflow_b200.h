@@ -20,6 +20,9 @@
  *   sf_fused_conv_lif     Kernels/fused_conv_lif.py:310-484 (sparse_fused_conv_lif_forward)
  *                         with the LIF semantics of Ops/sparse_fused_conv_lif.py:271-293,
  *                         run over all T steps in one launch.
+ *   sf_lif_multistep      the multi-step LIFNode that follows a BN in spikingjelly-style
+ *                         models (Ops/sparse_fused_conv_lif.py:271-293 applied over T;
+ *                         spikingjelly LIFNode, step_mode 'm'), one launch for all steps.
  */
 #ifndef SPARSEFLOW_B200_H
 #define SPARSEFLOW_B200_H
@@ -140,7 +143,9 @@ size_t sf_sparse_conv2d_workspace_size(const sf_conv_desc* d);
  * launches: a streaming pass writes the nonzero-channel masks of x into the
  * workspace, then the gather kernel reads masks (and x itself only for
  * images holding values other than 0 and 1). w_packed must be 16-byte
- * aligned; x has no alignment requirement. */
+ * aligned; x has no alignment requirement. Patterns: 3x3/s1/p1, 3x3/s2/p1,
+ * 1x1/s1/p0 and 1x1/s2/p0 (the last in one pass that builds the masks in
+ * shared memory; it uses no workspace). */
 sf_status sf_sparse_conv2d(const void* x, const void* w_packed, const float* bias,
                            void* y, const sf_conv_desc* d,
                            void* workspace, size_t workspace_bytes, void* stream);

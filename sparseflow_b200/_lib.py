@@ -203,7 +203,8 @@ def conv_status(device: torch.device) -> int:
 # ----------------------------------------------------------------------------
 
 def pack_weights(weight: torch.Tensor, out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
-    """[C_out, C_in, k, k] -> packed [C_in][k*k][round_up(C_out, 128)] (a flat byte buffer)."""
+    """[C_out, C_in, k, k] -> packed [block][C_in][k*k][32][cpl], block = 32*cpl output channels
+    (zero padded past C_out; cpl chosen by the library so one block fits shared memory)."""
     _require_cuda(weight)
     w = weight.detach().contiguous()
     co, ci, kh, kw = w.shape
