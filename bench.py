@@ -57,6 +57,10 @@ def parse():
     ap.add_argument("--no-extra", action="store_true", help="skip the C2/C3/prescan side measurements")
     ap.add_argument("--only-timed", action="store_true",
                     help="run only the warm-up and timed steps (no cuDNN, e2e, extras or CPU baseline); for ncu")
+    ap.add_argument("--sweep", action="store_true",
+                    help="C5 grid: C x H x density, sparse conv3x3 vs cuDNN and the HBM roofline (one JSON line per cell)")
+    ap.add_argument("--sweep-images", type=int, default=T_STEPS * N_BATCH,
+                    help="T*N images per sweep cell (BASELINE: T16 N64 = 1024)")
     ap.add_argument("--images", type=int, default=T_STEPS * N_BATCH,
                     help="T*N images per step (multiple of 16); smaller values make an ncu-sized case")
     return ap.parse_args()
@@ -275,8 +279,19 @@ def extras(dev, hbm_peak, steps):
         return m3(x3)
     ms = cuda_time(c3_step, steps, 3) / steps
     b3 = 4 * x3.numel() * 2 + 4 * 64 * 128 * 28 * 28 * 2 + 4 * 128 * 128 * 9
+
+    # What the reference runs for this layer on a GPU without its (dead) fused kernel:
+    # cuDNN conv over all T*N images, eval BN, then the LIF formula step by step in torch.
+    lif_ref = LIFNode(tau=2.0, v_threshold=1.0, v_reset=0.0)
+
+    def c3_torch():
+        y = bn(torch.nn.functional.conv2d(x3.flatten(0, 1), conv3.weight, None, 1, 1)).reshape(16, 64, 128, 28, 28)
+        lif_ref.reset()
+        return torch.stack([lif_ref._step(y[t]) for t in range(16)], 0)
+    ms_ref = cuda_time(c3_torch, max(3, steps // 5), 2) / max(3, steps // 5)
     out["c3_fused_conv_bn_lif"] = {"GBps": round(b3 / ms / 1e6, 1), "frac_of_measured_hbm": round(b3 / ms / 1e6 / hbm_peak, 3),
-                                   "ms": round(ms, 4)}
+                                   "ms": round(ms, 4), "cudnn_conv_bn_torch_lif_ms": round(ms_ref, 4),
+                                   "speedup_vs_cudnn_path": round(ms_ref / ms, 2)}
     del x3
     out["c4_spiking_resnet50"] = c4_resnet(dev)
     return out
@@ -319,10 +334,46 @@ def c4_resnet(dev, iters=3):
             "note": "same random-init model and input; every LIF node is one sf_lif_multistep launch in both"}
 
 
+def run_sweep(args):
+    """C5: conv3x3/s1/p1 C->C over C in {64,128,256,512}, H=W in {14,28,56}, density in
+    {0.001,0.01,0.05,0.2}; block size per the H->block rule (inert in the kernels). Bytes = x + y + w + b."""
+    from sparseflow_b200.Ops.sparse_conv2d import SparseConv2d
+    from sparseflow_b200.Utils.block_selector import select_block_size
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    hbm_peak, _, peak_kind = peaks()
+    n_img = args.sweep_images
+    for c in (64, 128, 256, 512):
+        conv = make_conv(c, c, 3, 1, 1, True, c, device=dev)
+        for h in (14, 28, 56):
+            mod = SparseConv2d.from_dense(conv, block_size=select_block_size(h))
+            mod.set_inference_mode(True)
+            for dens in (0.001, 0.01, 0.05, 0.2):
+                g = torch.Generator(device=dev).manual_seed(c * 1000 + h)
+                x = (torch.rand(n_img, c, h, h, device=dev, generator=g) < dens).float()
+                steps = 10
+                with torch.no_grad():
+                    ms = cuda_time(lambda: mod(x), steps, 3) / steps
+                    cud = cuda_time(lambda: torch.nn.functional.conv2d(x, conv.weight, conv.bias, 1, 1), steps, 3) / steps
+                nbytes = conv_bytes(n_img, c, h, h, c, h, h, 3)
+                gbps = nbytes / ms / 1e6
+                flops = 2.0 * n_img * c * c * 9 * h * h
+                print(json.dumps({"cell": f"C{c}_H{h}_p{dens}", "c": c, "h": h, "density": dens, "images": n_img,
+                                  "block": select_block_size(h), "ms": round(ms, 4), "cudnn_ms": round(cud, 4),
+                                  "speedup_vs_cudnn": round(cud / ms, 2), "GBps": round(gbps, 1),
+                                  "hbm_frac": round(gbps / hbm_peak, 3), "peak": f"{hbm_peak} GB/s ({peak_kind})",
+                                  "hbm_floor_ms": round(nbytes / hbm_peak / 1e6, 4),
+                                  "dense_equiv_tflops_cudnn": round(flops / cud / 1e9, 1)}), flush=True)
+                del x
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+        return
+    if args.sweep:
+        run_sweep(args)
         return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
