@@ -11,11 +11,3 @@ sf_status dispatch_f32(bool lif, int wdt, int K, int S, const ConvParams& p, con
 }  // namespace conv
 }  // namespace sf
 
-#ifdef SF_CONV_PHASE_PROFILE
-// Instrumented builds only: copies (and clears) the fp32 kernels' phase cycle totals.
-extern "C" int sf_debug_conv_phases(unsigned long long* out8) {
-  if (cudaMemcpyFromSymbol(out8, sf::conv::g_conv_phase, 64) != cudaSuccess) return 1;
-  unsigned long long z[8] = {0};
-  return cudaMemcpyToSymbol(sf::conv::g_conv_phase, z, 64) == cudaSuccess ? 0 : 1;
-}
-#endif

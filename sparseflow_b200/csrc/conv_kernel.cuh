@@ -74,6 +74,11 @@ inline int weight_block_cpl(int C, int K, int Co, int wsz) {
     if (cpl > 1 && cpl > slices) continue;
     if ((size_t)C * K * K * 32 * cpl * wsz <= kWsmemMax) return cpl;
   }
+  // No block fits shared memory: weights are read from L2. Four slices per
+  // lane walk each event for 128 output channels at once (4-pixel segments);
+  // SF_CONV_L2_CPL=2 keeps 8-pixel segments with sector-complete stores.
+  const char* e = getenv("SF_CONV_L2_CPL");
+  if (e && atoi(e) == 2) return slices >= 2 ? 2 : 1;
   return slices >= 4 ? 4 : (slices >= 2 ? 2 : 1);
 }
 
@@ -82,21 +87,6 @@ inline int weight_block_cpl(int C, int K, int Co, int wsz) {
 // CPL channels of one (channel, tap) with one vector load.
 inline int weight_blocks(int Co, int cpl) { return ((Co + 31) / 32 + cpl - 1) / cpl; }
 
-// Optional phase timing (builds with -DSF_CONV_PHASE_PROFILE only): thread 0
-// accumulates cycles per phase in registers and adds them to g_conv_phase.
-#ifdef SF_CONV_PHASE_PROFILE
-__device__ unsigned long long g_conv_phase[8];
-#define SF_PHASE(i)                  \
-  do {                               \
-    const long long t1_ = clock64(); \
-    ph_acc[i] += t1_ - ph_t0;        \
-    ph_t0 = t1_;                     \
-  } while (0)
-#else
-#define SF_PHASE(i) \
-  do {              \
-  } while (0)
-#endif
 
 struct ConvParams {
   const void* x;
@@ -366,10 +356,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   // ---------------------------------------------------------------- compute
-#ifdef SF_CONV_PHASE_PROFILE
-  long long ph_t0 = clock64();
-  long long ph_acc[5] = {0, 0, 0, 0, 0};
-#endif
   const XT* __restrict__ x = static_cast<const XT*>(p.x);
   const WT* __restrict__ wglob = static_cast<const WT*>(p.wp);
   float acc[B * R][CPL];
@@ -445,12 +431,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = 0; t < T; ++t, ++g) {
       const int s = g % p.nstage;
       const size_t img = (size_t)(LIF ? t * p.N + n : n);
-      SF_PHASE(4);
       if (!mbar_wait_bounded(&full[s], (uint32_t)((g / p.nstage) & 1))) {
         if (lane == 0) atomicExch(p.err, 1u);
         return;
       }
-      SF_PHASE(0);
       const unsigned long long* st = stages + (size_t)s * p.slot_words;
       const int e0 = (int)((((img * p.H + ih_lo) * p.W) * p.nw) & 1);  // word offset of the aligned copy
       const bool binary = (__ldg(p.flags + img) & 1u) == 0u;
@@ -477,7 +461,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           mk[rd] = m;
           nzpos[rd] = __ballot_sync(0xffffffffu, m != 0ull);
         }
-        SF_PHASE(1);
         // Events: each set bit of a nonzero position feeds up to K taps.
         auto gather = [&](auto binary_tag) {
           constexpr bool BIN = decltype(binary_tag)::value;
@@ -503,12 +486,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int kh = 0; kh < K; ++kh) {
                   const int rb = hh - kh;  // S * (output row within the tile)
                   if (rb >= 0 && rb % S == 0 && rb / S < B) {
+                    // All taps' weight vectors first, then the adds: with weights
+                    // in L2 (no shared-memory copy) the loads overlap.
+                    float w[K][CPL];
+#pragma unroll
+                    for (int kw = 0; kw < K; ++kw) {
+                      const int d = qq - kw;
+                      if (d >= 0 && d % S == 0 && d / S < R)
+                        WVec<WT, CPL, WSMEM>::ld(wc + (kh * K + kw) * 32 * CPL, w[kw]);
+                    }
 #pragma unroll
                     for (int kw = 0; kw < K; ++kw) {
                       const int d = qq - kw;
                       if (d >= 0 && d % S == 0 && d / S < R) {
-                        float w[CPL];
-                        WVec<WT, CPL, WSMEM>::ld(wc + (kh * K + kw) * 32 * CPL, w);
                         float(&a)[CPL] = acc[(rb / S) * R + d / S];
                         // Pairs for fp32 weights (a float2 load feeds add.f32x2 directly);
                         // bf16 weights measured faster with scalar adds.
@@ -516,17 +506,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                           for (int j = 0; j < CPL; j += 2) {
                             if constexpr (BIN)
-                              add_f32x2(a[j], a[j + 1], w[j], w[j + 1]);
+                              add_f32x2(a[j], a[j + 1], w[kw][j], w[kw][j + 1]);
                             else
-                              fma_f32x2(a[j], a[j + 1], xv, w[j], w[j + 1]);
+                              fma_f32x2(a[j], a[j + 1], xv, w[kw][j], w[kw][j + 1]);
                           }
                         } else {
 #pragma unroll
                           for (int j = 0; j < CPL; ++j) {
                             if constexpr (BIN)
-                              a[j] += w[j];
+                              a[j] += w[kw][j];
                             else
-                              a[j] = fmaf(xv, w[j], a[j]);
+                              a[j] = fmaf(xv, w[kw][j], a[j]);
                           }
                         }
                       }
@@ -537,16 +527,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         };
-#ifdef SF_CONV_EXPERIMENT_NO_GATHER
-        if (false) {
-#else
         // Warp-uniform skip of the unrolled position tests when no input
         // pixel of this tile has an event in this channel word.
         uint32_t nz_any = 0u;
 #pragma unroll
         for (int rd = 0; rd < ROUNDS; ++rd) nz_any |= nzpos[rd];
         if (active && nz_any != 0u) {
-#endif
           if (binary)
             gather(std::true_type{});
           else
@@ -555,14 +541,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
-      SF_PHASE(2);
 
       // Epilogue for (unit, t).
-#ifdef SF_CONV_EXPERIMENT_NO_EPILOGUE
-      if (false) {
-#else
       if (active) {
-#endif
 #pragma unroll
         for (int b = 0; b < B; ++b) {
           if (b >= nrows) break;
@@ -617,7 +598,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      SF_PHASE(3);
     }
 
     if constexpr (LIF) {
@@ -632,10 +612,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   if (p.tma_store && lane == 0) bulk_wait_group0();  // stores complete before the CTA leaves
-#ifdef SF_CONV_PHASE_PROFILE
-  if (tid == 0)
-    for (int i = 0; i < 5; ++i) atomicAdd(&g_conv_phase[i], (unsigned long long)ph_acc[i]);
-#endif
 }
 
 template <int K, int S, int CPL, int R, int B, typename XT, typename WT, bool LIF, bool WSMEM>

@@ -135,10 +135,8 @@ namespace {
 sf_status dispatch(bool lif, int xdt, int wdt, int K, int S, const ConvParams& p, const CUtensorMap& ym, int grid,
                    const Plan& pl, cudaStream_t st) {
   if (xdt == SF_DTYPE_F32) return dispatch_f32(lif, wdt, K, S, p, ym, grid, pl, st);
-#ifndef SF_CONV_ONLY_F32  // experiment builds compile only the fp32-input instantiations
   if (xdt == SF_DTYPE_F16) return dispatch_f16(lif, wdt, K, S, p, ym, grid, pl, st);
   if (xdt == SF_DTYPE_BF16) return dispatch_bf16(lif, wdt, K, S, p, ym, grid, pl, st);
-#endif
   return SF_ERR_UNSUPPORTED;
 }
 
