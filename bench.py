@@ -57,6 +57,8 @@ def parse():
     ap.add_argument("--no-extra", action="store_true", help="skip the C2/C3/prescan side measurements")
     ap.add_argument("--only-timed", action="store_true",
                     help="run only the warm-up and timed steps (no cuDNN, e2e, extras or CPU baseline); for ncu")
+    ap.add_argument("--kernel", choices=["conv", "prescan"], default="conv",
+                    help="with --only-timed: time the sparse conv (default) or the prescan on the same input")
     ap.add_argument("--sweep", action="store_true",
                     help="C5 grid: C x H x density, sparse conv3x3 vs cuDNN and the HBM roofline (one JSON line per cell)")
     ap.add_argument("--sweep-images", type=int, default=T_STEPS * N_BATCH,
@@ -397,6 +399,23 @@ def main():
     mod = SparseConv2d.from_dense(conv, block_size=16)
     mod.set_inference_mode(True)
     step_bytes = conv_bytes(n_img, C, H, W, C, H, W, 3)
+
+    if args.only_timed and args.kernel == "prescan":
+        from sparseflow_b200.Kernels._prescan_common import prescan2d
+        x4 = x.reshape(n_img, C, H, W)
+        nt = n_img * 7 * 4
+        ag = torch.empty(nt, dtype=torch.int32, device=dev)
+        tc, ids = torch.empty_like(ag), torch.empty_like(ag)
+        cnt = torch.zeros(1, dtype=torch.int32, device=dev)
+        ms = cuda_time(lambda: prescan2d(x4, 0, (H, W), (3, 3), 1, 1, (8, 16), 16, 1e-6, ag, tc, ids, cnt),
+                       args.steps, args.warmup, dist) / args.steps
+        pb = x4.numel() * 4 + nt * 12
+        if rank == 0:
+            print(json.dumps({"kernel": "prescan", "ms_per_step": round(ms, 4), "GBps": round(pb / ms / 1e6, 1),
+                              "frac_of_measured_hbm": round(pb / ms / 1e6 / hbm_peak, 3), "images": n_img}))
+        if dist is not None:
+            dist.destroy_process_group()
+        return
 
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
     phys = int(vis.split(",")[local]) if vis and vis.split(",")[local].strip().isdigit() else local
