@@ -351,8 +351,10 @@ __global__ void __launch_bounds__(256) prescan2d_kernel(PrescanParams p) {
 
 // Two-pass path, pass 2: one CTA per (image, run of tile rows). It stages
 // the run's receptive-field rows of group words in shared memory once (no
-// halo re-reads between tile rows), ORs every tile's window with one warp per
-// tile, and writes ag_mask, tile_class and each tile row's non-ZERO count.
+// halo re-reads between tile rows), ORs each row over every tile's
+// receptive-field columns (a thread per row and tile column), then each
+// tile's rows (a thread per tile), and writes ag_mask, tile_class and each
+// tile row's non-ZERO count.
 constexpr int kPoolThreads = 256;
 
 __global__ void __launch_bounds__(kPoolThreads) pool_tiles_kernel(PrescanParams p, int rows_per_cta) {
@@ -390,34 +392,45 @@ __global__ void __launch_bounds__(kPoolThreads) pool_tiles_kernel(PrescanParams 
   }
   if (tid < 64) s_cnt[tid] = 0;
   __syncthreads();
+  // B1: per (staged input row, tile column) OR of the tile's receptive-field columns.
+  uint32_t* racc = nanm + p.max_rows_in * p.W;  // [rows_in][GW] active groups
+  uint32_t* rnan = racc + p.max_rows_in * p.GW;  // [rows_in][GW] NaN groups
+  for (int idx = tid; idx < rows_in * p.GW; idx += kPoolThreads) {
+    const int r = idx / p.GW;
+    const int gw = idx - r * p.GW;
+    const int ow0 = gw * p.BW;
+    const int ow1 = min(ow0 + p.BW, p.Wo);
+    const int iw_lo = max(0, ow0 * p.S - p.P);
+    const int iw_hi = min(p.W, (ow1 - 1) * p.S - p.P + p.K);
+    uint32_t a = 0, nn = 0;
+    for (int c = iw_lo; c < iw_hi; ++c) {
+      a |= act[r * p.W + c];
+      nn |= nanm[r * p.W + c];
+    }
+    racc[idx] = a;
+    rnan[idx] = nn;
+  }
+  __syncthreads();
+  // B2: per tile, OR of its receptive-field rows.
   const int ntiles = (gh1 - gh0) * p.GW;
-  for (int t = warp; t < ntiles; t += kPoolThreads / 32) {
+  for (int t = tid; t < ntiles; t += kPoolThreads) {
     const int ghl = t / p.GW;
     const int gw = t - ghl * p.GW;
     const int toh0 = (gh0 + ghl) * p.BH;
     const int toh1 = min(toh0 + p.BH, p.Ho);
     const int r_lo = max(0, toh0 * p.S - p.P) - ih_lo;
     const int r_hi = min(p.H, (toh1 - 1) * p.S - p.P + p.K) - ih_lo;
-    const int ow0 = gw * p.BW;
-    const int ow1 = min(ow0 + p.BW, p.Wo);
-    const int iw_lo = max(0, ow0 * p.S - p.P);
-    const int iw_hi = min(p.W, (ow1 - 1) * p.S - p.P + p.K);
     uint32_t a = 0, nn = 0;
-    for (int r = r_lo; r < r_hi; ++r)
-      for (int c = iw_lo + lane; c < iw_hi; c += 32) {
-        a |= act[r * p.W + c];
-        nn |= nanm[r * p.W + c];
-      }
-    a = __reduce_or_sync(0xffffffffu, a);
-    nn = __reduce_or_sync(0xffffffffu, nn);
-    if (lane == 0) {
-      const uint32_t m = a & ~nn & p.group_full;
-      const int cls = (m == 0u) ? SF_TILE_ZERO : ((m == p.group_full) ? SF_TILE_DENSEISH : SF_TILE_SPARSE);
-      const size_t tile = ((size_t)n * p.GH + gh0 + ghl) * p.GW + gw;
-      p.ag_mask[tile] = (int32_t)m;
-      p.tile_class[tile] = cls;
-      if (cls != SF_TILE_ZERO) atomicAdd(&s_cnt[ghl], 1);
+    for (int r = r_lo; r < r_hi; ++r) {
+      a |= racc[r * p.GW + gw];
+      nn |= rnan[r * p.GW + gw];
     }
+    const uint32_t m = a & ~nn & p.group_full;
+    const int cls = (m == 0u) ? SF_TILE_ZERO : ((m == p.group_full) ? SF_TILE_DENSEISH : SF_TILE_SPARSE);
+    const size_t tile = ((size_t)n * p.GH + gh0 + ghl) * p.GW + gw;
+    p.ag_mask[tile] = (int32_t)m;
+    p.tile_class[tile] = cls;
+    if (cls != SF_TILE_ZERO) atomicAdd(&s_cnt[ghl], 1);
   }
   __syncthreads();
   if (p.row_count != nullptr && tid < gh1 - gh0) p.row_count[(size_t)n * p.GH + gh0 + tid] = s_cnt[tid];
@@ -689,11 +702,12 @@ extern "C" sf_status sf_prescan2d(const void* x, const sf_prescan_desc* d, int32
   }
   if (p.bits != nullptr) {
     // Tile rows per pooling CTA: as many as 48 KB of staged rows allow (<= 64).
+    // Staged rows: group words (2 x W) plus per-row tile-column ORs (2 x GW).
+    auto pool_smem = [&](int rows) { return 2ull * rows * (p.W + p.GW) * 4; };
     int rpc = 1;
-    while (rpc < 64 && rpc < p.GH && 2ull * ((size_t)((rpc + 1) * p.BH - 1) * p.S + p.K) * p.W * 4 <= 48 * 1024)
-      ++rpc;
+    while (rpc < 64 && rpc < p.GH && pool_smem(((rpc + 1) * p.BH - 1) * p.S + p.K) <= 48 * 1024) ++rpc;
     p.max_rows_in = std::min(p.H, (rpc * p.BH - 1) * p.S + p.K);
-    const size_t psmem = 2ull * p.max_rows_in * p.W * 4;
+    const size_t psmem = pool_smem(p.max_rows_in);
     const int chunks = (p.GH + rpc - 1) / rpc;
     if (psmem > 48 * 1024 &&
         cudaFuncSetAttribute(pool_tiles_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)psmem) != cudaSuccess)
