@@ -59,6 +59,10 @@ constexpr int kComputeWarps = kNWarps - 1;
 // registers a 1024-thread CTA allows and measured 30% slower; one row is the
 // default.
 constexpr int kRowsPerWarp = SF_CONV_ROWS_PER_WARP;
+#ifndef SF_CONV_GATHER_ROW_LOOP
+#define SF_CONV_GATHER_ROW_LOOP 1
+#endif
+constexpr bool kGatherRowLoop = SF_CONV_GATHER_ROW_LOOP != 0;
 constexpr int kProducerWarp = kNWarps - 1;
 constexpr int kMaxStages = 8;
 constexpr int kSmemLimit = 227 * 1024;
@@ -462,6 +466,74 @@ __global__ void __launch_bounds__(kThreads, 1)
           nzpos[rd] = __ballot_sync(0xffffffffu, m != 0ull);
         }
         // Events: each set bit of a nonzero position feeds up to K taps.
+        // One output row per warp (B == 1): input row hh feeds only kernel
+        // row hh, so the rows run as a loop and only the columns (which fix
+        // the accumulator) are unrolled: a third of the code of the fully
+        // unrolled form below, which the instruction cache holds better.
+        auto gather_rows = [&](auto binary_tag) {
+          constexpr bool BIN = decltype(binary_tag)::value;
+          const WT* wrow = wbase + (size_t)wd * 64 * KK * 32 * CPL;
+#pragma unroll 1
+          for (int hh = 0; hh < K; ++hh) {
+            const WT* wkh = wrow + hh * K * 32 * CPL;
+            const XT* xrow = x + ((img * p.C + wd * 64) * p.H + (ih0 + hh)) * p.W + col0;
+#pragma unroll
+            for (int qq = 0; qq < QN; ++qq) {
+              const int pos = hh * QN + qq;
+              uint32_t nzw = nzpos[0];
+              unsigned long long mw = mk[0];
+#pragma unroll
+              for (int rd = 1; rd < ROUNDS; ++rd)
+                if ((pos >> 5) == rd) {
+                  nzw = nzpos[rd];
+                  mw = mk[rd];
+                }
+              if (((nzw >> (pos & 31)) & 1u) == 0u) continue;
+              const unsigned long long m64 = shfl64(mw, pos & 31);
+#pragma unroll
+              for (int hw = 0; hw < 2; ++hw) {
+                uint32_t m = hw ? (uint32_t)(m64 >> 32) : (uint32_t)m64;
+                while (m) {
+                  const int ci = __ffs(m) - 1 + 32 * hw;
+                  m &= m - 1u;
+                  const WT* wc = wkh + (size_t)ci * (KK * 32 * CPL);
+                  float xv = 1.f;
+                  if constexpr (!BIN) xv = DT<XT>::to_f(__ldg(xrow + (size_t)ci * p.H * p.W + qq));
+                  float w[K][CPL];
+#pragma unroll
+                  for (int kw = 0; kw < K; ++kw) {
+                    const int d = qq - kw;
+                    if (d >= 0 && d % S == 0 && d / S < R) WVec<WT, CPL, WSMEM>::ld(wc + kw * 32 * CPL, w[kw]);
+                  }
+#pragma unroll
+                  for (int kw = 0; kw < K; ++kw) {
+                    const int d = qq - kw;
+                    if (d >= 0 && d % S == 0 && d / S < R) {
+                      float(&a)[CPL] = acc[d / S];
+                      if constexpr (CPL % 2 == 0 && std::is_same<WT, float>::value) {
+#pragma unroll
+                        for (int j = 0; j < CPL; j += 2) {
+                          if constexpr (BIN)
+                            add_f32x2(a[j], a[j + 1], w[kw][j], w[kw][j + 1]);
+                          else
+                            fma_f32x2(a[j], a[j + 1], xv, w[kw][j], w[kw][j + 1]);
+                        }
+                      } else {
+#pragma unroll
+                        for (int j = 0; j < CPL; ++j) {
+                          if constexpr (BIN)
+                            a[j] += w[kw][j];
+                          else
+                            a[j] = fmaf(xv, w[kw][j], a[j]);
+                        }
+                      }
+                    }
+                  }
+                }
+              }
+            }
+          }
+        };
         auto gather = [&](auto binary_tag) {
           constexpr bool BIN = decltype(binary_tag)::value;
 #pragma unroll
@@ -533,10 +605,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int rd = 0; rd < ROUNDS; ++rd) nz_any |= nzpos[rd];
         if (active && nz_any != 0u) {
-          if (binary)
-            gather(std::true_type{});
-          else
-            gather(std::false_type{});
+          if constexpr (B == 1 && kGatherRowLoop) {
+            if (binary)
+              gather_rows(std::true_type{});
+            else
+              gather_rows(std::false_type{});
+          } else {
+            if (binary)
+              gather(std::true_type{});
+            else
+              gather(std::false_type{});
+          }
         }
       }
       __syncwarp();
