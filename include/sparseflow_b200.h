@@ -19,7 +19,10 @@
  *                         sparse_conv3x3s1/s2 and conv1x1 NHWC kernels, :236-886).
  *   sf_fused_conv_lif     Kernels/fused_conv_lif.py:310-484 (sparse_fused_conv_lif_forward)
  *                         with the LIF semantics of Ops/sparse_fused_conv_lif.py:271-293,
- *                         run over all T steps in one launch.
+ *                         run over all T steps in one launch; optionally also writes the
+ *                         next layer's event masks.
+ *   sf_sparse_conv2d_from_masks, sf_event_masks_bytes
+ *                         no reference counterpart: the consumer side of those masks.
  *   sf_lif_multistep      the multi-step LIFNode that follows a BN in spikingjelly-style
  *                         models (Ops/sparse_fused_conv_lif.py:271-293 applied over T;
  *                         spikingjelly LIFNode, step_mode 'm'), one launch for all steps.
@@ -174,11 +177,27 @@ typedef struct sf_lif_desc {
 size_t sf_fused_conv_lif_workspace_size(const sf_lif_desc* d);
 
 /* v_inout: fp32 [n, c_out, h_out, w_out], read as v[0] and overwritten with
- * the membrane state after the last step. Supports 3x3/s1/p1 and 1x1/s1/p0. */
+ * the membrane state after the last step. Supports 3x3/s1/p1 and 1x1/s1/p0.
+ * spike_masks_out (may be NULL; 8-byte aligned, sf_event_masks_bytes(
+ * t_steps * n, c_out, h_out, w_out) bytes): the next layer's events, i.e. the
+ * nonzero-channel masks of spikes_out in the layout the mask pass of
+ * sf_sparse_conv2d writes ([t_steps*n][h_out][w_out][ceil(c_out/64)] 64-bit
+ * words), so the following convolution can run from them
+ * (sf_sparse_conv2d_from_masks) without reading the spikes again. */
 sf_status sf_fused_conv_lif(const void* x, const void* w_packed, const float* bias,
-                            float* v_inout, void* spikes_out,
+                            float* v_inout, void* spikes_out, void* spike_masks_out,
                             const sf_lif_desc* d,
                             void* workspace, size_t workspace_bytes, void* stream);
+
+/* Bytes of the event masks of n_images images of channels x h x w. */
+size_t sf_event_masks_bytes(int64_t n_images, int32_t channels, int32_t h, int32_t w);
+
+/* sf_sparse_conv2d of binary spikes given only their event masks (as written
+ * by sf_fused_conv_lif's spike_masks_out; 16-byte aligned): x is not read,
+ * no workspace is needed. d->x_dtype is the dtype of y. */
+sf_status sf_sparse_conv2d_from_masks(const void* event_masks, const void* w_packed,
+                                      const float* bias, void* y, const sf_conv_desc* d,
+                                      void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* Multi-step LIF neuron (the separate LIFNode after a BN, not fused into a  */

@@ -71,12 +71,15 @@ def sparse_conv2d_forward(
     x_nhwc=None, active_tile_ids_buf=None,
     launch_all_tiles=False,
     output_dtype=None,
+    event_masks=None,
 ):
     """Sparse conv2d of an NCHW CUDA tensor. See the module docstring.
 
     ``w_cl`` is an optional pre-packed weight buffer (from ``pack_weight``);
     ``x_nhwc`` and ``fallback_ratio`` are accepted for signature compatibility
     and unused (the kernel reads NCHW; the runtime dense policy is off).
+    ``event_masks``: x's per-pixel nonzero-channel masks as written by a fused
+    conv + LIF (x then holds binary spikes); the mask pass over x is skipped.
     """
     if not x.is_cuda:
         raise RuntimeError("sparse_conv2d_forward needs a CUDA tensor (the B200 path has no CPU fallback)")
@@ -165,7 +168,12 @@ def sparse_conv2d_forward(
     if return_ms:
         se, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         se.record()
-    _lib.sparse_conv2d(x, w_packed, b, y, c_out, kernel_size, stride, padding)
+    used_masks = event_masks is not None and (kernel_size, stride) != (1, 2)
+    if used_masks:
+        _lib.sparse_conv2d_from_masks(event_masks, tuple(x.shape), x.dtype, w_packed, b, y, kernel_size, stride,
+                                      padding)
+    else:
+        _lib.sparse_conv2d(x, w_packed, b, y, c_out, kernel_size, stride, padding)
     if return_ms:
         ee.record()
         torch.cuda.synchronize(x.device)
@@ -176,6 +184,7 @@ def sparse_conv2d_forward(
         "backend": "sparse_b200", "reason": "element_gather_sm100a",
         "total_tiles": n_tiles, "launch_count": n_tiles,
         "launch_mode": "persistent", "launch_mode_reason": "persistent_gather",
+        "event_masks": used_masks,
     }
     if active_tiles is not None:
         meta["active_tiles"] = active_tiles

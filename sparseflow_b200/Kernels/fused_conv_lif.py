@@ -49,6 +49,7 @@ def sparse_fused_conv_lif_forward(
     padding: Optional[int] = None,
     w_packed: Optional[torch.Tensor] = None,
     return_ms: bool = False,
+    emit_event_masks: bool = False,
 ):
     """x: [T, N, C, H, W] (or [N, C, H, W] for one step); v_prev: [N, C_out, H_out, W_out].
 
@@ -74,13 +75,38 @@ def sparse_fused_conv_lif_forward(
     if tuple(v.shape) != (n, co, ho, wo):
         raise ValueError(f"v_prev shape {tuple(v.shape)} != {(n, co, ho, wo)}")
     spikes = torch.empty(t, n, co, ho, wo, dtype=x5.dtype, device=x5.device)
+    masks = None
+    if emit_event_masks:
+        nbytes = _lib.event_masks_bytes(t * n, co, ho, wo)
+        masks = torch.empty(nbytes // 8, dtype=torch.int64, device=x5.device)
     ms = 0.0
     if return_ms:
         se, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         se.record()
-    _lib.fused_conv_lif(x5, wp, b, v, spikes, kernel_size, stride, padding, tau, v_threshold, v_reset, decay_input)
+    _lib.fused_conv_lif(x5, wp, b, v, spikes, kernel_size, stride, padding, tau, v_threshold, v_reset, decay_input,
+                        masks_out=masks)
     if return_ms:
         ee.record()
         torch.cuda.synchronize(x5.device)
         ms = se.elapsed_time(ee)
-    return (spikes[0] if single else spikes), v, ms
+    out = spikes[0] if single else spikes
+    if masks is not None:
+        attach_event_masks(out, masks)
+    return out, v, ms
+
+
+def attach_event_masks(spikes: torch.Tensor, masks: torch.Tensor) -> None:
+    """Record on the spikes tensor its event masks ([T*N][H][W][ceil(C/64)] 64-bit words), so that a
+    following SparseConv2d that receives this very tensor runs from them instead of re-reading it."""
+    spikes._sf_event_masks = (masks, spikes.data_ptr(), tuple(spikes.shape), spikes.dtype)
+
+
+def event_masks_of(x: torch.Tensor):
+    """The masks attached by attach_event_masks if x is still the tensor they describe, else None."""
+    rec = getattr(x, "_sf_event_masks", None)
+    if rec is None:
+        return None
+    masks, ptr, shape, dtype = rec
+    if ptr != x.data_ptr() or shape != tuple(x.shape) or dtype != x.dtype or x._version != 0:
+        return None
+    return masks

@@ -26,6 +26,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from ..Kernels.fused_conv_lif import event_masks_of
 from ..Kernels.conv2d import (SUPPORTED_PATTERNS, choose_group_size, output_hw, pack_weight,
                               sparse_conv2d_forward)
 from ..Utils.sparse_helpers import TILE_DENSEISH, TILE_SPARSE, TILE_ZERO, select_tile_sizes
@@ -182,6 +183,7 @@ class SparseConv2d(nn.Module):
         if self.profile_runtime:
             self._profile.calls += 1
             t_total = self._stamp()
+        event_masks = event_masks_of(x)  # set when x came straight from a FusedSparseConvLIF
         if x.dim() == 5:
             t, b, c, h, w = x.shape
             x4 = x.reshape(t * b, c, h, w)
@@ -192,8 +194,9 @@ class SparseConv2d(nn.Module):
         if not x4.is_cuda:
             raise RuntimeError("SparseConv2d runs on CUDA tensors only; the B200 path has no CPU fallback")
 
+        self._last_used_event_masks = False
         if self._supports_sparse():
-            y4, backend = self._sparse_forward(x4)
+            y4, backend = self._sparse_forward(x4, event_masks)
         else:
             y4 = F.conv2d(x4, self.weight, self.bias, self.stride, self.padding, self.dilation, self.groups)
             backend = "dense_fallback"
@@ -224,9 +227,11 @@ class SparseConv2d(nn.Module):
                 setattr(self, name, torch.empty(n_tiles, dtype=torch.int32, device=x4.device))
         return n_tiles
 
-    def _sparse_forward(self, x4):
+    def _sparse_forward(self, x4, event_masks=None):
         diag = self.collect_diag and not self._inference_mode
         kw = {}
+        if event_masks is not None and not diag:
+            kw["event_masks"] = event_masks
         if diag:
             self._ensure_buffers(x4)
             kw = dict(ag_mask_buf=self._ag_mask_buf, tile_class_buf=self._tile_class_buf,
@@ -238,6 +243,7 @@ class SparseConv2d(nn.Module):
             launch_all_tiles=self.launch_all_tiles, output_dtype=x4.dtype, **kw)
         y, ms = res[0], res[1]
         meta = res[-1]
+        self._last_used_event_masks = bool(meta.get("event_masks", False))
         self._last_sparse_ms = float(ms)
         self._last_dense_ms = 0.0
         if diag:

@@ -42,6 +42,11 @@ class FusedSparseConvLIF(nn.Module):
         self.threshold = float(threshold)
         self.block_size = block_size
         self.return_ms = bool(return_ms)
+        # Opt-in: the same kernel also writes the output spikes' event masks and
+        # attaches them to the spikes, so a following SparseConv2d skips its mask
+        # pass. Measured on the C3 layer: +0.126 ms to emit vs 0.063 ms saved
+        # downstream, hence off by default.
+        self.emit_event_masks = False
         self.weight = nn.Parameter(torch.empty(out_channels, in_channels // groups, *self.kernel_size))
         if bias:
             self.bias = nn.Parameter(torch.zeros(out_channels))
@@ -109,7 +114,7 @@ class FusedSparseConvLIF(nn.Module):
         spikes, v_next, ms = sparse_fused_conv_lif_forward(
             x, self.v, self.weight, self.bias, self.tau, self.v_threshold, self.v_reset, self.decay_input,
             kernel_size=self.kernel_size[0], stride=self.stride[0], padding=self.padding[0],
-            w_packed=self._packed(), return_ms=self.return_ms)
+            w_packed=self._packed(), return_ms=self.return_ms, emit_event_masks=self.emit_event_masks)
         self.v = v_next
         self._last_sparse_ms = ms
         return spikes

@@ -101,9 +101,11 @@ _SIGNATURES = {
     "sf_sparse_conv2d": (ctypes.c_int32, [_VP, _VP, _VP, _VP, ctypes.POINTER(ConvDesc), _VP, ctypes.c_size_t, _VP]),
     "sf_sparse_conv2d_status": (ctypes.c_int32, [_VP]),
     "sf_fused_conv_lif_workspace_size": (ctypes.c_size_t, [ctypes.POINTER(LifDesc)]),
-    "sf_fused_conv_lif": (ctypes.c_int32, [_VP, _VP, _VP, _VP, _VP, ctypes.POINTER(LifDesc), _VP, ctypes.c_size_t,
+    "sf_fused_conv_lif": (ctypes.c_int32, [_VP, _VP, _VP, _VP, _VP, _VP, ctypes.POINTER(LifDesc), _VP, ctypes.c_size_t,
                                            _VP]),
     "sf_lif_multistep": (ctypes.c_int32, [_VP, _VP, _VP, ctypes.POINTER(LifMsDesc), _VP]),
+    "sf_event_masks_bytes": (ctypes.c_size_t, [ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]),
+    "sf_sparse_conv2d_from_masks": (ctypes.c_int32, [_VP, _VP, _VP, _VP, ctypes.POINTER(ConvDesc), _VP]),
 }
 
 _lib = None
@@ -253,10 +255,28 @@ def sparse_conv2d(x: torch.Tensor, w_packed: torch.Tensor, bias: Optional[torch.
     _check("sf_sparse_conv2d", st)
 
 
+def event_masks_bytes(n_images: int, channels: int, h: int, w: int) -> int:
+    return int(load().sf_event_masks_bytes(n_images, channels, h, w))
+
+
+def sparse_conv2d_from_masks(masks: torch.Tensor, x_shape, x_dtype: torch.dtype, w_packed: torch.Tensor,
+                             bias: Optional[torch.Tensor], y: torch.Tensor, kernel: int, stride: int,
+                             padding: int) -> None:
+    """Convolution of binary spikes of shape x_shape = (n, c, h, w) given their event masks."""
+    _require_cuda(masks, w_packed, bias, y)
+    n, c, h, w = x_shape
+    _, co, ho, wo = y.shape
+    desc = ConvDesc(n, c, h, w, co, ho, wo, kernel, stride, padding, sf_dtype(x_dtype), sf_dtype(w_packed.dtype),
+                    int(bias is not None))
+    st = load().sf_sparse_conv2d_from_masks(_ptr(masks), _ptr(w_packed), _ptr(bias), _ptr(y), ctypes.byref(desc),
+                                            _stream(y.device))
+    _check("sf_sparse_conv2d_from_masks", st)
+
+
 def fused_conv_lif(x5: torch.Tensor, w_packed: torch.Tensor, bias: Optional[torch.Tensor], v: torch.Tensor,
                    spikes: torch.Tensor, kernel: int, stride: int, padding: int, tau: float, v_threshold: float,
-                   v_reset: Optional[float], decay_input: bool) -> None:
-    _require_cuda(x5, w_packed, bias, v, spikes)
+                   v_reset: Optional[float], decay_input: bool, masks_out: Optional[torch.Tensor] = None) -> None:
+    _require_cuda(x5, w_packed, bias, v, spikes, masks_out)
     t, n, c, h, w = x5.shape
     _, _, co, ho, wo = spikes.shape
     desc = LifDesc(t, n, c, h, w, co, ho, wo, kernel, stride, padding, float(tau), float(v_threshold),
@@ -265,8 +285,8 @@ def fused_conv_lif(x5: torch.Tensor, w_packed: torch.Tensor, bias: Optional[torc
     lib = load()
     nbytes = lib.sf_fused_conv_lif_workspace_size(ctypes.byref(desc))
     ws = workspace(x5.device, nbytes)
-    st = lib.sf_fused_conv_lif(_ptr(x5), _ptr(w_packed), _ptr(bias), _ptr(v), _ptr(spikes), ctypes.byref(desc),
-                               _ptr(ws), ws.numel(), _stream(x5.device))
+    st = lib.sf_fused_conv_lif(_ptr(x5), _ptr(w_packed), _ptr(bias), _ptr(v), _ptr(spikes), _ptr(masks_out),
+                               ctypes.byref(desc), _ptr(ws), ws.numel(), _stream(x5.device))
     _check("sf_fused_conv_lif", st)
 
 

@@ -4,9 +4,9 @@
 
 namespace sf {
 namespace conv {
-sf_status dispatch_f16(bool lif, int wdt, int K, int S, const ConvParams& p, const CUtensorMap& ym, int grid,
+sf_status dispatch_f16(int mode, int wdt, int K, int S, const ConvParams& p, const CUtensorMap& ym, int grid,
                        const Plan& pl, cudaStream_t st) {
-  return dispatch_x<__half>(lif, wdt, K, S, p, ym, grid, pl, st);
+  return dispatch_x<__half>(mode, wdt, K, S, p, ym, grid, pl, st);
 }
 }  // namespace conv
 }  // namespace sf

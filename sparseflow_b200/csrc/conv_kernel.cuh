@@ -101,6 +101,8 @@ struct ConvParams {
   uint32_t* err;
   const unsigned long long* masks;  // [T*N][H][W][nw]
   const uint32_t* flags;            // [T*N]: bit 0 set when values other than 0/1 occur
+  uint32_t* mask_out;               // LIF: spike masks [T*N][Ho][Wo][2*nw_out] 32-bit halves, or null
+  int nw_out;                       // ceil(Co / 64)
   int nw;
   float tau, vth, vreset;
   int hard_reset, decay_input;
@@ -280,9 +282,14 @@ __device__ __forceinline__ void store_slice(T* base, size_t co_stride, int co_li
   if (lane < co_lim) store_run<T, R>(base + lane * co_stride, v, nvalid);
 }
 
-template <int K, int S, int CPL, int R, int B, typename XT, typename WT, bool LIF, bool WSMEM>
+// MODE 0: convolution; 1: fused conv + LIF; 2: fused conv + LIF that also
+// writes the spikes' event masks (a separate instantiation, so the plain LIF
+// kernel carries none of that code).
+template <int K, int S, int CPL, int R, int B, typename XT, typename WT, int MODE, bool WSMEM>
 __global__ void __launch_bounds__(kThreads, 1)
     sparse_conv_kernel(const ConvParams p, const __grid_constant__ CUtensorMap ymap) {
+  constexpr bool LIF = MODE >= 1;
+  constexpr bool EMIT = MODE == 2;
   extern __shared__ __align__(128) unsigned char smem[];
   constexpr int KK = K * K;
   constexpr int QN = (R - 1) * S + K;  // input columns a row segment reads
@@ -649,6 +656,26 @@ __global__ void __launch_bounds__(kThreads, 1)
               out[j][i] = val;
             }
           }
+          if constexpr (EMIT) {
+            // Next layer's events: bit (co % 32) of half co / 32 of the 64-bit
+            // mask word of each output pixel, the same layout the mask pass
+            // writes, so a following convolution can skip that pass.
+            {
+#pragma unroll
+              for (int j = 0; j < CPL; ++j) {
+                const int co0 = (cob * CPL + j) * 32;
+                if (co0 >= p.Co) break;
+                uint32_t mine = 0u;
+#pragma unroll
+                for (int i = 0; i < R; ++i) {
+                  const uint32_t bits = __ballot_sync(0xffffffffu, out[j][i] != 0.f && co0 + lane < p.Co);
+                  if (lane == i) mine = bits;
+                }
+                if (lane < nvalid)
+                  p.mask_out[((img * p.Ho + orow + b) * p.Wo + seg0 + lane) * (size_t)(2 * p.nw_out) + co0 / 32] = mine;
+              }
+            }
+          }
           if (p.tma_store) {
             // Tile [32*CPL channels][R pixels] through this warp's staging
             // slot; one TMA tensor store writes it (clipped at the edges).
@@ -693,62 +720,65 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (p.tma_store && lane == 0) bulk_wait_group0();  // stores complete before the CTA leaves
 }
 
-template <int K, int S, int CPL, int R, int B, typename XT, typename WT, bool LIF, bool WSMEM>
+template <int K, int S, int CPL, int R, int B, typename XT, typename WT, int MODE, bool WSMEM>
 sf_status launch_conv(const ConvParams& p, const CUtensorMap& ymap, int grid, int smem, cudaStream_t st) {
-  auto kern = sparse_conv_kernel<K, S, CPL, R, B, XT, WT, LIF, WSMEM>;
+  auto kern = sparse_conv_kernel<K, S, CPL, R, B, XT, WT, MODE, WSMEM>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return SF_ERR_CUDA;
   kern<<<grid, kThreads, smem, st>>>(p, ymap);
   return cudaGetLastError() == cudaSuccess ? SF_OK : SF_ERR_CUDA;
 }
 
-template <int K, int S, typename XT, typename WT, bool LIF, bool WSMEM>
+template <int K, int S, typename XT, typename WT, int MODE, bool WSMEM>
 sf_status dispatch_cpl(const ConvParams& p, const CUtensorMap& ym, int grid, const Plan& pl, cudaStream_t st) {
-  constexpr int B = LIF ? 1 : kRowsPerWarp;  // output rows per warp
-  if (pl.CPL == 1) return launch_conv<K, S, 1, 8, B, XT, WT, LIF, WSMEM>(p, ym, grid, pl.smem, st);
-  if (pl.CPL == 2) return launch_conv<K, S, 2, 8, B, XT, WT, LIF, WSMEM>(p, ym, grid, pl.smem, st);
-  return launch_conv<K, S, 4, 4, B, XT, WT, LIF, WSMEM>(p, ym, grid, pl.smem, st);
+  constexpr int B = MODE >= 1 ? 1 : kRowsPerWarp;  // output rows per warp
+  if (pl.CPL == 1) return launch_conv<K, S, 1, 8, B, XT, WT, MODE, WSMEM>(p, ym, grid, pl.smem, st);
+  if (pl.CPL == 2) return launch_conv<K, S, 2, 8, B, XT, WT, MODE, WSMEM>(p, ym, grid, pl.smem, st);
+  return launch_conv<K, S, 4, 4, B, XT, WT, MODE, WSMEM>(p, ym, grid, pl.smem, st);
 }
 
-template <typename XT, typename WT, bool LIF, bool WSMEM>
+template <typename XT, typename WT, int MODE, bool WSMEM>
 sf_status dispatch_geom(int K, int S, const ConvParams& p, const CUtensorMap& ym, int grid, const Plan& pl,
                         cudaStream_t st) {
-  if (K == 3 && S == 1) return dispatch_cpl<3, 1, XT, WT, LIF, WSMEM>(p, ym, grid, pl, st);
-  if constexpr (!LIF) {
-    if (K == 3 && S == 2) return dispatch_cpl<3, 2, XT, WT, LIF, WSMEM>(p, ym, grid, pl, st);
+  if (K == 3 && S == 1) return dispatch_cpl<3, 1, XT, WT, MODE, WSMEM>(p, ym, grid, pl, st);
+  if constexpr (MODE == 0) {
+    if (K == 3 && S == 2) return dispatch_cpl<3, 2, XT, WT, MODE, WSMEM>(p, ym, grid, pl, st);
   }
-  if (K == 1 && S == 1) return dispatch_cpl<1, 1, XT, WT, LIF, WSMEM>(p, ym, grid, pl, st);
+  if (K == 1 && S == 1) return dispatch_cpl<1, 1, XT, WT, MODE, WSMEM>(p, ym, grid, pl, st);
   return SF_ERR_UNSUPPORTED;
 }
 
-// Per input dtype: launches the kernel instantiation matching (LIF, weight
+// Per input dtype: launches the kernel instantiation matching (mode, weight
 // dtype, weights in shared memory, kernel/stride, slices per lane). Defined
 // in conv_<dtype>.cu.
-sf_status dispatch_f32(bool lif, int wdt, int K, int S, const ConvParams& p, const CUtensorMap& ym, int grid,
+sf_status dispatch_f32(int mode, int wdt, int K, int S, const ConvParams& p, const CUtensorMap& ym, int grid,
                        const Plan& pl, cudaStream_t st);
-sf_status dispatch_f16(bool lif, int wdt, int K, int S, const ConvParams& p, const CUtensorMap& ym, int grid,
+sf_status dispatch_f16(int mode, int wdt, int K, int S, const ConvParams& p, const CUtensorMap& ym, int grid,
                        const Plan& pl, cudaStream_t st);
-sf_status dispatch_bf16(bool lif, int wdt, int K, int S, const ConvParams& p, const CUtensorMap& ym, int grid,
+sf_status dispatch_bf16(int mode, int wdt, int K, int S, const ConvParams& p, const CUtensorMap& ym, int grid,
                         const Plan& pl, cudaStream_t st);
 
-template <typename XT, typename WT, bool LIF>
+template <typename XT, typename WT, int MODE>
 sf_status dispatch_ws(int K, int S, const ConvParams& p, const CUtensorMap& ym, int grid, const Plan& pl,
                       cudaStream_t st) {
-  if (pl.wsmem) return dispatch_geom<XT, WT, LIF, true>(K, S, p, ym, grid, pl, st);
-  return dispatch_geom<XT, WT, LIF, false>(K, S, p, ym, grid, pl, st);
+  if (pl.wsmem) return dispatch_geom<XT, WT, MODE, true>(K, S, p, ym, grid, pl, st);
+  return dispatch_geom<XT, WT, MODE, false>(K, S, p, ym, grid, pl, st);
 }
 
 template <typename XT>
-sf_status dispatch_x(bool lif, int wdt, int K, int S, const ConvParams& p, const CUtensorMap& ym, int grid,
+sf_status dispatch_x(int mode, int wdt, int K, int S, const ConvParams& p, const CUtensorMap& ym, int grid,
                      const Plan& pl, cudaStream_t st) {
-  if (lif) {
-    if (wdt == SF_DTYPE_F32) return dispatch_ws<XT, float, true>(K, S, p, ym, grid, pl, st);
-    if (wdt == SF_DTYPE_BF16) return dispatch_ws<XT, __nv_bfloat16, true>(K, S, p, ym, grid, pl, st);
-  } else {
-    if (wdt == SF_DTYPE_F32) return dispatch_ws<XT, float, false>(K, S, p, ym, grid, pl, st);
-    if (wdt == SF_DTYPE_BF16) return dispatch_ws<XT, __nv_bfloat16, false>(K, S, p, ym, grid, pl, st);
+  if (wdt != SF_DTYPE_F32 && wdt != SF_DTYPE_BF16) return SF_ERR_UNSUPPORTED;
+  const bool f32 = wdt == SF_DTYPE_F32;
+  switch (mode) {
+    case 0: return f32 ? dispatch_ws<XT, float, 0>(K, S, p, ym, grid, pl, st)
+                       : dispatch_ws<XT, __nv_bfloat16, 0>(K, S, p, ym, grid, pl, st);
+    case 1: return f32 ? dispatch_ws<XT, float, 1>(K, S, p, ym, grid, pl, st)
+                       : dispatch_ws<XT, __nv_bfloat16, 1>(K, S, p, ym, grid, pl, st);
+    case 2: return f32 ? dispatch_ws<XT, float, 2>(K, S, p, ym, grid, pl, st)
+                       : dispatch_ws<XT, __nv_bfloat16, 2>(K, S, p, ym, grid, pl, st);
   }
-  return SF_ERR_UNSUPPORTED;
+  return SF_ERR_INVALID_ARG;
 }
 
 }  // namespace conv

@@ -18,6 +18,10 @@ namespace {
 // Set when a bounded wait in the conv kernel runs out (read by
 // sf_sparse_conv2d_status); a static device word, so no allocation is needed.
 __device__ uint32_t g_conv_error = 0;
+// All-binary flags for convolutions whose events come from a fused conv + LIF
+// (spikes are 0/1 by construction); zero-initialised when the module loads.
+constexpr int kZeroFlags = 65536;
+__device__ uint32_t g_zero_flags[kZeroFlags];
 
 // [co][ci][kk] (any dtype) -> [block][ci][kk][32][cpl] (fp32 or bf16), zero padded.
 template <typename WT>
@@ -132,11 +136,11 @@ int num_sms_current_device() {
 namespace conv {
 namespace {
 
-sf_status dispatch(bool lif, int xdt, int wdt, int K, int S, const ConvParams& p, const CUtensorMap& ym, int grid,
+sf_status dispatch(int mode, int xdt, int wdt, int K, int S, const ConvParams& p, const CUtensorMap& ym, int grid,
                    const Plan& pl, cudaStream_t st) {
-  if (xdt == SF_DTYPE_F32) return dispatch_f32(lif, wdt, K, S, p, ym, grid, pl, st);
-  if (xdt == SF_DTYPE_F16) return dispatch_f16(lif, wdt, K, S, p, ym, grid, pl, st);
-  if (xdt == SF_DTYPE_BF16) return dispatch_bf16(lif, wdt, K, S, p, ym, grid, pl, st);
+  if (xdt == SF_DTYPE_F32) return dispatch_f32(mode, wdt, K, S, p, ym, grid, pl, st);
+  if (xdt == SF_DTYPE_F16) return dispatch_f16(mode, wdt, K, S, p, ym, grid, pl, st);
+  if (xdt == SF_DTYPE_BF16) return dispatch_bf16(mode, wdt, K, S, p, ym, grid, pl, st);
   return SF_ERR_UNSUPPORTED;
 }
 
@@ -184,19 +188,22 @@ sf_status check_geometry(int T, int N, int C, int H, int W, int Co, int Ho, int 
 }
 
 // Stage 1 + stage 2 for T*N images; the LIF variant when lif is set.
+// masks_in: events of x precomputed by a fused conv + LIF (binary spikes;
+// x itself is then not read). mask_out: LIF only, the output spikes' events.
 sf_status run_conv(const void* x, const void* w_packed, const float* bias, void* y, float* v, int T, int N, int C,
                    int H, int W, int Co, int Ho, int Wo, int K, int S, int P, int xdt, int wdt, bool lif,
-                   const sf_lif_desc* lifd, void* workspace, size_t ws_bytes, cudaStream_t st) {
+                   const sf_lif_desc* lifd, void* workspace, size_t ws_bytes, cudaStream_t st,
+                   const unsigned long long* masks_in = nullptr, uint32_t* mask_out = nullptr) {
   sf_status s = check_geometry(T, N, C, H, W, Co, Ho, Wo, K, S, P, xdt, wdt);
   if (s != SF_OK) return s;
-  if (!x || !w_packed || !y) return SF_ERR_INVALID_ARG;
-  if (!workspace) return SF_ERR_WORKSPACE;
+  if ((!x && !masks_in) || !w_packed || !y) return SF_ERR_INVALID_ARG;
+  if (!workspace && !masks_in) return SF_ERR_WORKSPACE;
   if (!aligned16(w_packed)) return SF_ERR_ALIGNMENT;
   // 1x1 stride 2: one pass over x with masks built in shared memory
   // (pointwise.cu). For stride 1 that kernel measured slower than the two
   // stages (0.74 vs 0.54 ms on the C2 cell; both issue-bound), so it runs
   // only when SF_CONV_PW=1 asks for it.
-  if (!lif && K == 1 && (S == 2 || env_int("SF_CONV_PW") == 1)) {
+  if (!lif && !masks_in && K == 1 && (S == 2 || env_int("SF_CONV_PW") == 1)) {
     s = pw::run_pointwise(x, w_packed, bias, y, T * N, C, H, W, Co, Ho, Wo, S, xdt, wdt, st);
     if (s != SF_ERR_UNSUPPORTED) return s;
   }
@@ -208,8 +215,20 @@ sf_status run_conv(const void* x, const void* w_packed, const float* bias, void*
     return SF_ERR_UNSUPPORTED;
 
   EventBuffers ev;
-  s = extract_events(x, xdt, (long long)T * N, C, H * W, workspace, ws_bytes, ev, st);
-  if (s != SF_OK) return s;
+  if (masks_in) {
+    if ((long long)T * N > kZeroFlags) return SF_ERR_UNSUPPORTED;
+    ev.masks = const_cast<unsigned long long*>(masks_in);
+    ev.nw = nw;
+    if (cudaGetSymbolAddress(reinterpret_cast<void**>(&ev.flags), g_zero_flags) != cudaSuccess) return SF_ERR_CUDA;
+  } else {
+    s = extract_events(x, xdt, (long long)T * N, C, H * W, workspace, ws_bytes, ev, st);
+    if (s != SF_OK) return s;
+  }
+  if (mask_out && Co % 64 != 0) {
+    // Halves past C_out are never written by the kernel.
+    const size_t mbytes = (size_t)T * N * Ho * Wo * ((Co + 63) / 64) * 8;
+    if (cudaMemsetAsync(mask_out, 0, mbytes, st) != cudaSuccess) return SF_ERR_CUDA;
+  }
 
   ConvParams p;
   memset(&p, 0, sizeof(p));
@@ -221,6 +240,8 @@ sf_status run_conv(const void* x, const void* w_packed, const float* bias, void*
   if (cudaGetSymbolAddress(reinterpret_cast<void**>(&p.err), g_conv_error) != cudaSuccess) return SF_ERR_CUDA;
   p.masks = ev.masks;
   p.flags = ev.flags;
+  p.mask_out = mask_out;
+  p.nw_out = (Co + 63) / 64;
   p.nw = nw;
   p.tau = 1.f;
   p.vth = 1.f;
@@ -261,7 +282,7 @@ sf_status run_conv(const void* x, const void* w_packed, const float* bias, void*
     if (s != SF_OK) return s;
   }
   const int grid_used = (p.n_units + p.units_per_cta - 1) / p.units_per_cta;
-  return dispatch(lif, xdt, wdt, K, S, p, ym, grid_used, pl, st);
+  return dispatch(lif ? (mask_out ? 2 : 1) : 0, xdt, wdt, K, S, p, ym, grid_used, pl, st);
 }
 
 }  // namespace
@@ -319,15 +340,33 @@ extern "C" size_t sf_fused_conv_lif_workspace_size(const sf_lif_desc* d) {
 }
 
 extern "C" sf_status sf_fused_conv_lif(const void* x, const void* w_packed, const float* bias, float* v_inout,
-                                       void* spikes_out, const sf_lif_desc* d, void* workspace,
-                                       size_t workspace_bytes, void* stream) {
+                                       void* spikes_out, void* spike_masks_out, const sf_lif_desc* d,
+                                       void* workspace, size_t workspace_bytes, void* stream) {
   if (!d || !v_inout) return SF_ERR_INVALID_ARG;
   if (d->has_bias && !bias) return SF_ERR_INVALID_ARG;
   if (!(d->tau > 0.f)) return SF_ERR_INVALID_ARG;
   if (d->kernel == 3 && d->stride != 1) return SF_ERR_UNSUPPORTED;
+  if (spike_masks_out && (reinterpret_cast<uintptr_t>(spike_masks_out) & 7u) != 0) return SF_ERR_ALIGNMENT;
   return run_conv(x, w_packed, d->has_bias ? bias : nullptr, spikes_out, v_inout, d->t_steps, d->n, d->c_in, d->h,
                   d->w, d->c_out, d->h_out, d->w_out, d->kernel, d->stride, d->padding, d->x_dtype, d->w_dtype, true,
-                  d, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+                  d, workspace, workspace_bytes, static_cast<cudaStream_t>(stream), nullptr,
+                  static_cast<uint32_t*>(spike_masks_out));
+}
+
+extern "C" size_t sf_event_masks_bytes(int64_t n_images, int32_t channels, int32_t h, int32_t w) {
+  if (n_images <= 0 || channels <= 0 || h <= 0 || w <= 0) return 0;
+  return (size_t)n_images * h * w * ((channels + 63) / 64) * 8;
+}
+
+extern "C" sf_status sf_sparse_conv2d_from_masks(const void* event_masks, const void* w_packed, const float* bias,
+                                                 void* y, const sf_conv_desc* d, void* stream) {
+  if (!d || !event_masks) return SF_ERR_INVALID_ARG;
+  if (d->has_bias && !bias) return SF_ERR_INVALID_ARG;
+  if ((reinterpret_cast<uintptr_t>(event_masks) & 15u) != 0) return SF_ERR_ALIGNMENT;
+  return run_conv(nullptr, w_packed, d->has_bias ? bias : nullptr, y, nullptr, 1, d->n, d->c_in, d->h, d->w,
+                  d->c_out, d->h_out, d->w_out, d->kernel, d->stride, d->padding, d->x_dtype, d->w_dtype, false,
+                  nullptr, nullptr, 0, static_cast<cudaStream_t>(stream),
+                  static_cast<const unsigned long long*>(event_masks));
 }
 
 extern "C" sf_status sf_sparse_conv2d_status(void* stream) {

@@ -1,0 +1,83 @@
+"""Fused conv + LIF emits the next layer's event masks; a following SparseConv2d runs from them."""
+import pytest
+import torch
+import torch.nn as nn
+
+pytestmark = pytest.mark.gpu
+
+
+def _masks_from_spikes(s4):
+    """[N, C, H, W] -> int64 [N, H, W, ceil(C/64)] with bit c%64 of word c//64 = (s != 0)."""
+    n, c, h, w = s4.shape
+    nw = (c + 63) // 64
+    pad = torch.zeros(n, nw * 64, h, w, dtype=torch.bool, device=s4.device)
+    pad[:, :c] = s4 != 0
+    bits = pad.reshape(n, nw, 64, h, w).permute(0, 3, 4, 1, 2).to(torch.int64)
+    weights = torch.ones(64, dtype=torch.int64, device=s4.device) << torch.arange(64, device=s4.device)
+    return (bits * weights).sum(-1)  # wraps into int64 like the kernel's uint64 words
+
+
+def _fused(c_in, c_out, k, seed):
+    from sparseflow_b200.Ops.sparse_fused_conv_lif import FusedSparseConvLIF
+    from sparseflow_b200.Ops.lif_node import LIFNode
+    g = torch.Generator().manual_seed(seed)
+    conv = nn.Conv2d(c_in, c_out, k, 1, k // 2, bias=True)
+    conv.weight.data = torch.randn(c_out, c_in, k, k, generator=g) * (3.0 / (c_in * k * k)) ** 0.5
+    conv.bias.data = torch.randn(c_out, generator=g) * 0.3
+    m = FusedSparseConvLIF.from_conv_and_lif(conv.cuda(), LIFNode(tau=2.0, v_threshold=0.5, v_reset=0.0))
+    m.emit_event_masks = True
+    return m
+
+
+@pytest.mark.parametrize("c_in,c_out,k", [(64, 64, 3), (32, 40, 3), (48, 130, 1)])
+def test_fused_lif_masks_match_spikes(c_in, c_out, k):
+    g = torch.Generator().manual_seed(c_out)
+    x = (torch.rand(4, 3, c_in, 14, 15, generator=g) < 0.2).float().cuda()
+    m = _fused(c_in, c_out, k, 7)
+    s = m(x)
+    masks = s._sf_event_masks[0]
+    want = _masks_from_spikes(s.reshape(12, c_out, 14, 15))
+    assert float(s.mean()) > 0.01  # the layer does fire
+    assert torch.equal(masks.reshape(want.shape), want)
+
+
+@pytest.mark.parametrize("c_mid,k2", [(64, 3), (40, 3), (72, 1)])
+def test_next_conv_runs_from_masks(c_mid, k2):
+    from sparseflow_b200.Ops.sparse_conv2d import SparseConv2d
+    g = torch.Generator().manual_seed(c_mid + k2)
+    x = (torch.rand(4, 2, 32, 12, 12, generator=g) < 0.1).float().cuda()
+    first = _fused(32, c_mid, 3, 9)
+    conv2 = nn.Conv2d(c_mid, 48, k2, 1, k2 // 2)
+    conv2.weight.data = torch.randn(48, c_mid, k2, k2, generator=g) * 0.1
+    second = SparseConv2d.from_dense(conv2.cuda())
+    s = first(x)
+    y_masks = second(s)
+    assert second._last_used_event_masks
+    y_plain = second(s.clone())  # a new tensor: no masks attached, mask pass runs
+    assert not second._last_used_event_masks
+    torch.testing.assert_close(y_masks, y_plain, rtol=0, atol=0)
+
+
+def test_stale_masks_are_not_used():
+    from sparseflow_b200.Ops.sparse_conv2d import SparseConv2d
+    x = (torch.rand(2, 2, 32, 10, 10) < 0.2).float().cuda()
+    first = _fused(32, 32, 3, 3)
+    conv2 = nn.Conv2d(32, 16, 3, 1, 1).cuda()
+    second = SparseConv2d.from_dense(conv2)
+    s = first(x)
+    s.zero_()  # in place: the attached masks no longer describe s
+    y = second(s)
+    assert not second._last_used_event_masks
+    torch.testing.assert_close(y, conv2.bias.detach().view(1, 1, 16, 1, 1).expand_as(y), rtol=0, atol=1e-6)
+
+
+def test_masks_off_by_default_and_plain_lif_unchanged():
+    """Without emission the spikes carry no masks and equal the emitting kernel's spikes."""
+    x = (torch.rand(3, 2, 32, 9, 11) < 0.2).float().cuda()
+    a = _fused(32, 48, 3, 5)
+    b = _fused(32, 48, 3, 5)
+    b.emit_event_masks = False
+    sa, sb = a(x), b(x)
+    assert not hasattr(sb, "_sf_event_masks")
+    torch.testing.assert_close(sa, sb, rtol=0, atol=0)
+    torch.testing.assert_close(a.v, b.v, rtol=0, atol=0)
