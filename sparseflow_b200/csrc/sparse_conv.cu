@@ -8,6 +8,10 @@
 #include "events.cuh"
 
 namespace sf {
+namespace pwtc {
+sf_status run_pointwise_tc(const void* x, const void* w_packed, const float* bias, void* y, uint32_t* err, int N,
+                           int C, int H, int W, int Co, int xdt, int wdt, cudaStream_t st);
+}  // namespace pwtc
 namespace pw {
 sf_status run_pointwise(const void* x, const void* w_packed, const float* bias, void* y, int N, int C, int H,
                         int W, int Co, int Ho, int Wo, int S, int xdt, int wdt, cudaStream_t st);
@@ -199,6 +203,13 @@ sf_status run_conv(const void* x, const void* w_packed, const float* bias, void*
   if ((!x && !masks_in) || !w_packed || !y) return SF_ERR_INVALID_ARG;
   if (!workspace && !masks_in) return SF_ERR_WORKSPACE;
   if (!aligned16(w_packed)) return SF_ERR_ALIGNMENT;
+  // 1x1 stride 1: tcgen05 GEMM tiles over x streamed once (pointwise_tc.cu).
+  if (!lif && !masks_in && K == 1 && S == 1 && P == 0 && env_int("SF_CONV_TC_OFF") == 0) {
+    uint32_t* err = nullptr;
+    if (cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_conv_error) != cudaSuccess) return SF_ERR_CUDA;
+    s = pwtc::run_pointwise_tc(x, w_packed, bias, y, err, T * N, C, H, W, Co, xdt, wdt, st);
+    if (s != SF_ERR_UNSUPPORTED) return s;
+  }
   // 1x1 stride 2: one pass over x with masks built in shared memory
   // (pointwise.cu). For stride 1 that kernel measured slower than the two
   // stages (0.74 vs 0.54 ms on the C2 cell; both issue-bound), so it runs
