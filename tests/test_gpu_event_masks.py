@@ -55,7 +55,10 @@ def test_next_conv_runs_from_masks(c_mid, k2):
     assert second._last_used_event_masks
     y_plain = second(s.clone())  # a new tensor: no masks attached, mask pass runs
     assert not second._last_used_event_masks
-    torch.testing.assert_close(y_masks, y_plain, rtol=0, atol=0)
+    if k2 == 3:  # both runs use the same gather kernel: bit-identical
+        torch.testing.assert_close(y_masks, y_plain, rtol=0, atol=0)
+    else:  # 1x1 without masks takes the tensor-core kernel: same sums, another order
+        torch.testing.assert_close(y_masks, y_plain, rtol=1e-5, atol=1e-6)
 
 
 def test_stale_masks_are_not_used():
