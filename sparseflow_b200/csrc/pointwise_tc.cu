@@ -26,11 +26,13 @@
 //              tcgen05.mma kind::f16 for each nonzero chunk and commits to
 //              the mbarriers that free the A slot and hand D over.
 //
-// Exactness: A holds 0/1 (exact in bf16); the B operand is the weights split
-// into bf16 planes w = hi + mid + lo (one plane for bf16 weights), so every
-// product is exact and the fp32 accumulation matches the fp32 reference to
-// a few ulp. A tile holding any other value is computed on the CUDA cores
-// instead (fp32 FMAs in ascending channel order) and its D is discarded.
+// Exactness: the B operand is the weights split into bf16 planes
+// w = hi + mid + lo (one plane for bf16 weights), and A holds x in bf16; when
+// every x of a tile is exactly a bf16 (spikes 0/1 are; so are small integers
+// and powers of two) every product is exact and the fp32 accumulation
+// matches the fp32 reference to a few ulp. A tile holding any other value is
+// computed on the CUDA cores instead (fp32 FMAs in ascending channel order)
+// and its D is discarded.
 //
 // Every mbarrier wait gives up after one second of wall time (the error word
 // is set and the CTA drains); TMA loads without multicast; TMEM is released
@@ -148,7 +150,7 @@ struct Bars {
   uint64_t d_full[2], d_empty[2];
   uint32_t tmem_base;
   uint32_t a_nz[kASlots][kConvWarps];  // per converter warp: its part of the chunk has a nonzero
-  uint32_t odd[2];                      // tile in D[b] holds a value other than 0 / 1
+  uint32_t odd[2];                      // tile in D[b] holds a value that is not exactly a bf16
 };
 
 template <typename XT, typename WT>
@@ -370,20 +372,26 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int e = 0; e < 8; ++e) v[k][e] = DT<XT>::to_f(st[(o * 8 + e) * kM + phalf * 64 + k * 32 + lane]);
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars->s_empty[s]);
+        // The MMA is exact whenever every x is exactly a bf16 (then each
+        // product with a bf16 weight plane is exact in fp32): for the fp32
+        // bits u that means u & 0xffff == 0, tested on the OR of all values,
+        // which also gives "any nonzero". Such values convert by taking the
+        // high halves (a byte permute).
+        uint32_t orall = 0u;
 #pragma unroll
         for (int k = 0; k < kPP; ++k) {
           uint4 qv;
           uint32_t* qq = &qv.x;
 #pragma unroll
           for (int e = 0; e < 8; e += 2) {
-            nz |= (v[k][e] != 0.f) | (v[k][e + 1] != 0.f);
-            odd |= (v[k][e] != 0.f && v[k][e] != 1.f) | (v[k][e + 1] != 0.f && v[k][e + 1] != 1.f);
-            qq[e / 2] = pack_bf16x2(v[k][e], v[k][e + 1]);
+            const uint32_t u0 = __float_as_uint(v[k][e]), u1 = __float_as_uint(v[k][e + 1]);
+            orall |= u0 | u1;
+            qq[e / 2] = __byte_perm(u0, u1, 0x7632);
           }
           *reinterpret_cast<uint4*>(ab + sw128(phalf * 64 + k * 32 + lane, o * 8, kM)) = qv;
         }
-        nz = __any_sync(0xffffffffu, nz != 0u);
-        odd = __any_sync(0xffffffffu, odd != 0u);
+        nz = __any_sync(0xffffffffu, (orall & 0x7fffffffu) != 0u);
+        odd = __any_sync(0xffffffffu, (orall & 0xffffu) != 0u);
         if (lane == 0) {
           bars->a_nz[a][warp] = nz;
           if (odd) atomicOr(&bars->odd[b], 1u);

@@ -173,3 +173,19 @@ def test_conv1x1_one_pass_matches_two_stage(monkeypatch, s):
         monkeypatch.delenv("SF_CONV_PW")
         y3, _ = sparse_conv2d_forward(x, wt, None, kernel_size=1, stride=2, padding=0)
         torch.testing.assert_close(y3, y1[:, :, ::2, ::2], rtol=1e-6, atol=1e-6)
+
+
+@pytest.mark.parametrize("wdt", [torch.float32, torch.bfloat16])
+def test_conv1x1_bf16_exact_values_on_tensor_cores(wdt):
+    """Small integers and powers of two are exact in bf16, so the tensor-core 1x1 path keeps
+    them (not only 0/1 spikes); real values in other images take the exact CUDA-core path."""
+    from sparseflow_b200.Kernels.conv2d import sparse_conv2d_forward
+    g = torch.Generator().manual_seed(23)
+    x = torch.randint(-3, 4, (3, 96, 24, 24), generator=g).float() * (torch.rand(3, 96, 24, 24, generator=g) < 0.1)
+    x[1] *= 0.25                                   # powers of two stay exact
+    x[2] = torch.randn(96, 24, 24, generator=g) * (torch.rand(96, 24, 24, generator=g) < 0.1)
+    wt = (torch.randn(80, 96, 1, 1, generator=g) * 0.1).to(wdt)
+    b = torch.randn(80, generator=g) * 0.1
+    y, _ = sparse_conv2d_forward(x.cuda(), wt.cuda(), b.cuda(), kernel_size=1, stride=1, padding=0)
+    ref = oracle.conv2d(x.numpy(), wt.float().numpy(), b.numpy(), 1, 0)
+    _assert_close(y.cpu().numpy(), ref)
