@@ -54,7 +54,8 @@ constexpr int kThreads = (kMmaWarp + 1) * 32;
 constexpr int kM = 128;       // pixels per tile = MMA M = TMEM lanes
 constexpr int kKC = 64;       // channels per chunk (one 128-byte swizzle row of bf16)
 constexpr int kMaxStages = 6; // staging ring (as many as shared memory allows)
-constexpr int kASlots = 2;    // bf16 A ring
+constexpr int kASlots = 4;    // bf16 A ring
+constexpr int kMaxD = 4;      // TMEM accumulators (as many as 512 columns hold)
 
 struct TcParams {
   const void* x;
@@ -63,7 +64,7 @@ struct TcParams {
   void* y;
   uint32_t* err;
   int N, C, HW, Co;
-  int Kpad, Npad, nplanes, nchunks, nstages;
+  int Kpad, Npad, nplanes, nchunks, nstages, nd;
   int cpl;
   int tiles_per_img;
   long long ntiles, tiles_per_cta;
@@ -147,10 +148,10 @@ __device__ __forceinline__ float packed_w(const TcParams& p, int co, int ci) {
 struct Bars {
   uint64_t s_full[kMaxStages], s_empty[kMaxStages];
   uint64_t a_full[kASlots], a_empty[kASlots];
-  uint64_t d_full[2], d_empty[2];
+  uint64_t d_full[kMaxD], d_empty[kMaxD];
   uint32_t tmem_base;
   uint32_t a_nz[kASlots][kConvWarps];  // per converter warp: its part of the chunk has a nonzero
-  uint32_t odd[2];                      // tile in D[b] holds a value that is not exactly a bf16
+  uint32_t odd[kMaxD];                  // tile in D[b] holds a value that is not exactly a bf16
 };
 
 template <typename XT, typename WT>
@@ -179,7 +180,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars->a_full[a], kConvWarps);
       mbar_init(&bars->a_empty[a], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < p.nd; ++b) {
       mbar_init(&bars->d_full[b], 1);
       mbar_init(&bars->d_empty[b], kEpiWarps);
       bars->odd[b] = 0u;
@@ -246,8 +247,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t idesc = idesc_bf16(kM, p.Npad);
       const uint32_t bsa = smem_u32(bbuf);
       for (int i = 0; i < nt && !failed; ++i) {
-        const int b = i & 1;
-        if (i >= 2 && !mbar_wait_ns(&bars->d_empty[b], (uint32_t)(((i >> 1) - 1) & 1))) {
+        const int b = i % p.nd;
+        if (i >= p.nd && !mbar_wait_ns(&bars->d_empty[b], (uint32_t)(((i / p.nd) - 1) & 1))) {
           failed = true;
           break;
         }
@@ -288,11 +289,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Epilogue warps 16-23: warp w reads TMEM lane quarter w % 4 (its pixels)
     // and one half of the columns (output channels).
     auto epilogue = [&](int i) {
-      const int b = i & 1;
+      const int b = i % p.nd;
       const long long tile = t0 + i;
       const int img = (int)(tile / p.tiles_per_img);
       const int px0 = (int)(tile - (long long)img * p.tiles_per_img) * kM;
-      if (!mbar_wait_ns(&bars->d_full[b], (uint32_t)((i >> 1) & 1))) {
+      if (!mbar_wait_ns(&bars->d_full[b], (uint32_t)((i / p.nd) & 1))) {
         failed = true;
         return;
       }
@@ -340,11 +341,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     // half w / 8.
     const int o = warp & 7, phalf = warp >> 3;
     for (int i = 0; i < nt; ++i) {
-      const int b = i & 1;
-      // odd[b] was last read by tile i-2's epilogue: wait until that epilogue
+      const int b = i % p.nd;
+      // odd[b] was last read by tile i-nd's epilogue: wait until that epilogue
       // released D[b], then clear it. A timed-out wait skips work but never a
       // barrier.
-      if (!failed && i >= 2 && !mbar_wait_ns(&bars->d_empty[b], (uint32_t)(((i >> 1) - 1) & 1))) failed = true;
+      if (!failed && i >= p.nd && !mbar_wait_ns(&bars->d_empty[b], (uint32_t)(((i / p.nd) - 1) & 1)))
+        failed = true;
       asm volatile("bar.sync 1, %0;" ::"r"(kConvWarps * 32) : "memory");
       if (tid == 0) bars->odd[b] = 0u;
       asm volatile("bar.sync 1, %0;" ::"r"(kConvWarps * 32) : "memory");
@@ -480,8 +482,9 @@ sf_status run_pointwise_tc(const void* x, const void* w_packed, const float* bia
   p.stage_bytes = (uint32_t)(kKC * kM * esz);
   p.a_bytes = (uint32_t)(kM * kKC * 2);
   p.b_plane_bytes = (uint32_t)(p.Npad * p.Kpad * 2);
+  p.nd = std::max(2, std::min(kMaxD, 512 / p.Npad));
   uint32_t cols = 32;
-  while (cols < (uint32_t)(2 * p.Npad)) cols <<= 1;
+  while (cols < (uint32_t)(p.nd * p.Npad)) cols <<= 1;
   p.tmem_cols = cols;
   const size_t fixed = 1024 + kASlots * (size_t)p.a_bytes + (size_t)p.nplanes * p.b_plane_bytes + sizeof(Bars);
   if (fixed + 2 * (size_t)p.stage_bytes > 232448) return SF_ERR_UNSUPPORTED;
