@@ -57,8 +57,9 @@ def parse():
     ap.add_argument("--no-extra", action="store_true", help="skip the C2/C3/prescan side measurements")
     ap.add_argument("--only-timed", action="store_true",
                     help="run only the warm-up and timed steps (no cuDNN, e2e, extras or CPU baseline); for ncu")
-    ap.add_argument("--kernel", choices=["conv", "prescan"], default="conv",
-                    help="with --only-timed: time the sparse conv (default) or the prescan on the same input")
+    ap.add_argument("--kernel", choices=["conv", "prescan", "c2"], default="conv",
+                    help="with --only-timed: time the sparse conv (default), the prescan on the same input, "
+                         "or the C2 1x1 cell (--images = T*N of C2, default 512)")
     ap.add_argument("--sweep", action="store_true",
                     help="C5 grid: C x H x density, sparse conv3x3 vs cuDNN and the HBM roofline (one JSON line per cell)")
     ap.add_argument("--sweep-images", type=int, default=T_STEPS * N_BATCH,
@@ -399,6 +400,28 @@ def main():
     mod = SparseConv2d.from_dense(conv, block_size=16)
     mod.set_inference_mode(True)
     step_bytes = conv_bytes(n_img, C, H, W, C, H, W, 3)
+
+    if args.only_timed and args.kernel == "c2":
+        from sparseflow_b200.Ops.sparse_conv2d import SparseConv2d
+        n2 = args.images if args.images != T_STEPS * N_BATCH else 512
+        g2 = torch.Generator(device=dev).manual_seed(17 + rank)
+        blk = (torch.rand(n2, 256, 4, 4, device=dev, generator=g2) < 0.05).float()
+        mask = blk.repeat_interleave(16, 2).repeat_interleave(16, 3)[:, :, :56, :56]
+        x2 = (mask * (torch.rand(n2, 256, 56, 56, device=dev, generator=g2) < 0.3).float()).contiguous()
+        del blk, mask
+        conv2 = nn.Conv2d(256, 64, 1, bias=False)
+        conv2.weight.data = torch.randn(64, 256, 1, 1, generator=torch.Generator().manual_seed(2)) * 0.02
+        m2 = SparseConv2d.from_dense(conv2.to(dev).to(torch.bfloat16), block_size=16)
+        m2.set_inference_mode(True)
+        with torch.no_grad():
+            ms = cuda_time(lambda: m2(x2), args.steps, args.warmup, dist) / args.steps
+        b2 = conv_bytes(n2, 256, 56, 56, 64, 56, 56, 1, wsz=2, bias=False)
+        if rank == 0:
+            print(json.dumps({"kernel": "c2", "ms_per_step": round(ms, 4), "GBps": round(b2 / ms / 1e6, 1),
+                              "frac_of_measured_hbm": round(b2 / ms / 1e6 / hbm_peak, 3), "images": n2}))
+        if dist is not None:
+            dist.destroy_process_group()
+        return
 
     if args.only_timed and args.kernel == "prescan":
         from sparseflow_b200.Kernels._prescan_common import prescan2d
