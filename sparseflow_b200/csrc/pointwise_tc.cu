@@ -151,7 +151,7 @@ struct Bars {
   uint64_t d_full[kMaxD], d_empty[kMaxD];
   uint32_t tmem_base;
   uint32_t a_nz[kASlots][kConvWarps];  // per converter warp: its part of the chunk has a nonzero
-  uint32_t odd[kMaxD];                  // tile in D[b] holds a value that is not exactly a bf16
+  uint32_t odd[kMaxD];                  // = i + 1 when tile i (in D[b]) holds a value that is not exactly a bf16
 };
 
 template <typename XT, typename WT>
@@ -298,7 +298,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         return;
       }
       tc_fence_after();
-      const bool odd = bars->odd[b] != 0u;
+      const bool odd = bars->odd[b] == (uint32_t)(i + 1);
       const int ew = warp - kConvWarps;
       const int quarter = warp & 3;  // TMEM lane quarter this warp may read
       const int half = ew >> 2;      // column half
@@ -342,14 +342,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int o = warp & 7, phalf = warp >> 3;
     for (int i = 0; i < nt; ++i) {
       const int b = i % p.nd;
-      // odd[b] was last read by tile i-nd's epilogue: wait until that epilogue
-      // released D[b], then clear it. A timed-out wait skips work but never a
-      // barrier.
-      if (!failed && i >= p.nd && !mbar_wait_ns(&bars->d_empty[b], (uint32_t)(((i / p.nd) - 1) & 1)))
-        failed = true;
-      asm volatile("bar.sync 1, %0;" ::"r"(kConvWarps * 32) : "memory");
-      if (tid == 0) bars->odd[b] = 0u;
-      asm volatile("bar.sync 1, %0;" ::"r"(kConvWarps * 32) : "memory");
       for (int kc = 0; kc < KC && !failed; ++kc) {
         const int g = i * KC + kc, s = g % p.nstages, a = g % kASlots;
         if (!mbar_wait_ns(&bars->s_full[s], (uint32_t)((g / p.nstages) & 1))) {
@@ -396,7 +388,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         odd = __any_sync(0xffffffffu, (orall & 0xffffu) != 0u);
         if (lane == 0) {
           bars->a_nz[a][warp] = nz;
-          if (odd) atomicOr(&bars->odd[b], 1u);
+          if (odd) bars->odd[b] = (uint32_t)(i + 1);  // tagged with the tile: no clearing needed
         }
         fence_proxy_async_smem();
         __syncwarp();
