@@ -189,3 +189,20 @@ def test_conv1x1_bf16_exact_values_on_tensor_cores(wdt):
     y, _ = sparse_conv2d_forward(x.cuda(), wt.cuda(), b.cuda(), kernel_size=1, stride=1, padding=0)
     ref = oracle.conv2d(x.numpy(), wt.float().numpy(), b.numpy(), 1, 0)
     _assert_close(y.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("xdt", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("co", [48, 300])
+def test_conv1x1_16bit_inputs_vs_oracle(xdt, co):
+    """1x1 with 16-bit activations: the tensor-core kernel for C_out <= 256 (f16 values that are
+    not bf16-exact take its CUDA-core tiles), the gather kernels above."""
+    from sparseflow_b200.Kernels.conv2d import sparse_conv2d_forward
+    g = torch.Generator().manual_seed(co)
+    x = (torch.rand(3, 128, 20, 20, generator=g) < 0.05).float()
+    x[2] *= torch.randn(128, 20, 20, generator=g)  # one image with real values
+    x = x.to(xdt)
+    wt = torch.randn(co, 128, 1, 1, generator=g) * 0.1
+    y, _ = sparse_conv2d_forward(x.cuda(), wt.cuda(), None, kernel_size=1, stride=1, padding=0)
+    assert y.dtype == xdt
+    ref = oracle.conv2d(x.float().numpy(), wt.numpy(), None, 1, 0)
+    _assert_close(y.float().cpu().numpy(), ref, rtol=1e-2)
