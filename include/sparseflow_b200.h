@@ -221,6 +221,17 @@ typedef struct sf_lif_ms_desc {
 sf_status sf_lif_multistep(const void* x, float* v_inout, void* spikes_out, const sf_lif_ms_desc* d,
                            void* stream);
 
+/* ------------------------------------------------------------------------ */
+/* Diagnostics.                                                              */
+/* ------------------------------------------------------------------------ */
+/* Exercises the bounded-wait path every pipelined kernel here relies on: one
+ * thread waits on an mbarrier that nothing arrives on, gives up after
+ * limit_ns of wall time and records the timeout. Synchronous on `stream`.
+ * Returns SF_ERR_DEVICE_TIMEOUT when the wait expired as it should (and the
+ * context is still usable), SF_OK if the barrier completed (a bug), or
+ * SF_ERR_CUDA. No counterpart in the reference. */
+sf_status sf_selftest_bounded_wait(uint64_t limit_ns, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -105,6 +105,7 @@ _SIGNATURES = {
                                            _VP]),
     "sf_lif_multistep": (ctypes.c_int32, [_VP, _VP, _VP, ctypes.POINTER(LifMsDesc), _VP]),
     "sf_event_masks_bytes": (ctypes.c_size_t, [ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]),
+    "sf_selftest_bounded_wait": (ctypes.c_int32, [ctypes.c_uint64, _VP]),
     "sf_sparse_conv2d_from_masks": (ctypes.c_int32, [_VP, _VP, _VP, _VP, ctypes.POINTER(ConvDesc), _VP]),
 }
 

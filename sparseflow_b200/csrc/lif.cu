@@ -113,3 +113,32 @@ extern "C" sf_status sf_lif_multistep(const void* x, float* v_inout, void* spike
   }
   return SF_ERR_INVALID_ARG;
 }
+
+// ---------------------------------------------------------------------------
+// Bounded-wait self test (diagnostics): an mbarrier that never completes.
+// ---------------------------------------------------------------------------
+namespace sf {
+namespace {
+__global__ void bounded_wait_selftest_kernel(uint64_t limit_ns, uint32_t* out) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);  // one arrival expected; none is ever made
+    fence_mbar_init();
+    *out = mbar_wait_ns(&bar, 0u, limit_ns) ? 1u : 2u;  // 2: gave up, as it must
+  }
+}
+}  // namespace
+}  // namespace sf
+
+extern "C" sf_status sf_selftest_bounded_wait(uint64_t limit_ns, void* stream) {
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint32_t* d = nullptr;
+  uint32_t h = 0;
+  if (cudaMallocAsync(reinterpret_cast<void**>(&d), 4, st) != cudaSuccess) return SF_ERR_CUDA;
+  sf::bounded_wait_selftest_kernel<<<1, 32, 0, st>>>(limit_ns, d);
+  const bool ok = cudaGetLastError() == cudaSuccess &&
+                  cudaMemcpyAsync(&h, d, 4, cudaMemcpyDeviceToHost, st) == cudaSuccess &&
+                  cudaFreeAsync(d, st) == cudaSuccess && cudaStreamSynchronize(st) == cudaSuccess;
+  if (!ok) return SF_ERR_CUDA;
+  return h == 2u ? SF_ERR_DEVICE_TIMEOUT : (h == 1u ? SF_OK : SF_ERR_CUDA);
+}
