@@ -261,6 +261,21 @@ template <typename T, int R>
 __device__ __forceinline__ void store_slice(T* base, size_t co_stride, int co_lim, int lane, int nvalid,
                                             const float (&v)[R]) {
   if constexpr (sizeof(T) == 4 && R == 8) {
+#ifdef SF_CONV_V8_STORE
+    // sm_100 256-bit stores: each lane writes its channel's 8 pixels, one
+    // whole 32-byte sector, with no lane exchange. Off by default: on the C5
+    // cell 1.8 % faster at 1 % density but 8.6 % slower at 0 % (each store
+    // instruction touches 32 lines instead of 16).
+    if (nvalid == R && (reinterpret_cast<uintptr_t>(base) & 31u) == 0 && (co_stride & 7u) == 0) {
+      if (lane < co_lim) {
+        T* dst = base + (size_t)lane * co_stride;
+        asm volatile("st.global.v8.f32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(dst), "f"(v[0]), "f"(v[1]),
+                     "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7])
+                     : "memory");
+      }
+      return;
+    }
+#endif
     if (nvalid == R && (reinterpret_cast<uintptr_t>(base) & 15u) == 0 && (co_stride & 3u) == 0) {
       const int h = lane & 1;
       float recv[4];
