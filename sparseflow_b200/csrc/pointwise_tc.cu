@@ -225,18 +225,23 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == kProducerWarp) {
     if (lane == 0) {
+      int s = 0;
+      uint32_t round = 0;  // passes over the ring (ring position advanced incrementally: no division)
       for (int i = 0; i < nt && !failed; ++i) {
         const long long tile = t0 + i;
         const int img = (int)(tile / p.tiles_per_img);
         const int px0 = (int)(tile - (long long)img * p.tiles_per_img) * kM;
         for (int kc = 0; kc < KC; ++kc) {
-          const int g = i * KC + kc, s = g % p.nstages;
-          if (g >= p.nstages && !mbar_wait_ns(&bars->s_empty[s], (uint32_t)(((g / p.nstages) - 1) & 1))) {
+          if (round > 0 && !mbar_wait_ns(&bars->s_empty[s], (round - 1) & 1u)) {
             failed = true;
             break;
           }
           mbar_arrive_expect_tx(&bars->s_full[s], p.stage_bytes);
           tma_load_3d(stage + (size_t)s * p.stage_bytes, &xmap, px0, kc * kKC, img, &bars->s_full[s]);
+          if (++s == p.nstages) {
+            s = 0;
+            ++round;
+          }
         }
       }
       if (failed) atomicExch(p.err, 1u);
@@ -340,11 +345,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Converter warps 0-15: warp w converts channel octet w % 8 for pixel
     // half w / 8.
     const int o = warp & 7, phalf = warp >> 3;
+    int s = 0;
+    uint32_t sround = 0;  // staging ring position, advanced incrementally
     for (int i = 0; i < nt; ++i) {
       const int b = i % p.nd;
       for (int kc = 0; kc < KC && !failed; ++kc) {
-        const int g = i * KC + kc, s = g % p.nstages, a = g % kASlots;
-        if (!mbar_wait_ns(&bars->s_full[s], (uint32_t)((g / p.nstages) & 1))) {
+        const int g = i * KC + kc, a = g % kASlots;
+        if (!mbar_wait_ns(&bars->s_full[s], sround & 1u)) {
           failed = true;
           break;
         }
@@ -366,6 +373,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int e = 0; e < 8; ++e) v[k][e] = DT<XT>::to_f(st[(o * 8 + e) * kM + phalf * 64 + k * 32 + lane]);
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars->s_empty[s]);
+        if (++s == p.nstages) {
+          s = 0;
+          ++sround;
+        }
         // The MMA is exact whenever every x is exactly a bf16 (then each
         // product with a bf16 weight plane is exact in fp32): for the fp32
         // bits u that means u & 0xffff == 0, tested on the OR of all values,
