@@ -154,14 +154,19 @@ struct Bars {
   uint32_t odd[kMaxD];                  // = i + 1 when tile i (in D[b]) holds a value that is not exactly a bf16
 };
 
-template <typename XT, typename WT>
+// SUB: MMA sub-tiles of 128 pixels per tile. Two make each TMA row 1 KB
+// (256 pixels) instead of 512 B.
+template <typename XT, typename WT, int SUB>
 __global__ void __launch_bounds__(kThreads, 1)
     pointwise_tc_kernel(const TcParams p, const __grid_constant__ CUtensorMap xmap) {
+  constexpr int kTile = kM * SUB;          // pixels per tile
+  constexpr int kSlots = kASlots / SUB;    // A ring (each slot SUB x 16 KB)
+  constexpr uint32_t kSubA = kM * kKC * 2; // bytes of one sub-tile's A chunk
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   unsigned char* stage = smem;                                   // nstages x [64][128] of XT
   unsigned char* abuf = stage + p.nstages * p.stage_bytes;       // kASlots x A chunk (16 KB)
-  unsigned char* bbuf = abuf + kASlots * p.a_bytes;              // nplanes x [Npad][Kpad] bf16
+  unsigned char* bbuf = abuf + kSlots * p.a_bytes;               // nplanes x [Npad][Kpad] bf16
   Bars* bars = reinterpret_cast<Bars*>(bbuf + (size_t)p.nplanes * p.b_plane_bytes);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -176,7 +181,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars->s_full[s], 1);
       mbar_init(&bars->s_empty[s], kConvWarps);
     }
-    for (int a = 0; a < kASlots; ++a) {
+    for (int a = 0; a < kSlots; ++a) {
       mbar_init(&bars->a_full[a], kConvWarps);
       mbar_init(&bars->a_empty[a], 1);
     }
@@ -230,7 +235,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int i = 0; i < nt && !failed; ++i) {
         const long long tile = t0 + i;
         const int img = (int)(tile / p.tiles_per_img);
-        const int px0 = (int)(tile - (long long)img * p.tiles_per_img) * kM;
+        const int px0 = (int)(tile - (long long)img * p.tiles_per_img) * kTile;
         for (int kc = 0; kc < KC; ++kc) {
           if (round > 0 && !mbar_wait_ns(&bars->s_empty[s], (round - 1) & 1u)) {
             failed = true;
@@ -257,11 +262,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           failed = true;
           break;
         }
-        const uint32_t d = tmem + (uint32_t)(b * p.Npad);
+        const uint32_t d = tmem + (uint32_t)(b * SUB * p.Npad);
         uint32_t acc = 0u;
         for (int kc = 0; kc < KC; ++kc) {
-          const int g = i * KC + kc, a = g % kASlots;
-          if (!mbar_wait_ns(&bars->a_full[a], (uint32_t)((g / kASlots) & 1))) {
+          const int g = i * KC + kc, a = g % kSlots;
+          if (!mbar_wait_ns(&bars->a_full[a], (uint32_t)((g / kSlots) & 1))) {
             failed = true;
             break;
           }
@@ -274,10 +279,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t asa = smem_u32(abuf + (size_t)a * p.a_bytes);
 #pragma unroll
             for (int k16 = 0; k16 < kKC / 16; ++k16) {
-              const uint64_t ad = sdesc(asa + (uint32_t)(k16 * 32));
               for (int pl = 0; pl < p.nplanes; ++pl) {
                 const uint64_t bd = sdesc(bsa + (uint32_t)(pl * p.b_plane_bytes + kc * p.Npad * 128 + k16 * 32));
-                mma_bf16(d, ad, bd, idesc, acc);
+#pragma unroll
+                for (int sb = 0; sb < SUB; ++sb)
+                  mma_bf16(d + (uint32_t)(sb * p.Npad), sdesc(asa + sb * kSubA + (uint32_t)(k16 * 32)), bd, idesc,
+                           acc);
                 acc = 1u;
               }
             }
@@ -297,7 +304,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int b = i % p.nd;
       const long long tile = t0 + i;
       const int img = (int)(tile / p.tiles_per_img);
-      const int px0 = (int)(tile - (long long)img * p.tiles_per_img) * kM;
+      const int px0 = (int)(tile - (long long)img * p.tiles_per_img) * kTile;
       if (!mbar_wait_ns(&bars->d_full[b], (uint32_t)((i / p.nd) & 1))) {
         failed = true;
         return;
@@ -307,13 +314,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int ew = warp - kConvWarps;
       const int quarter = warp & 3;  // TMEM lane quarter this warp may read
       const int half = ew >> 2;      // column half
-      const int px = px0 + quarter * 32 + lane;
       const int ncol = p.Npad / 2;
       XT* yimg = static_cast<XT*>(p.y) + (size_t)img * p.Co * p.HW;
+#pragma unroll
+      for (int sb = 0; sb < SUB; ++sb) {
+      const int px = px0 + sb * kM + quarter * 32 + lane;
       if (!odd) {
         for (int c0 = half * ncol; c0 < (half + 1) * ncol; c0 += 16) {
           float v[16];
-          tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * p.Npad + c0), v);
+          tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)((b * SUB + sb) * p.Npad + c0), v);
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
             const int co = c0 + e;
@@ -335,6 +344,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           yimg[(size_t)co * p.HW + px] = DT<XT>::from_f(acc + (p.bias ? __ldg(p.bias + co) : 0.f));
         }
       }
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->d_empty[b]);
@@ -350,12 +360,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < nt; ++i) {
       const int b = i % p.nd;
       for (int kc = 0; kc < KC && !failed; ++kc) {
-        const int g = i * KC + kc, a = g % kASlots;
+        const int g = i * KC + kc, a = g % kSlots;
         if (!mbar_wait_ns(&bars->s_full[s], sround & 1u)) {
           failed = true;
           break;
         }
-        if (g >= kASlots && !mbar_wait_ns(&bars->a_empty[a], (uint32_t)(((g / kASlots) - 1) & 1))) {
+        if (g >= kSlots && !mbar_wait_ns(&bars->a_empty[a], (uint32_t)(((g / kSlots) - 1) & 1))) {
           failed = true;
           break;
         }
@@ -365,12 +375,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Lane l takes pixels phalf*64 + l and + 32: conflict-free 4-byte reads,
         // and each warp-wide 16-byte store covers all eight swizzle positions.
         // The stage is released as soon as its values are in registers.
-        constexpr int kPP = kM / 64;  // pixels per lane
+        constexpr int kPP = kTile / 64;  // pixels per lane
         float v[kPP][8];
 #pragma unroll
         for (int k = 0; k < kPP; ++k)
 #pragma unroll
-          for (int e = 0; e < 8; ++e) v[k][e] = DT<XT>::to_f(st[(o * 8 + e) * kM + phalf * 64 + k * 32 + lane]);
+          for (int e = 0; e < 8; ++e)
+            v[k][e] = DT<XT>::to_f(st[(o * 8 + e) * kTile + phalf * (kTile / 2) + k * 32 + lane]);
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars->s_empty[s]);
         if (++s == p.nstages) {
@@ -393,7 +404,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             orall |= u0 | u1;
             qq[e / 2] = __byte_perm(u0, u1, 0x7632);
           }
-          *reinterpret_cast<uint4*>(ab + sw128(phalf * 64 + k * 32 + lane, o * 8, kM)) = qv;
+          const int px = phalf * (kTile / 2) + k * 32 + lane;  // pixel in the tile -> sub-tile, row
+          *reinterpret_cast<uint4*>(ab + (px >> 7) * kSubA + sw128(px & (kM - 1), o * 8, kM)) = qv;
         }
         nz = __any_sync(0xffffffffu, (orall & 0x7fffffffu) != 0u);
         odd = __any_sync(0xffffffffu, (orall & 0xffffu) != 0u);
@@ -432,8 +444,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encoder() {
 }
 
 template <typename XT, typename WT>
-sf_status launch(TcParams p, const CUtensorMap& xmap, size_t smem, cudaStream_t st) {
-  auto kern = pointwise_tc_kernel<XT, WT>;
+sf_status launch(TcParams p, const CUtensorMap& xmap, size_t smem, int sub, cudaStream_t st) {
+  auto kern = sub == 2 ? pointwise_tc_kernel<XT, WT, 2> : pointwise_tc_kernel<XT, WT, 1>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return SF_ERR_CUDA;
   const long long ctas = std::min<long long>(p.ntiles, (long long)num_sms_current_device());
@@ -444,9 +456,9 @@ sf_status launch(TcParams p, const CUtensorMap& xmap, size_t smem, cudaStream_t 
 }
 
 template <typename XT>
-sf_status dispatch_w(int wdt, const TcParams& p, const CUtensorMap& xmap, size_t smem, cudaStream_t st) {
-  if (wdt == SF_DTYPE_F32) return launch<XT, float>(p, xmap, smem, st);
-  if (wdt == SF_DTYPE_BF16) return launch<XT, __nv_bfloat16>(p, xmap, smem, st);
+sf_status dispatch_w(int wdt, const TcParams& p, const CUtensorMap& xmap, size_t smem, int sub, cudaStream_t st) {
+  if (wdt == SF_DTYPE_F32) return launch<XT, float>(p, xmap, smem, sub, st);
+  if (wdt == SF_DTYPE_BF16) return launch<XT, __nv_bfloat16>(p, xmap, smem, sub, st);
   return SF_ERR_UNSUPPORTED;
 }
 
@@ -479,20 +491,34 @@ sf_status run_pointwise_tc(const void* x, const void* w_packed, const float* bia
   p.Npad = std::max(32, (Co + 31) / 32 * 32);  // two epilogue column halves of multiples of 16
   p.nplanes = wdt == SF_DTYPE_F32 ? 3 : 1;
   p.cpl = conv::weight_block_cpl(C, 1, Co, (int)dtype_size(wdt));
-  p.tiles_per_img = (int)((HW + kM - 1) / kM);
-  p.ntiles = (long long)N * p.tiles_per_img;
-  p.tiles_per_cta = 0;
-  p.stage_bytes = (uint32_t)(kKC * kM * esz);
-  p.a_bytes = (uint32_t)(kM * kKC * 2);
   p.b_plane_bytes = (uint32_t)(p.Npad * p.Kpad * 2);
-  p.nd = std::max(2, std::min(kMaxD, 512 / p.Npad));
-  uint32_t cols = 32;
-  while (cols < (uint32_t)(p.nd * p.Npad)) cols <<= 1;
-  p.tmem_cols = cols;
-  const size_t fixed = 1024 + kASlots * (size_t)p.a_bytes + (size_t)p.nplanes * p.b_plane_bytes + sizeof(Bars);
-  if (fixed + 2 * (size_t)p.stage_bytes > 232448) return SF_ERR_UNSUPPORTED;
-  p.nstages = (int)std::min<size_t>(kMaxStages, (232448 - fixed) / p.stage_bytes);
-  const size_t smem = fixed + (size_t)p.nstages * p.stage_bytes;
+  // Two 128-pixel sub-tiles per tile when shared memory and TMEM allow (1 KB
+  // TMA rows), else one.
+  auto plan = [&](int sub, size_t* smem_out) {
+    const int nd = std::min(kMaxD, 512 / (sub * p.Npad));
+    if (nd < 2) return false;
+    const size_t stage = (size_t)kKC * kM * sub * esz;
+    const size_t fixed = 1024 + (size_t)kASlots * kM * kKC * 2 + (size_t)p.nplanes * p.b_plane_bytes + sizeof(Bars);
+    if (fixed + 2 * stage > 232448) return false;
+    p.nd = nd;
+    p.nstages = (int)std::min<size_t>(kMaxStages, (232448 - fixed) / stage);
+    p.stage_bytes = (uint32_t)stage;
+    p.a_bytes = (uint32_t)(kM * kKC * 2 * sub);
+    *smem_out = fixed + (size_t)p.nstages * stage;
+    uint32_t cols = 32;
+    while (cols < (uint32_t)(nd * sub * p.Npad)) cols <<= 1;
+    p.tmem_cols = cols;
+    p.tiles_per_img = (int)((HW + kM * sub - 1) / (kM * sub));
+    p.ntiles = (long long)N * p.tiles_per_img;
+    return true;
+  };
+  size_t smem = 0;
+  int sub = 2;
+  if (!plan(2, &smem)) {
+    sub = 1;
+    if (!plan(1, &smem)) return SF_ERR_UNSUPPORTED;
+  }
+  p.tiles_per_cta = 0;
 
   // x as a 3-D tensor (pixels, channels, images); box = one chunk.
   CUtensorMap xmap;
@@ -501,16 +527,16 @@ sf_status run_pointwise_tc(const void* x, const void* w_packed, const float* bia
                                                        : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const cuuint64_t dims[3] = {(cuuint64_t)HW, (cuuint64_t)C, (cuuint64_t)N};
   const cuuint64_t strides[2] = {(cuuint64_t)(HW * esz), (cuuint64_t)(HW * esz * C)};
-  const cuuint32_t box[3] = {(cuuint32_t)kM, (cuuint32_t)kKC, 1u};
+  const cuuint32_t box[3] = {(cuuint32_t)(kM * sub), (cuuint32_t)kKC, 1u};
   const cuuint32_t estr[3] = {1u, 1u, 1u};
   if (enc(&xmap, dt, 3, const_cast<void*>(x), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
           CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
       CUDA_SUCCESS)
     return SF_ERR_UNSUPPORTED;
   switch (xdt) {
-    case SF_DTYPE_F32: return dispatch_w<float>(wdt, p, xmap, smem, st);
-    case SF_DTYPE_F16: return dispatch_w<__half>(wdt, p, xmap, smem, st);
-    case SF_DTYPE_BF16: return dispatch_w<__nv_bfloat16>(wdt, p, xmap, smem, st);
+    case SF_DTYPE_F32: return dispatch_w<float>(wdt, p, xmap, smem, sub, st);
+    case SF_DTYPE_F16: return dispatch_w<__half>(wdt, p, xmap, smem, sub, st);
+    case SF_DTYPE_BF16: return dispatch_w<__nv_bfloat16>(wdt, p, xmap, smem, sub, st);
   }
   return SF_ERR_INVALID_ARG;
 }
