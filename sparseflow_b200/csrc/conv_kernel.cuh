@@ -105,6 +105,7 @@ struct ConvParams {
   int nw_out;                       // ceil(Co / 64)
   int nw;
   float tau, vth, vreset;
+  float inv_tau;  // 1 / tau when tau is a power of two (MODE 3/4)
   int hard_reset, decay_input;
   int T, N, C, H, W, Co, Ho, Wo, P;
   int TH, nbands, ncolb, ncob, n_units, tpr, tpu;  // tpr: row segments per output row; tpu: per unit
@@ -299,12 +300,16 @@ __device__ __forceinline__ void store_slice(T* base, size_t co_stride, int co_li
 
 // MODE 0: convolution; 1: fused conv + LIF; 2: fused conv + LIF that also
 // writes the spikes' event masks (a separate instantiation, so the plain LIF
-// kernel carries none of that code).
+// kernel carries none of that code); 3 / 4: as 1 / 2 for a power-of-two tau.
 template <int K, int S, int CPL, int R, int B, typename XT, typename WT, int MODE, bool WSMEM>
 __global__ void __launch_bounds__(kThreads, 1)
     sparse_conv_kernel(const ConvParams p, const __grid_constant__ CUtensorMap ymap) {
   constexpr bool LIF = MODE >= 1;
-  constexpr bool EMIT = MODE == 2;
+  constexpr bool EMIT = MODE == 2 || MODE == 4;
+  // MODE 3/4: tau a power of two, so x / tau == x * (1 / tau) exactly (both
+  // the correctly rounded value of one real number) and the LIF epilogue
+  // carries no division code.
+  constexpr bool TAU_POW2 = MODE >= 3;
   extern __shared__ __align__(128) unsigned char smem[];
   constexpr int KK = K * K;
   constexpr int QN = (R - 1) * S + K;  // input columns a row segment reads
@@ -661,9 +666,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const float vr = p.hard_reset ? p.vreset : 0.f;
                 float vt;
                 if (p.decay_input)
-                  vt = vp + (val - (vp - vr)) / p.tau;
+                  vt = vp + (TAU_POW2 ? __fmul_rn(val - (vp - vr), p.inv_tau) : (val - (vp - vr)) / p.tau);
                 else
-                  vt = vp - (vp - vr) / p.tau + val;
+                  vt = vp - (TAU_POW2 ? __fmul_rn(vp - vr, p.inv_tau) : (vp - vr) / p.tau) + val;
                 const bool spk = vt >= p.vth;
                 vreg[j][i] = p.hard_reset ? (spk ? p.vreset : vt) : (vt - (spk ? p.vth : 0.f));
                 val = spk ? 1.f : 0.f;
@@ -792,6 +797,10 @@ sf_status dispatch_x(int mode, int wdt, int K, int S, const ConvParams& p, const
                        : dispatch_ws<XT, __nv_bfloat16, 1>(K, S, p, ym, grid, pl, st);
     case 2: return f32 ? dispatch_ws<XT, float, 2>(K, S, p, ym, grid, pl, st)
                        : dispatch_ws<XT, __nv_bfloat16, 2>(K, S, p, ym, grid, pl, st);
+    case 3: return f32 ? dispatch_ws<XT, float, 3>(K, S, p, ym, grid, pl, st)
+                       : dispatch_ws<XT, __nv_bfloat16, 3>(K, S, p, ym, grid, pl, st);
+    case 4: return f32 ? dispatch_ws<XT, float, 4>(K, S, p, ym, grid, pl, st)
+                       : dispatch_ws<XT, __nv_bfloat16, 4>(K, S, p, ym, grid, pl, st);
   }
   return SF_ERR_INVALID_ARG;
 }

@@ -1,6 +1,7 @@
 // C-ABI entry points of the sparse convolution (stage 1 event extraction +
 // stage 2 gather) and of the fused conv+LIF kernel: argument checks, launch
 // planning, weight packing. The kernels are in events.cu and conv_kernel.cuh.
+#include <cmath>
 #include <cstdlib>
 #include <cstring>
 #include <cudaTypedefs.h>
@@ -293,7 +294,15 @@ sf_status run_conv(const void* x, const void* w_packed, const float* bias, void*
     if (s != SF_OK) return s;
   }
   const int grid_used = (p.n_units + p.units_per_cta - 1) / p.units_per_cta;
-  return dispatch(lif ? (mask_out ? 2 : 1) : 0, xdt, wdt, K, S, p, ym, grid_used, pl, st);
+  int mode = 0;
+  if (lif) {
+    int e = 0;
+    const float m = std::frexp(p.tau, &e);
+    const bool pow2 = m == 0.5f && e > -125 && e < 126;  // tau = 2^(e-1), 1/tau a normal float
+    p.inv_tau = pow2 ? 1.f / p.tau : 0.f;
+    mode = (mask_out ? 2 : 1) + (pow2 ? 2 : 0);
+  }
+  return dispatch(mode, xdt, wdt, K, S, p, ym, grid_used, pl, st);
 }
 
 }  // namespace
