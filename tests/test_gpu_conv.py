@@ -206,3 +206,26 @@ def test_conv1x1_16bit_inputs_vs_oracle(xdt, co):
     assert y.dtype == xdt
     ref = oracle.conv2d(x.float().numpy(), wt.numpy(), None, 1, 0)
     _assert_close(y.float().cpu().numpy(), ref, rtol=1e-2)
+
+
+def test_conv1x1_full_size_c2_cell_vs_cudnn_fp32():
+    """Full C2 workload (T=16, N=32, 256->64, 56x56, block-clustered spikes, bf16 weights) on the
+    tensor-core path: against cuDNN fp32 (TF32 off) on the same bf16-valued weights, and
+    deterministic across runs."""
+    from sparseflow_b200.Kernels.conv2d import sparse_conv2d_forward
+    g = torch.Generator(device="cuda").manual_seed(17)
+    blk = (torch.rand(512, 256, 4, 4, device="cuda", generator=g) < 0.05).float()
+    mask = blk.repeat_interleave(16, 2).repeat_interleave(16, 3)[:, :, :56, :56]
+    x = (mask * (torch.rand(512, 256, 56, 56, device="cuda", generator=g) < 0.3).float()).contiguous()
+    del blk, mask
+    w = (torch.randn(64, 256, 1, 1, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    y, _ = sparse_conv2d_forward(x, w, None, kernel_size=1, stride=1, padding=0)
+    prev = torch.backends.cudnn.allow_tf32
+    torch.backends.cudnn.allow_tf32 = False
+    try:
+        ref = torch.nn.functional.conv2d(x, w.float())
+    finally:
+        torch.backends.cudnn.allow_tf32 = prev
+    assert (y - ref).abs().max().item() <= RTOL * ref.abs().max().item()
+    y2, _ = sparse_conv2d_forward(x, w, None, kernel_size=1, stride=1, padding=0)
+    assert torch.equal(y, y2)

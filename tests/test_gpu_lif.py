@@ -129,3 +129,39 @@ def test_fused_lif_tau_values_match_oracle(tau):
         # fp32 vs double conv sums: a spike may flip only where v sits within ~1e-6 of v_th
         assert (got == so).mean() > 0.999
     assert np.abs(v.cpu().numpy() - vo).max() < 1e-4
+
+
+def test_fused_conv_bn_lif_full_size_c3_vs_cudnn_path():
+    """Full C3 workload (T=16, N=64, C=128, 28x28, p=0.005, BN folded, tau=2 hard reset): spikes
+    equal the cuDNN-fp32 conv + BN + LIF formula except where that path's membrane is within
+    1e-5 of the threshold; final membranes within 1e-4."""
+    from sparseflow_b200.Ops.sparse_fused_conv_lif import FusedSparseConvLIF
+    from sparseflow_b200.Ops.lif_node import LIFNode
+    g = torch.Generator(device="cuda").manual_seed(3)
+    x = (torch.rand(16, 64, 128, 28, 28, device="cuda", generator=g) < 0.005).float()
+    conv = nn.Conv2d(128, 128, 3, 1, 1, bias=False).cuda()
+    conv.weight.data = torch.randn(128, 128, 3, 3, device="cuda", generator=g) * (2.0 / (128 * 9)) ** 0.5 * 4
+    bn = nn.BatchNorm2d(128).cuda().eval()
+    bn.weight.data = torch.rand(128, device="cuda", generator=g) + 0.5
+    bn.bias.data = torch.randn(128, device="cuda", generator=g) * 0.1
+    bn.running_mean = torch.randn(128, device="cuda", generator=g) * 0.1
+    bn.running_var = torch.rand(128, device="cuda", generator=g) + 0.5
+    m = FusedSparseConvLIF.from_conv_bn_lif(conv, bn, LIFNode(tau=2.0, v_threshold=1.0, v_reset=0.0))
+    s = m(x)
+    prev = torch.backends.cudnn.allow_tf32
+    torch.backends.cudnn.allow_tf32 = False
+    try:
+        cur = bn(torch.nn.functional.conv2d(x.flatten(0, 1), conv.weight, None, 1, 1)).reshape(16, 64, 128, 28, 28)
+    finally:
+        torch.backends.cudnn.allow_tf32 = prev
+    v = torch.zeros(64, 128, 28, 28, device="cuda")
+    flips = 0
+    for t in range(16):
+        h = v + (cur[t] - v) / 2.0
+        ref = (h >= 1.0).float()
+        near = (h - 1.0).abs() < 1e-5
+        flips += int(((s[t] != ref) & ~near).sum())
+        v = torch.where(ref.bool(), torch.zeros_like(h), h)
+    assert float(s.mean()) > 1e-4  # the layer fires
+    assert flips == 0
+    assert (m.v - v).abs().max().item() < 1e-4
