@@ -230,6 +230,20 @@ __device__ __forceinline__ void store_run(T* dst, const float (&v)[R], int nvali
       return;
     }
   }
+  if constexpr (sizeof(T) == 4 && R % 2 == 0) {
+    // Rows whose length breaks 16-byte alignment (W = 14, 7, ...) or ragged
+    // last segments: 8-byte stores where two pixels are valid.
+    if ((reinterpret_cast<uintptr_t>(dst) & 7u) == 0) {
+#pragma unroll
+      for (int j = 0; j < R; j += 2) {
+        if (j + 1 < nvalid)
+          *reinterpret_cast<float2*>(dst + j) = make_float2(v[j], v[j + 1]);
+        else if (j < nvalid)
+          dst[j] = DT<T>::from_f(v[j]);
+      }
+      return;
+    }
+  }
 #pragma unroll
   for (int j = 0; j < R; ++j)
     if (j < nvalid) dst[j] = DT<T>::from_f(v[j]);
