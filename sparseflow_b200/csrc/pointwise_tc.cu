@@ -513,8 +513,8 @@ sf_status run_pointwise_tc(const void* x, const void* w_packed, const float* bia
     return true;
   };
   size_t smem = 0;
-  int sub = 2;
-  if (!plan(2, &smem)) {
+  int sub = HW > kM ? 2 : 1;  // an image of <= 128 pixels would leave a 256-pixel tile mostly empty
+  if (sub == 1 || !plan(2, &smem)) {
     sub = 1;
     if (!plan(1, &smem)) return SF_ERR_UNSUPPORTED;
   }
