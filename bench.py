@@ -60,7 +60,7 @@ def parse():
     ap.add_argument("--no-extra", action="store_true", help="skip the C2/C3/prescan side measurements")
     ap.add_argument("--only-timed", action="store_true",
                     help="run only the warm-up and timed steps (no cuDNN, e2e, extras or CPU baseline); for ncu")
-    ap.add_argument("--kernel", choices=["conv", "prescan", "c2"], default="conv",
+    ap.add_argument("--kernel", choices=["conv", "prescan", "c2", "c3", "lif"], default="conv",
                     help="with --only-timed: time the sparse conv (default), the prescan on the same input, "
                          "or the C2 1x1 cell (--images = T*N of C2, default 512)")
     ap.add_argument("--sweep", action="store_true",
@@ -422,6 +422,42 @@ def main():
         if rank == 0:
             print(json.dumps({"kernel": "c2", "ms_per_step": round(ms, 4), "GBps": round(b2 / ms / 1e6, 1),
                               "frac_of_measured_hbm": round(b2 / ms / 1e6 / hbm_peak, 3), "images": n2}))
+        if dist is not None:
+            dist.destroy_process_group()
+        return
+
+    if args.only_timed and args.kernel in ("c3", "lif"):
+        # C3 fused conv3x3 + BN-fold + LIF (T16, C128 28x28, Bernoulli(0.005)
+        # spikes), or the standalone multi-step LIF on the same shape with
+        # real-valued input currents N(0,1). --images sets T*N (default 16*64).
+        from sparseflow_b200.Ops.sparse_fused_conv_lif import FusedSparseConvLIF
+        from sparseflow_b200.Ops.lif_node import LIFNode
+        n3 = (args.images if args.images != T_STEPS * N_BATCH else 16 * 64) // 16
+        g3 = torch.Generator(device=dev).manual_seed(23 + rank)
+        if args.kernel == "c3":
+            x3 = (torch.rand(16, n3, 128, 28, 28, device=dev, generator=g3) < 0.005).float()
+            conv3 = make_conv(128, 128, 3, 1, 1, False, 3, device=dev)
+            bn = nn.BatchNorm2d(128).to(dev).eval()
+            m3 = FusedSparseConvLIF.from_conv_bn_lif(conv3, bn, LIFNode(tau=2.0, v_threshold=1.0, v_reset=0.0))
+
+            def step():
+                m3.reset()
+                return m3(x3)
+            nb = 4 * x3.numel() * 2 + 4 * n3 * 128 * 28 * 28 * 2 + 4 * 128 * 128 * 9
+        else:
+            x3 = torch.randn(16, n3, 128, 28, 28, device=dev, generator=g3)
+            lif = LIFNode(tau=2.0, v_threshold=1.0, v_reset=0.0, step_mode="m")
+
+            def step():
+                lif.reset()
+                return lif(x3)
+            nb = 4 * x3.numel() * 2 + 4 * n3 * 128 * 28 * 28
+        with torch.no_grad():
+            ms = cuda_time(step, args.steps, args.warmup, dist) / args.steps
+        if rank == 0:
+            print(json.dumps({"kernel": args.kernel, "ms_per_step": round(ms, 4), "GBps": round(nb / ms / 1e6, 1),
+                              "frac_of_measured_hbm": round(nb / ms / 1e6 / hbm_peak, 3), "images": 16 * n3,
+                              "bytes": nb}))
         if dist is not None:
             dist.destroy_process_group()
         return
