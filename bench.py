@@ -62,7 +62,8 @@ def parse():
                     help="run only the warm-up and timed steps (no cuDNN, e2e, extras or CPU baseline); for ncu")
     ap.add_argument("--kernel", choices=["conv", "prescan", "c2", "c3", "lif"], default="conv",
                     help="with --only-timed: time the sparse conv (default), the prescan on the same input, "
-                         "or the C2 1x1 cell (--images = T*N of C2, default 512)")
+                         "the C2 1x1 cell (--images = T*N of C2, default 512), the C3 fused conv+LIF or the "
+                         "standalone LIF (--images = T*N, default 1024)")
     ap.add_argument("--sweep", action="store_true",
                     help="C5 grid: C x H x density, sparse conv3x3 vs cuDNN and the HBM roofline (one JSON line per cell)")
     ap.add_argument("--sweep-images", type=int, default=T_STEPS * N_BATCH,
