@@ -37,6 +37,34 @@ __device__ __forceinline__ float lif_update(float& v, float x, const LifParams& 
   return s ? 1.f : 0.f;
 }
 
+// Streaming (evict-first) vector loads and stores: x is read once and the
+// spikes are written once, so neither should displace v or other data in L2.
+template <typename T, int V>
+__device__ __forceinline__ LVec<T, V> ld_stream(const LVec<T, V>* p) {
+  if constexpr (sizeof(LVec<T, V>) == 16) {
+    const float4 f = __ldcs(reinterpret_cast<const float4*>(p));
+    return *reinterpret_cast<const LVec<T, V>*>(&f);
+  } else if constexpr (sizeof(LVec<T, V>) == 8) {
+    const float2 f = __ldcs(reinterpret_cast<const float2*>(p));
+    return *reinterpret_cast<const LVec<T, V>*>(&f);
+  } else {
+    return *p;
+  }
+}
+template <typename T, int V>
+__device__ __forceinline__ void st_stream(LVec<T, V>* p, const LVec<T, V>& v) {
+  if constexpr (sizeof(LVec<T, V>) == 16)
+    __stcs(reinterpret_cast<float4*>(p), *reinterpret_cast<const float4*>(&v));
+  else if constexpr (sizeof(LVec<T, V>) == 8)
+    __stcs(reinterpret_cast<float2*>(p), *reinterpret_cast<const float2*>(&v));
+  else
+    *p = v;
+}
+
+// Steps whose x is loaded ahead of their updates: the loads of a group do not
+// depend on the membrane state, so all of them are in flight together.
+constexpr int kLifPrefetch = 8;
+
 template <typename XT, typename ST, int VEC>
 __global__ void __launch_bounds__(256) lif_multistep_kernel(const XT* __restrict__ x, float* __restrict__ v,
                                                             ST* __restrict__ s, long long numel, int T,
@@ -45,15 +73,20 @@ __global__ void __launch_bounds__(256) lif_multistep_kernel(const XT* __restrict
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < nvec;
        i += (long long)gridDim.x * blockDim.x) {
     LVec<float, VEC> vv = reinterpret_cast<const LVec<float, VEC>*>(v)[i];
-    // Loads of step t+1 do not depend on step t's state: unrolling keeps
-    // several in flight.
-#pragma unroll 4
-    for (int t = 0; t < T; ++t) {
-      const LVec<XT, VEC> xv = reinterpret_cast<const LVec<XT, VEC>*>(x + (size_t)t * numel)[i];
-      LVec<ST, VEC> sv;
+    for (int t0 = 0; t0 < T; t0 += kLifPrefetch) {
+      LVec<XT, VEC> xb[kLifPrefetch];
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) sv.v[e] = DT<ST>::from_f(lif_update(vv.v[e], DT<XT>::to_f(xv.v[e]), q));
-      reinterpret_cast<LVec<ST, VEC>*>(s + (size_t)t * numel)[i] = sv;
+      for (int k = 0; k < kLifPrefetch; ++k)
+        if (t0 + k < T) xb[k] = ld_stream(reinterpret_cast<const LVec<XT, VEC>*>(x + (size_t)(t0 + k) * numel) + i);
+#pragma unroll
+      for (int k = 0; k < kLifPrefetch; ++k) {
+        if (t0 + k < T) {
+          LVec<ST, VEC> sv;
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) sv.v[e] = DT<ST>::from_f(lif_update(vv.v[e], DT<XT>::to_f(xb[k].v[e]), q));
+          st_stream(reinterpret_cast<LVec<ST, VEC>*>(s + (size_t)(t0 + k) * numel) + i, sv);
+        }
+      }
     }
     reinterpret_cast<LVec<float, VEC>*>(v)[i] = vv;
   }
@@ -65,7 +98,8 @@ sf_status launch(const void* x, float* v, void* s, long long numel, int T, const
                    (reinterpret_cast<uintptr_t>(s) % (4 * sizeof(ST))) == 0;
   const int V = vec ? 4 : 1;
   const long long nvec = numel / V;
-  const long long blocks = std::min<long long>((nvec + 255) / 256, (long long)num_sms_current_device() * 8);
+  // One vector per thread where the grid allows (no tail of uneven loop trips).
+  const long long blocks = std::min<long long>((nvec + 255) / 256, 1ll << 30);
   if (blocks <= 0) return SF_OK;
   if (vec)
     lif_multistep_kernel<XT, ST, 4><<<(unsigned)blocks, 256, 0, st>>>(static_cast<const XT*>(x), v,
