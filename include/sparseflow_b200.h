@@ -26,6 +26,7 @@
  *   sf_lif_multistep      the multi-step LIFNode that follows a BN in spikingjelly-style
  *                         models (Ops/sparse_fused_conv_lif.py:271-293 applied over T;
  *                         spikingjelly LIFNode, step_mode 'm'), one launch for all steps.
+ *   sf_lif_multistep_events  the same, also writing the next convolution's event masks.
  */
 #ifndef SPARSEFLOW_B200_H
 #define SPARSEFLOW_B200_H
@@ -220,6 +221,18 @@ typedef struct sf_lif_ms_desc {
  * vector access. No workspace. */
 sf_status sf_lif_multistep(const void* x, float* v_inout, void* spikes_out, const sf_lif_ms_desc* d,
                            void* stream);
+
+/* sf_lif_multistep on x viewed as [t_steps][n][c][h][w] (d->numel == n*c*h*w)
+ * that also writes the spikes' event masks to spike_masks_out (8-byte aligned,
+ * sf_event_masks_bytes(t_steps * n, c, h, w) bytes; every word written): the
+ * layout the mask pass of sf_sparse_conv2d writes, so sf_sparse_conv2d_from_masks
+ * can run the next convolution without reading the spikes. Spikes and v are
+ * identical to sf_lif_multistep's. Reference: the producer-side bitmap of the
+ * LIFNode that follows a BN (no fused conv), whose spikes the reference's
+ * prescan reads again (Kernels/_prescan_common.py:32-109). */
+sf_status sf_lif_multistep_events(const void* x, float* v_inout, void* spikes_out, void* spike_masks_out,
+                                  const sf_lif_ms_desc* d, int32_t n, int32_t c, int32_t h, int32_t w,
+                                  void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* Diagnostics.                                                              */

@@ -28,6 +28,10 @@ class LIFNode(nn.Module):
         self.detach_reset = detach_reset
         self.step_mode = step_mode
         self.v = None
+        # Opt-in: a 5-D multi-step call on CUDA also writes the spikes' event masks
+        # (sf_lif_multistep_events) and attaches them to the output, so a following
+        # SparseConv2d given that very tensor skips its mask pass over the spikes.
+        self.emit_event_masks = False
 
     def reset(self):
         self.v = None
@@ -66,6 +70,14 @@ class LIFNode(nn.Module):
         else:
             self.v = self.v.float().contiguous()
         spikes = torch.empty_like(x)
+        if self.emit_event_masks and x.dim() == 5:
+            from ..Kernels.fused_conv_lif import attach_event_masks
+            t, n, c, h, w = x.shape
+            masks = torch.empty(_lib.event_masks_bytes(t * n, c, h, w) // 8, dtype=torch.int64, device=x.device)
+            _lib.lif_multistep_events(x, self.v, spikes, masks, self.tau, self.v_threshold, self.v_reset,
+                                      self.decay_input)
+            attach_event_masks(spikes, masks)
+            return spikes
         _lib.lif_multistep(x, self.v, spikes, self.tau, self.v_threshold, self.v_reset, self.decay_input)
         return spikes
 

@@ -104,6 +104,8 @@ _SIGNATURES = {
     "sf_fused_conv_lif": (ctypes.c_int32, [_VP, _VP, _VP, _VP, _VP, _VP, ctypes.POINTER(LifDesc), _VP, ctypes.c_size_t,
                                            _VP]),
     "sf_lif_multistep": (ctypes.c_int32, [_VP, _VP, _VP, ctypes.POINTER(LifMsDesc), _VP]),
+    "sf_lif_multistep_events": (ctypes.c_int32, [_VP, _VP, _VP, _VP, ctypes.POINTER(LifMsDesc), ctypes.c_int32,
+                                                 ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _VP]),
     "sf_event_masks_bytes": (ctypes.c_size_t, [ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]),
     "sf_selftest_bounded_wait": (ctypes.c_int32, [ctypes.c_uint64, _VP]),
     "sf_sparse_conv2d_from_masks": (ctypes.c_int32, [_VP, _VP, _VP, _VP, ctypes.POINTER(ConvDesc), _VP]),
@@ -305,3 +307,24 @@ def lif_multistep(x: torch.Tensor, v: torch.Tensor, spikes: torch.Tensor, tau: f
                      int(v_reset is not None), int(bool(decay_input)), sf_dtype(x.dtype), sf_dtype(spikes.dtype))
     st = load().sf_lif_multistep(_ptr(x), _ptr(v), _ptr(spikes), ctypes.byref(desc), _stream(x.device))
     _check("sf_lif_multistep", st)
+
+
+def lif_multistep_events(x: torch.Tensor, v: torch.Tensor, spikes: torch.Tensor, masks: torch.Tensor, tau: float,
+                         v_threshold: float, v_reset: Optional[float], decay_input: bool) -> None:
+    """lif_multistep on x = [T, N, C, H, W] that also writes the spikes' event masks into ``masks``
+    (sf_event_masks_bytes(T*N, C, H, W) bytes, 8-byte aligned)."""
+    _require_cuda(x, v, spikes, masks)
+    if v.dtype != torch.float32 or not (x.is_contiguous() and v.is_contiguous() and spikes.is_contiguous()):
+        raise ValueError("lif_multistep_events needs contiguous tensors and an fp32 membrane")
+    if x.dim() != 5:
+        raise ValueError(f"lif_multistep_events needs a 5-D [T, N, C, H, W] input, got {x.dim()}-D")
+    t, n, c, h, w = x.shape
+    if tuple(v.shape) != (n, c, h, w) or spikes.shape != x.shape:
+        raise ValueError("shape mismatch between x, v and spikes")
+    if masks.numel() * masks.element_size() < event_masks_bytes(t * n, c, h, w):
+        raise ValueError("event-mask buffer too small")
+    desc = LifMsDesc(n * c * h * w, t, float(tau), float(v_threshold), 0.0 if v_reset is None else float(v_reset),
+                     int(v_reset is not None), int(bool(decay_input)), sf_dtype(x.dtype), sf_dtype(spikes.dtype))
+    st = load().sf_lif_multistep_events(_ptr(x), _ptr(v), _ptr(spikes), _ptr(masks), ctypes.byref(desc), n, c, h, w,
+                                        _stream(x.device))
+    _check("sf_lif_multistep_events", st)

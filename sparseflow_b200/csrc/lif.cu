@@ -11,6 +11,7 @@
 // kernels per step and moves v through HBM every step; here each thread owns
 // VEC elements, keeps their v in registers across all T steps, and reads x /
 // writes spikes once: bytes = T * numel * (|x| + |spike|) + 8 * numel.
+#include <cmath>
 #include "common.cuh"
 
 namespace sf {
@@ -121,6 +122,155 @@ sf_status dispatch_s(int sdt, const void* x, float* v, void* s, long long numel,
   return SF_ERR_INVALID_ARG;
 }
 
+
+// ---------------------------------------------------------------------------
+// The same LIF, also writing the spikes' event masks for the next sparse
+// convolution (the layout of the mask pass: per image and pixel, bit c % 64
+// of 64-bit word c / 64 set iff channel c spiked; written here as 32-bit
+// halves). A warp owns 32 consecutive pixels (lane = pixel) x 32 channels of
+// one image: every load and store instruction covers one contiguous 128-byte
+// row segment (fp32), the 32 membranes stay in registers across all steps,
+// and each lane assembles its pixel's half word bit by bit (no ballots).
+// ---------------------------------------------------------------------------
+constexpr int kEvCh = 32;  // channels per warp (one 32-bit half word)
+#ifndef SF_LIF_EV_T
+#define SF_LIF_EV_T 4
+#endif
+#ifndef SF_LIF_EV_G
+#define SF_LIF_EV_G 4
+#endif
+#ifndef SF_LIF_EV_MINB
+#define SF_LIF_EV_MINB 4
+#endif
+constexpr int kEvT = SF_LIF_EV_T;  // steps per load group
+constexpr int kEvG = SF_LIF_EV_G;  // channels per load group
+
+// lif_update with x / tau computed as x * (1 / tau): for tau a power of two
+// both are the correctly rounded value of the same real number, so the
+// results (and spikes) are identical without the division sequence.
+__device__ __forceinline__ float lif_update_pow2(float& v, float x, const LifParams& q, float inv_tau) {
+  float h;
+  if (q.decay_input)
+    h = v + __fmul_rn(x - (v - q.vr), inv_tau);
+  else
+    h = v - __fmul_rn(v - q.vr, inv_tau) + x;
+  const bool s = h >= q.vth;
+  v = q.hard ? (s ? q.vr : h) : (h - (s ? q.vth : 0.f));
+  return s ? 1.f : 0.f;
+}
+
+template <typename XT, typename ST, bool POW2>
+__global__ void __launch_bounds__(256, SF_LIF_EV_MINB) lif_events_kernel(const XT* __restrict__ x, float* __restrict__ v,
+                                                         ST* __restrict__ s, uint32_t* __restrict__ masks, int T,
+                                                         int N, int C, int HW, int ncb, int npb, int nw2,
+                                                         LifParams q, float inv_tau) {
+  // Membranes of the warp's 32 channels x 32 pixels, [channel][warp][lane]:
+  // conflict-free, and no per-channel register file to unroll.
+  __shared__ float vs[kEvCh][8][32];
+  const int wib = threadIdx.x >> 5;
+  const long long gw = (long long)blockIdx.x * (blockDim.x >> 5) + wib;
+  const int lane = threadIdx.x & 31;
+  if (gw >= (long long)N * ncb * npb) return;
+  const int pb = (int)(gw % npb);
+  const long long rest = gw / npb;
+  const int cb = (int)(rest % ncb);
+  const int img = (int)(rest / ncb);
+  const int p = pb * 32 + lane;
+  const bool pix = p < HW;
+  const int c0 = cb * kEvCh;
+  const int nc = min(kEvCh, C - c0);
+  const size_t step = (size_t)N * C * HW;
+  const size_t off = ((size_t)img * C + c0) * HW + p;  // channel c0 of this lane's pixel
+  // With no sibling block for the upper half word of the last 64-channel word,
+  // this warp also writes that half as zero.
+  const bool zero_upper = (cb % 2 == 0) && cb + 1 < nw2 && c0 + kEvCh >= C;
+
+  for (int j = 0; j < kEvCh; ++j) vs[j][wib][lane] = (pix && j < nc) ? v[off + j * HW] : 0.f;
+  // Steps in groups of kEvT, channels in groups of kEvG: the group's
+  // kEvT x kEvG loads are independent of the membrane and all in flight
+  // together; each channel then runs through the group's steps.
+  for (int t0 = 0; t0 < T; t0 += kEvT) {
+    uint32_t word[kEvT];
+#pragma unroll
+    for (int k = 0; k < kEvT; ++k) word[k] = 0u;
+#pragma unroll 1
+    for (int g0 = 0; g0 < nc; g0 += kEvG) {
+      float xr[kEvT][kEvG];
+#pragma unroll
+      for (int k = 0; k < kEvT; ++k) {
+        const XT* xt = x + (size_t)(t0 + k) * step + off + g0 * HW;
+#pragma unroll
+        for (int j = 0; j < kEvG; ++j)
+          xr[k][j] = (pix && t0 + k < T && g0 + j < nc) ? DT<XT>::to_f(__ldcs(xt + j * HW)) : 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < kEvG; ++j) {
+        if (g0 + j < nc) {
+          float vv = vs[g0 + j][wib][lane];
+#pragma unroll
+          for (int k = 0; k < kEvT; ++k) {
+            if (t0 + k < T) {
+              const float sp = POW2 ? lif_update_pow2(vv, xr[k][j], q, inv_tau) : lif_update(vv, xr[k][j], q);
+              word[k] |= (sp != 0.f ? 1u : 0u) << (g0 + j);
+              if (pix) __stcs(s + (size_t)(t0 + k) * step + off + (g0 + j) * HW, DT<ST>::from_f(sp));
+            }
+          }
+          vs[g0 + j][wib][lane] = vv;
+        }
+      }
+    }
+    if (pix) {
+#pragma unroll
+      for (int k = 0; k < kEvT; ++k) {
+        if (t0 + k < T) {
+          uint32_t* mw = masks + ((size_t)((size_t)(t0 + k) * N + img) * HW + p) * nw2;
+          mw[cb] = word[k];
+          if (zero_upper) mw[cb + 1] = 0u;
+        }
+      }
+    }
+  }
+  for (int j = 0; j < nc; ++j)
+    if (pix) v[off + j * HW] = vs[j][wib][lane];
+}
+
+// 1 / tau when tau is a power of two (with a normal reciprocal), else 0.
+inline float pow2_reciprocal(float tau) {
+  int e = 0;
+  const float m = std::frexp(std::fabs(tau), &e);
+  if (m != 0.5f || e < -124 || e > 126) return 0.f;
+  return 1.f / tau;
+}
+
+template <typename XT, typename ST>
+sf_status launch_events(const void* x, float* v, void* s, void* masks, int T, int N, int C, int HW,
+                        const LifParams& q, cudaStream_t st) {
+  const int ncb = (C + kEvCh - 1) / kEvCh, npb = (HW + 31) / 32, nw2 = 2 * ((C + 63) / 64);
+  const long long warps = (long long)N * ncb * npb;
+  const long long blocks = (warps + 7) / 8;
+  if (blocks > INT32_MAX) return SF_ERR_UNSUPPORTED;
+  const float inv = pow2_reciprocal(q.tau);
+  if (inv != 0.f)
+    lif_events_kernel<XT, ST, true><<<(unsigned)blocks, 256, 0, st>>>(
+        static_cast<const XT*>(x), v, static_cast<ST*>(s), static_cast<uint32_t*>(masks), T, N, C, HW, ncb, npb,
+        nw2, q, inv);
+  else
+    lif_events_kernel<XT, ST, false><<<(unsigned)blocks, 256, 0, st>>>(
+        static_cast<const XT*>(x), v, static_cast<ST*>(s), static_cast<uint32_t*>(masks), T, N, C, HW, ncb, npb,
+        nw2, q, 0.f);
+  return cudaGetLastError() == cudaSuccess ? SF_OK : SF_ERR_CUDA;
+}
+
+template <typename XT>
+sf_status dispatch_events_s(int sdt, const void* x, float* v, void* s, void* m, int T, int N, int C, int HW,
+                            const LifParams& q, cudaStream_t st) {
+  switch (sdt) {
+    case SF_DTYPE_F32: return launch_events<XT, float>(x, v, s, m, T, N, C, HW, q, st);
+    case SF_DTYPE_F16: return launch_events<XT, __half>(x, v, s, m, T, N, C, HW, q, st);
+    case SF_DTYPE_BF16: return launch_events<XT, __nv_bfloat16>(x, v, s, m, T, N, C, HW, q, st);
+  }
+  return SF_ERR_INVALID_ARG;
+}
 }  // namespace
 }  // namespace sf
 
@@ -144,6 +294,36 @@ extern "C" sf_status sf_lif_multistep(const void* x, float* v_inout, void* spike
     case SF_DTYPE_F16: return dispatch_s<__half>(d->s_dtype, x, v_inout, spikes_out, d->numel, d->t_steps, q, st);
     case SF_DTYPE_BF16:
       return dispatch_s<__nv_bfloat16>(d->s_dtype, x, v_inout, spikes_out, d->numel, d->t_steps, q, st);
+  }
+  return SF_ERR_INVALID_ARG;
+}
+
+extern "C" sf_status sf_lif_multistep_events(const void* x, float* v_inout, void* spikes_out, void* spike_masks_out,
+                                             const sf_lif_ms_desc* d, int32_t n, int32_t c, int32_t h, int32_t w,
+                                             void* stream) {
+  if (!d || !x || !v_inout || !spikes_out || !spike_masks_out) return SF_ERR_INVALID_ARG;
+  if (n < 0 || c < 0 || h < 0 || w < 0 || d->t_steps < 0 || !(d->tau != 0.f)) return SF_ERR_INVALID_ARG;
+  if ((long long)n * c * h * w != d->numel) return SF_ERR_INVALID_ARG;
+  if (dtype_size(d->x_dtype) == 0 || dtype_size(d->s_dtype) == 0) return SF_ERR_INVALID_ARG;
+  if ((reinterpret_cast<uintptr_t>(spike_masks_out) & 7u) != 0) return SF_ERR_ALIGNMENT;
+  if ((long long)h * w * 32 > INT32_MAX) return SF_ERR_UNSUPPORTED;  // channel offsets in 32-bit
+  if (d->numel == 0 || d->t_steps == 0) return SF_OK;
+  LifParams q;
+  q.tau = d->tau;
+  q.vth = d->v_threshold;
+  q.vr = d->hard_reset ? d->v_reset : 0.f;
+  q.hard = d->hard_reset;
+  q.decay_input = d->decay_input;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int T = d->t_steps, HW = h * w;
+  switch (d->x_dtype) {
+    case SF_DTYPE_F32:
+      return dispatch_events_s<float>(d->s_dtype, x, v_inout, spikes_out, spike_masks_out, T, n, c, HW, q, st);
+    case SF_DTYPE_F16:
+      return dispatch_events_s<__half>(d->s_dtype, x, v_inout, spikes_out, spike_masks_out, T, n, c, HW, q, st);
+    case SF_DTYPE_BF16:
+      return dispatch_events_s<__nv_bfloat16>(d->s_dtype, x, v_inout, spikes_out, spike_masks_out, T, n, c, HW, q,
+                                              st);
   }
   return SF_ERR_INVALID_ARG;
 }

@@ -84,3 +84,48 @@ def test_masks_off_by_default_and_plain_lif_unchanged():
     assert not hasattr(sb, "_sf_event_masks")
     torch.testing.assert_close(sa, sb, rtol=0, atol=0)
     torch.testing.assert_close(a.v, b.v, rtol=0, atol=0)
+
+
+# Standalone LIF (the LIFNode after a BN) writing the next convolution's events.
+
+def _lif_pair(c, h, w, dtype, seed, t=3, n=2):
+    from sparseflow_b200.Ops.lif_node import LIFNode
+    g = torch.Generator().manual_seed(seed)
+    x = (torch.randn(t, n, c, h, w, generator=g) * 1.5 + 0.3).to(dtype).cuda()
+    plain = LIFNode(tau=2.0, v_threshold=1.0, v_reset=0.0)
+    ev = LIFNode(tau=2.0, v_threshold=1.0, v_reset=0.0)
+    ev.emit_event_masks = True
+    return x, plain, ev
+
+
+@pytest.mark.parametrize("c,h,w,dtype", [(64, 14, 14, torch.float32), (32, 8, 8, torch.float32),
+                                          (40, 7, 9, torch.float32), (130, 6, 6, torch.float32),
+                                          (96, 12, 10, torch.float16), (64, 5, 5, torch.bfloat16)])
+def test_lif_events_match_spikes_and_plain_lif(c, h, w, dtype):
+    x, plain, ev = _lif_pair(c, h, w, dtype, c + h)
+    s_plain = plain(x)
+    s_ev = ev(x)
+    assert torch.equal(s_ev, s_plain)
+    assert torch.equal(ev.v, plain.v)
+    masks = s_ev._sf_event_masks[0]
+    t, n = x.shape[:2]
+    want = _masks_from_spikes(s_ev.reshape(t * n, c, h, w))
+    assert 0.05 < float(s_ev.float().mean()) < 0.95
+    assert torch.equal(masks[: want.numel()].reshape(want.shape), want)
+    # A second call continues from the stored membrane, like the plain node.
+    assert torch.equal(ev(x), plain(x))
+    assert torch.equal(ev.v, plain.v)
+
+
+def test_lif_events_drive_next_conv():
+    from sparseflow_b200.Ops.sparse_conv2d import SparseConv2d
+    x, _, ev = _lif_pair(64, 16, 16, torch.float32, 5, t=2, n=3)
+    conv = nn.Conv2d(64, 48, 3, 1, 1)
+    conv.weight.data = torch.randn(48, 64, 3, 3, generator=torch.Generator().manual_seed(1)) * 0.1
+    sc = SparseConv2d.from_dense(conv.cuda())
+    s = ev(x)
+    y_masks = sc(s)
+    assert sc._last_used_event_masks
+    y_plain = sc(s.clone())
+    assert not sc._last_used_event_masks
+    torch.testing.assert_close(y_masks, y_plain, rtol=0, atol=0)
