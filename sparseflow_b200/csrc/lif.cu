@@ -12,6 +12,7 @@
 // VEC elements, keeps their v in registers across all T steps, and reads x /
 // writes spikes once: bytes = T * numel * (|x| + |spike|) + 8 * numel.
 #include <cmath>
+#include <cstdlib>
 #include "common.cuh"
 
 namespace sf {
@@ -261,13 +262,187 @@ sf_status launch_events(const void* x, float* v, void* s, void* masks, int T, in
   return cudaGetLastError() == cudaSuccess ? SF_OK : SF_ERR_CUDA;
 }
 
+// Fast path of the event-emitting LIF (C*H*W a multiple of 128, 16-byte
+// aligned tensors, an image's spikes at most kBitmapMaxBytes bits/8):
+//  1. lif_bitmap_kernel: the streaming sf_lif_multistep kernel plus four warp
+//     ballots per step, which pack each warp's 128 consecutive spikes into
+//     four 32-bit words of a flat bitmap (bit j % 32 of word j / 32 =
+//     element j of the image, j = c*H*W + p). An image's bitmap (C*H*W/8
+//     bytes) is never larger than its region of the event-mask buffer
+//     (H*W*ceil(C/64)*8 bytes), so it is written at the start of that region.
+//  2. bitmap_to_masks_kernel: one CTA per image loads the bitmap into shared
+//     memory, synchronises, and overwrites the region with the per-pixel
+//     channel masks. Each CTA touches only its own image's region.
+// The spikes are read 1/32 as often as by the mask pass over them.
+constexpr int kBmPrefetch = 4;  // steps loaded ahead in lif_bitmap_kernel
+constexpr int kBitmapMaxBytes = 200 * 1024;  // shared memory of one transpose CTA
+
+__device__ __forceinline__ uint32_t spread_nibbles(uint32_t b) {  // bit j of b (j < 8) -> bit 4j
+  b = (b | (b << 12)) & 0x000F000Fu;
+  b = (b | (b << 6)) & 0x03030303u;
+  b = (b | (b << 3)) & 0x11111111u;
+  return b;
+}
+
+template <typename XT, typename ST, bool POW2>
+__global__ void __launch_bounds__(256, 4) lif_bitmap_kernel(const XT* __restrict__ x, float* __restrict__ v,
+                                                         ST* __restrict__ s, uint32_t* __restrict__ masks,
+                                                         long long numel, int T, long long img_elems,
+                                                         long long region_words, int n_per_step, LifParams q,
+                                                         float inv_tau) {
+  constexpr int VEC = 4;
+  const long long nvec = numel / VEC;
+  const int lane = threadIdx.x & 31;
+  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+  for (long long wb = ((long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 32; wb < nvec;
+       wb += warps * 32) {
+    const long long i = wb + lane;
+    const bool ok = i < nvec;
+    LVec<float, VEC> vv{};
+    if (ok) vv = reinterpret_cast<const LVec<float, VEC>*>(v)[i];
+    // The warp's 128 elements lie in one image (img_elems % 128 == 0).
+    const long long e0 = wb * VEC;
+    const long long img_in_step = e0 / img_elems;
+    const long long j0 = e0 - img_in_step * img_elems;  // multiple of 128
+    for (int t0 = 0; t0 < T; t0 += kBmPrefetch) {
+      LVec<XT, VEC> xb[kBmPrefetch];
+#pragma unroll
+      for (int k = 0; k < kBmPrefetch; ++k)
+        if (ok && t0 + k < T)
+          xb[k] = ld_stream(reinterpret_cast<const LVec<XT, VEC>*>(x + (size_t)(t0 + k) * numel) + i);
+#pragma unroll
+      for (int k = 0; k < kBmPrefetch; ++k) {
+        if (t0 + k < T) {
+          LVec<ST, VEC> sv;
+          uint32_t b[VEC];
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) {
+            const float xe = DT<XT>::to_f(xb[k].v[e]);
+            const float sp =
+                ok ? (POW2 ? lif_update_pow2(vv.v[e], xe, q, inv_tau) : lif_update(vv.v[e], xe, q)) : 0.f;
+            sv.v[e] = DT<ST>::from_f(sp);
+            b[e] = __ballot_sync(0xffffffffu, sp != 0.f);  // bit l: element 4l + e of the warp's 128
+          }
+          if (ok) st_stream(reinterpret_cast<LVec<ST, VEC>*>(s + (size_t)(t0 + k) * numel) + i, sv);
+          if (lane < 4) {
+            // Word `lane` covers elements 32*lane .. +31 = lanes 8*lane .. +7.
+            uint32_t w = 0u;
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) w |= spread_nibbles((b[e] >> (8 * lane)) & 0xffu) << e;
+            const long long img = (long long)(t0 + k) * n_per_step + img_in_step;
+            masks[img * region_words + (j0 >> 5) + lane] = w;
+          }
+        }
+      }
+    }
+    if (ok) reinterpret_cast<LVec<float, VEC>*>(v)[i] = vv;
+  }
+}
+
+// 32x32 bit-matrix transpose across a warp: lane r holds row r (bit c =
+// element (r, c)); afterwards lane c holds column c (bit r = element (r, c)).
+// Each stage swaps the off-diagonal blocks of size s.
+__device__ __forceinline__ uint32_t warp_transpose32(uint32_t x, int lane) {
+  const uint32_t m[5] = {0x0000FFFFu, 0x00FF00FFu, 0x0F0F0F0Fu, 0x33333333u, 0x55555555u};
+#pragma unroll
+  for (int k = 0; k < 5; ++k) {
+    const int sh = 16 >> k;
+    const uint32_t y = __shfl_xor_sync(0xffffffffu, x, sh);
+    x = (lane & sh) ? ((x & ~m[k]) | ((y >> sh) & m[k])) : ((x & m[k]) | ((y & m[k]) << sh));
+  }
+  return x;
+}
+
+// One CTA per image: bitmap (start of the image's region) -> shared memory ->
+// per-pixel channel masks over the same region. A warp item is 32 pixels x
+// 32 channels: lane = channel reads its 32-pixel window of the bitmap, the
+// warp transposes, lane = pixel writes that 32-channel half word.
+__global__ void __launch_bounds__(512) bitmap_to_masks_kernel(uint32_t* __restrict__ masks, int C, int HW,
+                                                              long long region_words, int nw) {
+  extern __shared__ uint32_t bm[];
+  uint32_t* reg = masks + (size_t)blockIdx.x * region_words;
+  const int nbits_words = (int)(((long long)C * HW) >> 5);
+  for (int k = threadIdx.x; k < nbits_words; k += blockDim.x) bm[k] = reg[k];
+  if (threadIdx.x == 0) bm[nbits_words] = 0u;  // the last window's upper neighbour
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const int ngroups = (HW + 31) / 32, nhalves = 2 * nw;
+  for (int item = warp; item < ngroups * nhalves; item += nwarps) {
+    const int g = item / nhalves, hb = item - g * nhalves;
+    const int c = hb * 32 + lane, p0 = g * 32;
+    uint32_t row = 0u;
+    if (c < C) {
+      const int bit = c * HW + p0;
+      row = __funnelshift_r(bm[bit >> 5], bm[(bit >> 5) + 1], bit & 31);
+      const int np = HW - p0;
+      if (np < 32) row &= (1u << np) - 1u;  // pixels past the row belong to the next channel
+    }
+    const uint32_t col = warp_transpose32(row, lane);
+    if (p0 + lane < HW) reg[(size_t)(p0 + lane) * nhalves + hb] = col;
+  }
+}
+
+template <typename XT, typename ST>
+bool launch_events_bitmap(const void* x, float* v, void* s, void* masks, int T, int N, int C, int HW,
+                          const LifParams& q, cudaStream_t st, sf_status* status) {
+  const long long img_elems = (long long)C * HW;
+  const long long bitmap_bytes = img_elems / 8;
+  if (img_elems % 128 != 0 || bitmap_bytes > kBitmapMaxBytes) return false;
+  if (!aligned16(v) || !aligned16(x) || (reinterpret_cast<uintptr_t>(s) % (4 * sizeof(ST))) != 0 ||
+      (reinterpret_cast<uintptr_t>(masks) & 15u) != 0)
+    return false;
+  const int nw = (C + 63) / 64;
+  const long long region_words = (long long)HW * nw * 2;  // 32-bit words per image
+  const long long numel = (long long)N * C * HW;
+  const long long nvec = numel / 4;
+  const long long blocks = std::min<long long>((nvec + 255) / 256, 1ll << 30);
+  const float inv = pow2_reciprocal(q.tau);
+  if (inv != 0.f)
+    lif_bitmap_kernel<XT, ST, true><<<(unsigned)blocks, 256, 0, st>>>(
+        static_cast<const XT*>(x), v, static_cast<ST*>(s), static_cast<uint32_t*>(masks), numel, T, img_elems,
+        region_words, N, q, inv);
+  else
+    lif_bitmap_kernel<XT, ST, false><<<(unsigned)blocks, 256, 0, st>>>(
+        static_cast<const XT*>(x), v, static_cast<ST*>(s), static_cast<uint32_t*>(masks), numel, T, img_elems,
+        region_words, N, q, 0.f);
+  if (cudaGetLastError() != cudaSuccess) {
+    *status = SF_ERR_CUDA;
+    return true;
+  }
+  const int smem = (int)bitmap_bytes + 4;
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(bitmap_to_masks_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
+    *status = SF_ERR_CUDA;
+    return true;
+  }
+  const long long images = (long long)T * N;
+  if (images > INT32_MAX) {
+    *status = SF_ERR_UNSUPPORTED;
+    return true;
+  }
+  bitmap_to_masks_kernel<<<(unsigned)images, 512, smem, st>>>(static_cast<uint32_t*>(masks), C, HW, region_words,
+                                                              nw);
+  *status = cudaGetLastError() == cudaSuccess ? SF_OK : SF_ERR_CUDA;
+  return true;
+}
+
+template <typename XT, typename ST>
+sf_status launch_events_any(const void* x, float* v, void* s, void* m, int T, int N, int C, int HW,
+                            const LifParams& q, cudaStream_t st) {
+  sf_status status = SF_OK;
+  if (getenv("SF_LIF_EV_GENERAL") == nullptr &&
+      launch_events_bitmap<XT, ST>(x, v, s, m, T, N, C, HW, q, st, &status))
+    return status;
+  return launch_events<XT, ST>(x, v, s, m, T, N, C, HW, q, st);
+}
+
 template <typename XT>
 sf_status dispatch_events_s(int sdt, const void* x, float* v, void* s, void* m, int T, int N, int C, int HW,
                             const LifParams& q, cudaStream_t st) {
   switch (sdt) {
-    case SF_DTYPE_F32: return launch_events<XT, float>(x, v, s, m, T, N, C, HW, q, st);
-    case SF_DTYPE_F16: return launch_events<XT, __half>(x, v, s, m, T, N, C, HW, q, st);
-    case SF_DTYPE_BF16: return launch_events<XT, __nv_bfloat16>(x, v, s, m, T, N, C, HW, q, st);
+    case SF_DTYPE_F32: return launch_events_any<XT, float>(x, v, s, m, T, N, C, HW, q, st);
+    case SF_DTYPE_F16: return launch_events_any<XT, __half>(x, v, s, m, T, N, C, HW, q, st);
+    case SF_DTYPE_BF16: return launch_events_any<XT, __nv_bfloat16>(x, v, s, m, T, N, C, HW, q, st);
   }
   return SF_ERR_INVALID_ARG;
 }

@@ -129,3 +129,35 @@ def test_lif_events_drive_next_conv():
     y_plain = sc(s.clone())
     assert not sc._last_used_event_masks
     torch.testing.assert_close(y_masks, y_plain, rtol=0, atol=0)
+
+
+@pytest.mark.parametrize("c,h,w,tau", [(64, 14, 14, 2.0), (32, 8, 8, 3.0), (128, 7, 8, 2.0)])
+def test_lif_events_general_kernel(c, h, w, tau, monkeypatch):
+    """The lane-per-pixel kernel that serves shapes the bitmap path does not take, forced on shapes it would."""
+    from sparseflow_b200.Ops.lif_node import LIFNode
+    monkeypatch.setenv("SF_LIF_EV_GENERAL", "1")
+    g = torch.Generator().manual_seed(c)
+    x = (torch.randn(3, 2, c, h, w, generator=g) * 1.5 + 0.3).cuda()
+    plain = LIFNode(tau=tau, v_threshold=1.0, v_reset=0.0)
+    ev = LIFNode(tau=tau, v_threshold=1.0, v_reset=0.0)
+    ev.emit_event_masks = True
+    s_ev, s_plain = ev(x), plain(x)
+    assert torch.equal(s_ev, s_plain) and torch.equal(ev.v, plain.v)
+    want = _masks_from_spikes(s_ev.reshape(6, c, h, w))
+    masks = s_ev._sf_event_masks[0]
+    assert torch.equal(masks[: want.numel()].reshape(want.shape), want)
+
+
+@pytest.mark.parametrize("tau,v_reset", [(3.0, 0.0), (2.0, None), (0.5, -0.2)])
+def test_lif_events_bitmap_path_params(tau, v_reset):
+    """Bitmap path (C*H*W % 128 == 0) with non-power-of-two tau and soft / negative reset."""
+    from sparseflow_b200.Ops.lif_node import LIFNode
+    g = torch.Generator().manual_seed(11)
+    x = (torch.randn(4, 2, 64, 8, 8, generator=g) * 1.5 + 0.3).cuda()
+    plain = LIFNode(tau=tau, v_threshold=1.0, v_reset=v_reset)
+    ev = LIFNode(tau=tau, v_threshold=1.0, v_reset=v_reset)
+    ev.emit_event_masks = True
+    s_ev, s_plain = ev(x), plain(x)
+    assert torch.equal(s_ev, s_plain) and torch.equal(ev.v, plain.v)
+    want = _masks_from_spikes(s_ev.reshape(8, 64, 8, 8))
+    assert torch.equal(s_ev._sf_event_masks[0].reshape(want.shape), want)
