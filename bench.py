@@ -60,10 +60,10 @@ def parse():
     ap.add_argument("--no-extra", action="store_true", help="skip the C2/C3/prescan side measurements")
     ap.add_argument("--only-timed", action="store_true",
                     help="run only the warm-up and timed steps (no cuDNN, e2e, extras or CPU baseline); for ncu")
-    ap.add_argument("--kernel", choices=["conv", "prescan", "c2", "c3", "lif"], default="conv",
+    ap.add_argument("--kernel", choices=["conv", "prescan", "c2", "c3", "lif", "lif_events"], default="conv",
                     help="with --only-timed: time the sparse conv (default), the prescan on the same input, "
                          "the C2 1x1 cell (--images = T*N of C2, default 512), the C3 fused conv+LIF or the "
-                         "standalone LIF (--images = T*N, default 1024)")
+                         "standalone LIF, without or with the event masks (--images = T*N, default 1024)")
     ap.add_argument("--sweep", action="store_true",
                     help="C5 grid: C x H x density, sparse conv3x3 vs cuDNN and the HBM roofline (one JSON line per cell)")
     ap.add_argument("--sweep-images", type=int, default=T_STEPS * N_BATCH,
@@ -300,6 +300,27 @@ def extras(dev, hbm_peak, steps):
                                    "ms": round(ms, 4), "cudnn_conv_bn_torch_lif_ms": round(ms_ref, 4),
                                    "speedup_vs_cudnn_path": round(ms_ref / ms, 2)}
     del x3
+    # LIF -> SparseConv2d on the headline layer shape (T16 N64 C64 56x56, ~1 % spikes): the LIF
+    # writing the next convolution's event masks (LIFNode.emit_event_masks) against the plain
+    # LIF followed by the convolution's own mask pass over the spikes.
+    xl = torch.randn(T_STEPS, N_BATCH, C, H, W, device=dev, generator=g) * 0.8
+    convl = make_conv(C, C, 3, 1, 1, True, 5, device=dev)
+    scl = SparseConv2d.from_dense(convl, block_size=16)
+    scl.set_inference_mode(True)
+    chain = {}
+    for emit in (False, True):
+        lifl = LIFNode(tau=2.0, v_threshold=1.0, v_reset=0.0)
+        lifl.emit_event_masks = emit
+
+        def lif_conv():
+            lifl.reset()
+            return scl(lifl(xl))
+        chain["emit_ms" if emit else "plain_ms"] = round(cuda_time(lif_conv, steps, 3) / steps, 4)
+    lifl.reset()
+    chain["spike_density"] = round(float(lifl(xl).float().mean()), 4)
+    chain["speedup"] = round(chain["plain_ms"] / chain["emit_ms"], 3)
+    out["lif_events_to_conv"] = chain
+    del xl
     out["c4_spiking_resnet50"] = c4_resnet(dev)
     return out
 
@@ -427,7 +448,7 @@ def main():
             dist.destroy_process_group()
         return
 
-    if args.only_timed and args.kernel in ("c3", "lif"):
+    if args.only_timed and args.kernel in ("c3", "lif", "lif_events"):
         # C3 fused conv3x3 + BN-fold + LIF (T16, C128 28x28, Bernoulli(0.005)
         # spikes), or the standalone multi-step LIF on the same shape with
         # real-valued input currents N(0,1). --images sets T*N (default 16*64).
@@ -448,11 +469,14 @@ def main():
         else:
             x3 = torch.randn(16, n3, 128, 28, 28, device=dev, generator=g3)
             lif = LIFNode(tau=2.0, v_threshold=1.0, v_reset=0.0, step_mode="m")
+            lif.emit_event_masks = args.kernel == "lif_events"
 
             def step():
                 lif.reset()
                 return lif(x3)
             nb = 4 * x3.numel() * 2 + 4 * n3 * 128 * 28 * 28
+            if lif.emit_event_masks:
+                nb += 16 * n3 * 28 * 28 * 16  # event masks: 2 words of 8 bytes per pixel
         with torch.no_grad():
             ms = cuda_time(step, args.steps, args.warmup, dist) / args.steps
         if rank == 0:
