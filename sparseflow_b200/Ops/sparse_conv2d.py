@@ -108,6 +108,9 @@ class SparseConv2d(nn.Module):
 
         self.collect_diag = False
         self._last_diag = {}
+        # "dense" when a dispatch decision (Utils.dispatch_model.apply_dispatch) routes this layer to
+        # cuDNN: the module keeps its parameters and 4-D / 5-D handling and runs F.conv2d.
+        self.dispatch_backend = "sparse"
         self.profile_runtime = profile_runtime
         self._profile = _ProfileStats()
         self.backend_family = "sparse_kernel"
@@ -195,12 +198,12 @@ class SparseConv2d(nn.Module):
             raise RuntimeError("SparseConv2d runs on CUDA tensors only; the B200 path has no CPU fallback")
 
         self._last_used_event_masks = False
-        if self._supports_sparse():
+        if self._supports_sparse() and self.dispatch_backend != "dense":
             y4, backend = self._sparse_forward(x4, event_masks)
         else:
             y4 = F.conv2d(x4, self.weight, self.bias, self.stride, self.padding, self.dilation, self.groups)
             backend = "dense_fallback"
-            self.fallback_reason = "unsupported_pattern"
+            self.fallback_reason = "dispatch_dense" if self.dispatch_backend == "dense" else "unsupported_pattern"
             self._last_sparse_ms = 0.0
         if self.profile_runtime:
             if backend == "dense_fallback":

@@ -9,3 +9,16 @@ SPARSE_DENSE_RATIO_THRESHOLD = 0.85
 # The reference ships its runtime EMA/dense-fallback policy switched off
 # (Utils/config.py:43); the B200 path keeps that default and never syncs.
 ENABLE_RUNTIME_FALLBACK_POLICY = False
+
+# Execution-grounded dispatch thresholds (reference Utils/config.py:50-61): minimum dense MACs a
+# layer's sparse path must skip per tile, by kernel family; minimum saved-work fraction; margins;
+# minimum confidence for a sparse decision.
+DISPATCH_TAU_3X3 = 100_000
+DISPATCH_TAU_1X1 = 200_000
+DISPATCH_TAU_LINEAR = 800_000
+DISPATCH_TAU_ATTN_LINEAR = 900_000
+DISPATCH_TAU_ATTN_MATMUL = 1_200_000
+DISPATCH_R_MIN = 0.15
+DISPATCH_R_MARGIN = 0.0
+DISPATCH_TAU_MARGIN = 0.0
+DISPATCH_MIN_CONFIDENCE = 0.60
