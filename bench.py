@@ -60,10 +60,11 @@ def parse():
     ap.add_argument("--no-extra", action="store_true", help="skip the C2/C3/prescan side measurements")
     ap.add_argument("--only-timed", action="store_true",
                     help="run only the warm-up and timed steps (no cuDNN, e2e, extras or CPU baseline); for ncu")
-    ap.add_argument("--kernel", choices=["conv", "prescan", "c2", "c3", "lif", "lif_events"], default="conv",
+    ap.add_argument("--kernel", choices=["conv", "prescan", "c2", "c3", "lif", "lif_events", "c4"], default="conv",
                     help="with --only-timed: time the sparse conv (default), the prescan on the same input, "
                          "the C2 1x1 cell (--images = T*N of C2, default 512), the C3 fused conv+LIF or the "
-                         "standalone LIF, without or with the event masks (--images = T*N, default 1024)")
+                         "standalone LIF, without or with the event masks (--images = T*N, default 1024), or "
+                         "the C4 Spiking-ResNet50 forward after optimize()")
     ap.add_argument("--sweep", action="store_true",
                     help="C5 grid: C x H x density, sparse conv3x3 vs cuDNN and the HBM roofline (one JSON line per cell)")
     ap.add_argument("--sweep-images", type=int, default=T_STEPS * N_BATCH,
@@ -444,6 +445,28 @@ def main():
         if rank == 0:
             print(json.dumps({"kernel": "c2", "ms_per_step": round(ms, 4), "GBps": round(b2 / ms / 1e6, 1),
                               "frac_of_measured_hbm": round(b2 / ms / 1e6 / hbm_peak, 3), "images": n2}))
+        if dist is not None:
+            dist.destroy_process_group()
+        return
+
+    if args.only_timed and args.kernel == "c4":
+        # C4: one forward of the optimize()d Spiking-ResNet50 (T16 N128 3x32x32) per step.
+        import sparseflow_b200
+        from sparseflow_b200.snn import spiking_resnet50
+        from sparseflow_b200.Ops.lif_node import reset_net
+        torch.manual_seed(5)
+        model = spiking_resnet50().to(dev).eval()
+        img = torch.randn(128, 3, 32, 32, generator=torch.Generator().manual_seed(6)).to(dev)
+        x = img.unsqueeze(0).repeat(16, 1, 1, 1, 1)
+        sparseflow_b200.optimize(model, sample_input=x[:, :2], verbose=False)
+
+        def fwd():
+            reset_net(model)
+            return model(x)
+        with torch.no_grad():
+            ms = cuda_time(fwd, args.steps, args.warmup, dist) / args.steps
+        if rank == 0:
+            print(json.dumps({"kernel": "c4", "ms_per_step": round(ms, 3), "img_per_s": round(128 / (ms / 1e3), 1)}))
         if dist is not None:
             dist.destroy_process_group()
         return

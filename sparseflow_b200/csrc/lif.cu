@@ -362,7 +362,8 @@ __global__ void __launch_bounds__(512) bitmap_to_masks_kernel(uint32_t* __restri
   extern __shared__ uint32_t bm[];
   uint32_t* reg = masks + (size_t)blockIdx.x * region_words;
   const int nbits_words = (int)(((long long)C * HW) >> 5);
-  for (int k = threadIdx.x; k < nbits_words; k += blockDim.x) bm[k] = reg[k];
+#pragma unroll 8
+  for (int k = threadIdx.x; k < nbits_words; k += blockDim.x) bm[k] = __ldcs(reg + k);
   if (threadIdx.x == 0) bm[nbits_words] = 0u;  // the last window's upper neighbour
   __syncthreads();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
