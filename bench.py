@@ -351,6 +351,21 @@ def c4_resnet(dev, iters=3):
         for name, model in (("dense", dense), ("sparse", sparse)):
             ms = cuda_time(lambda: run(model), iters, 2) / iters
             res[name] = ms
+        # The same forwards replayed from CUDA graphs (one launch of the whole captured forward;
+        # about 700 kernels per forward otherwise leave the step partly bound by host launches).
+        for name, model in (("dense", dense), ("sparse", sparse)):
+            try:
+                side = torch.cuda.Stream()
+                side.wait_stream(torch.cuda.current_stream())
+                with torch.cuda.stream(side):
+                    run(model)  # warm every lazily built buffer outside the capture
+                torch.cuda.current_stream().wait_stream(side)
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    run(model)
+                res[name + "_graph"] = cuda_time(graph.replay, iters, 2) / iters
+            except Exception as e:  # noqa: BLE001 -- reported, never silently replaced
+                res[name + "_graph_error"] = str(e)[:200]
         reset_net(dense)
         reset_net(sparse)
         ref = dense(x)
@@ -360,6 +375,9 @@ def c4_resnet(dev, iters=3):
     return {"img_per_s_sparse": round(N / (res["sparse"] / 1e3), 1), "img_per_s_dense": round(N / (res["dense"] / 1e3), 1),
             "ms_sparse": round(res["sparse"], 2), "ms_dense": round(res["dense"], 2), "sparse_layers": n_sparse,
             "logits_rel_err_vs_dense": err,
+            **{f"img_per_s_{k[:-6]}_cuda_graph": round(N / (v / 1e3), 1) for k, v in res.items()
+               if k.endswith("_graph") and isinstance(v, float)},
+            **{k: v for k, v in res.items() if k.endswith("_graph_error")},
             "note": "same random-init model and input; every LIF node is one sf_lif_multistep launch in both"}
 
 

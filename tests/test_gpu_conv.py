@@ -175,6 +175,23 @@ def test_conv1x1_one_pass_matches_two_stage(monkeypatch, s):
         torch.testing.assert_close(y3, y1[:, :, ::2, ::2], rtol=1e-6, atol=1e-6)
 
 
+@pytest.mark.parametrize("h,w", [(8, 8), (3, 12), (8, 16)])
+def test_conv1x1_small_images_both_paths(monkeypatch, h, w):
+    """Images of fewer than 128 pixels take the gather kernels by default; forced onto the
+    tensor-core kernel (SF_CONV_TC_MIN_HW=1) its padded single sub-tile gives the same result."""
+    from sparseflow_b200.Kernels.conv2d import sparse_conv2d_forward
+    g = torch.Generator().manual_seed(h * w)
+    x = (torch.rand(40, 64, h, w, generator=g) < 0.05).float()
+    wt = torch.randn(256, 64, 1, 1, generator=g) * 0.1
+    b = torch.randn(256, generator=g) * 0.1
+    ref = oracle.conv2d(x.numpy(), wt.numpy(), b.numpy(), 1, 0)
+    y_default, _ = sparse_conv2d_forward(x.cuda(), wt.cuda(), b.cuda(), kernel_size=1, stride=1, padding=0)
+    monkeypatch.setenv("SF_CONV_TC_MIN_HW", "1")
+    y_tc, _ = sparse_conv2d_forward(x.cuda(), wt.cuda(), b.cuda(), kernel_size=1, stride=1, padding=0)
+    _assert_close(y_default.cpu().numpy(), ref)
+    _assert_close(y_tc.cpu().numpy(), ref)
+
+
 @pytest.mark.parametrize("wdt", [torch.float32, torch.bfloat16])
 def test_conv1x1_bf16_exact_values_on_tensor_cores(wdt):
     """Small integers and powers of two are exact in bf16, so the tensor-core 1x1 path keeps
