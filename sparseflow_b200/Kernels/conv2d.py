@@ -21,7 +21,7 @@ import torch
 import torch.nn.functional as F
 
 from .. import _lib
-from ..Utils.config import PRESCAN_ACTIVITY_EPS, SPARSE_DENSE_RATIO_THRESHOLD
+from ..Utils.config import PRESCAN_ACTIVITY_EPS, SPARSE_DENSE_RATIO_THRESHOLD, TC_MIN_PIXELS
 from ..Utils.sparse_helpers import (TILE_DENSEISH, TILE_SPARSE, TILE_ZERO, choose_group_size, popcount_buf,
                                     select_tile_sizes)
 from ._prescan_common import prescan2d
@@ -168,7 +168,10 @@ def sparse_conv2d_forward(
     if return_ms:
         se, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         se.record()
-    used_masks = event_masks is not None and (kernel_size, stride) != (1, 2)
+    # 1x1/s2 has no mask-driven kernel; a 1x1/s1 layer on images of at least one 128-pixel MMA tile
+    # runs faster on the tensor-core kernel from x itself than from the masks.
+    used_masks = (event_masks is not None and (kernel_size, stride) != (1, 2)
+                  and not (kernel_size == 1 and stride == 1 and h_in * w_in >= TC_MIN_PIXELS))
     if used_masks:
         _lib.sparse_conv2d_from_masks(event_masks, tuple(x.shape), x.dtype, w_packed, b, y, kernel_size, stride,
                                       padding)

@@ -22,3 +22,13 @@ DISPATCH_R_MIN = 0.15
 DISPATCH_R_MARGIN = 0.0
 DISPATCH_TAU_MARGIN = 0.0
 DISPATCH_MIN_CONFIDENCE = 0.60
+
+# Images of at least this many pixels run 1x1/s1 convolutions on the tcgen05 kernel (the library's
+# SF_CONV_TC_MIN_HW default); below it, and for masks handed over by a spike producer, the gather
+# kernels run.
+TC_MIN_PIXELS = 128
+
+# optimize(): the LIF nodes whose spikes feed a replaced convolution write those spikes' event masks
+# (LIFNode.emit_event_masks), so the convolution skips its mask pass. Results are identical either
+# way; SF_EMIT_EVENT_MASKS=0 in the environment turns it off.
+EMIT_EVENT_MASKS = True

@@ -30,10 +30,32 @@ def optimize(model, sample_input=None, block_sizes=None, verbose=True, threshold
         model, targets, block_sizes=block_sizes,
         sparse_kwargs={"threshold": float(threshold), "return_ms": bool(return_ms),
                        "collect_diag": bool(collect_diag), "profile_runtime": bool(profile_runtime)})
+    _enable_event_masks(model, targets)
     if verbose:
         print(f"[SparseFlow] Replacement summary: total={replaced}, sparse={sparse}, "
               f"static_zero={static_zero}, dense_keep={dense_keep}")
     return model
+
+
+def _enable_event_masks(model, targets):
+    """Spike sources (this package's LIFNode) of replaced convolutions emit the next layer's event masks.
+
+    Other spike sources (a spikingjelly neuron, say) have no such switch and are left alone; a source
+    whose output is modified before the convolution sees it loses nothing, the masks are then unused.
+    """
+    import os
+    from .Ops.sparse_conv2d import SparseConv2d
+    from .Utils.config import EMIT_EVENT_MASKS
+    if not EMIT_EVENT_MASKS or os.environ.get("SF_EMIT_EVENT_MASKS", "1") == "0":
+        return
+    for t in targets:
+        try:
+            conv = model.get_submodule(t.conv_name)
+            src = model.get_submodule(t.spike_name) if t.spike_name else None
+        except AttributeError:
+            continue
+        if isinstance(conv, SparseConv2d) and src is not None and hasattr(src, "emit_event_masks"):
+            src.emit_event_masks = True
 
 
 __all__ = ["optimize", "__version__"]

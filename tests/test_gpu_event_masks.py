@@ -41,11 +41,11 @@ def test_fused_lif_masks_match_spikes(c_in, c_out, k):
     assert torch.equal(masks.reshape(want.shape), want)
 
 
-@pytest.mark.parametrize("c_mid,k2", [(64, 3), (40, 3), (72, 1)])
-def test_next_conv_runs_from_masks(c_mid, k2):
+@pytest.mark.parametrize("c_mid,k2,hw", [(64, 3, 12), (40, 3, 12), (72, 1, 10)])
+def test_next_conv_runs_from_masks(c_mid, k2, hw):
     from sparseflow_b200.Ops.sparse_conv2d import SparseConv2d
     g = torch.Generator().manual_seed(c_mid + k2)
-    x = (torch.rand(4, 2, 32, 12, 12, generator=g) < 0.1).float().cuda()
+    x = (torch.rand(4, 2, 32, hw, hw, generator=g) < 0.1).float().cuda()
     first = _fused(32, c_mid, 3, 9)
     conv2 = nn.Conv2d(c_mid, 48, k2, 1, k2 // 2)
     conv2.weight.data = torch.randn(48, c_mid, k2, k2, generator=g) * 0.1
@@ -55,10 +55,28 @@ def test_next_conv_runs_from_masks(c_mid, k2):
     assert second._last_used_event_masks
     y_plain = second(s.clone())  # a new tensor: no masks attached, mask pass runs
     assert not second._last_used_event_masks
-    if k2 == 3:  # both runs use the same gather kernel: bit-identical
-        torch.testing.assert_close(y_masks, y_plain, rtol=0, atol=0)
-    else:  # 1x1 without masks takes the tensor-core kernel: same sums, another order
-        torch.testing.assert_close(y_masks, y_plain, rtol=1e-5, atol=1e-6)
+    # Both runs use the same gather kernel (1x1 on images below one 128-pixel MMA tile
+    # too): bit-identical.
+    torch.testing.assert_close(y_masks, y_plain, rtol=0, atol=0)
+
+
+def test_1x1_on_large_images_ignores_masks():
+    """A 1x1/s1 layer on images of at least 128 pixels runs the tensor-core kernel from the spikes
+    themselves (faster there than the mask-driven gather kernel), with the attached masks unused."""
+    from sparseflow_b200.Ops.sparse_conv2d import SparseConv2d
+    g = torch.Generator().manual_seed(3)
+    x = (torch.rand(4, 2, 32, 12, 12, generator=g) < 0.1).float().cuda()
+    first = _fused(32, 72, 3, 9)
+    conv2 = nn.Conv2d(72, 48, 1, 1, 0)
+    conv2.weight.data = torch.randn(48, 72, 1, 1, generator=g) * 0.1
+    conv2 = conv2.cuda()
+    second = SparseConv2d.from_dense(conv2)
+    s = first(x)
+    assert getattr(s, "_sf_event_masks", None) is not None
+    y = second(s)
+    assert not second._last_used_event_masks
+    ref = torch.nn.functional.conv2d(s.reshape(8, 72, 12, 12).double(), conv2.weight.double(), conv2.bias.double())
+    torch.testing.assert_close(y.reshape(8, 48, 12, 12).double(), ref, rtol=1e-5, atol=1e-5)
 
 
 def test_stale_masks_are_not_used():
