@@ -378,7 +378,7 @@ def c4_resnet(dev, iters=3):
             **{f"img_per_s_{k[:-6]}_cuda_graph": round(N / (v / 1e3), 1) for k, v in res.items()
                if k.endswith("_graph") and isinstance(v, float)},
             **{k: v for k, v in res.items() if k.endswith("_graph_error")},
-            "note": "same random-init model and input; every LIF node is one sf_lif_multistep launch in both"}
+            "note": "same random-init model and input; every LIF node is one launch of the multi-step LIF kernel (with event masks where it feeds a replaced convolution)"}
 
 
 def run_sweep(args):
