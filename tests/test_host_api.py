@@ -163,3 +163,27 @@ def test_native_argument_checks_without_gpu():
     assert lib.sf_packed_weight_bytes(128, 128, 3, 0) == 128 * 9 * 128 * 4
     cd = _lib.ConvDesc(2, 64, 56, 56, 64, 56, 56, 3, 1, 1, 0, 0, 1)
     assert lib.sf_sparse_conv2d_workspace_size(ctypes.byref(cd)) == 2 * 56 * 56 * 8 + 256
+
+
+def test_optimize_turns_on_event_masks_for_sources_of_replaced_convs(monkeypatch):
+    """optimize() makes the LIF nodes feeding replaced convolutions emit event masks; the switch
+    SF_EMIT_EVENT_MASKS=0 leaves every node as it was."""
+    import sparseflow_b200
+    from sparseflow_b200.Ops.lif_node import LIFNode
+    from sparseflow_b200.Ops.sparse_conv2d import SparseConv2d
+    from sparseflow_b200.snn import spiking_resnet50
+
+    def run():
+        torch.manual_seed(0)
+        m = spiking_resnet50().eval()
+        sparseflow_b200.optimize(m, sample_input=torch.randn(2, 2, 3, 32, 32), verbose=False)
+        return m
+
+    m = run()
+    emitting = {n for n, mod in m.named_modules() if isinstance(mod, LIFNode) and mod.emit_event_masks}
+    replaced = {n for n, mod in m.named_modules() if isinstance(mod, SparseConv2d)}
+    assert "layer1.0.conv2" in replaced and "layer1.0.sn1" in emitting and "layer1.0.sn2" in emitting
+    assert "layer3.0.sn1" not in emitting and "layer4.2.sn3" not in emitting  # their consumers stay dense
+    monkeypatch.setenv("SF_EMIT_EVENT_MASKS", "0")
+    m2 = run()
+    assert not any(isinstance(mod, LIFNode) and mod.emit_event_masks for mod in m2.modules())
