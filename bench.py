@@ -250,6 +250,22 @@ def extras(dev, hbm_peak, steps):
                          "ms": round(ms, 4), "bytes": pb}
     del x
 
+    # The headline layer with bf16 activations in and out (spikes are exact in bf16; fp32 weights,
+    # fp32 accumulation; outputs rounded to bf16): half the bytes of the fp32 cell, against cuDNN
+    # on the same bf16 tensors.
+    xb = (torch.rand(T_STEPS * N_BATCH, C, H, W, device=dev, generator=g) < DENSITY).to(torch.bfloat16)
+    convb = make_conv(C, C, 3, 1, 1, True, 1, device=dev)
+    mb = SparseConv2d.from_dense(convb, block_size=16)
+    mb.set_inference_mode(True)
+    ms_b = cuda_time(lambda: mb(xb), steps, 3) / steps
+    wb, bb = convb.weight.to(torch.bfloat16), convb.bias.to(torch.bfloat16)
+    cud_b = cuda_time(lambda: torch.nn.functional.conv2d(xb, wb, bb, 1, 1), steps, 3) / steps
+    bytes_b = conv_bytes(T_STEPS * N_BATCH, C, H, W, C, H, W, 3, esz=2)
+    out["c5_bf16_io"] = {"ms": round(ms_b, 4), "GBps": round(bytes_b / ms_b / 1e6, 1),
+                         "frac_of_measured_hbm": round(bytes_b / ms_b / 1e6 / hbm_peak, 3),
+                         "cudnn_bf16_ms": round(cud_b, 4), "speedup_vs_cudnn_bf16": round(cud_b / ms_b, 2)}
+    del xb
+
     # C2: 1x1 256->64, T16 N32 56x56 block-clustered spikes, bf16 weights.
     n2 = 16 * 32
     blk = (torch.rand(n2, 256, 4, 4, device=dev, generator=g) < 0.05).float()
