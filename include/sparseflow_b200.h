@@ -114,6 +114,13 @@ sf_status sf_prescan2d_static_ws(const void* x, const sf_prescan_desc* d,
                                  int32_t* ag_mask, int32_t* tile_class,
                                  int32_t* active_ids, int32_t* active_count, void* stream);
 
+/* Error word of the most recent sf_prescan2d_static_ws call on the current
+ * device (synchronous on `stream`): SF_OK, or SF_ERR_DEVICE_TIMEOUT when one
+ * of that call's bounded look-back waits ran out (its active_ids are then not
+ * valid). The next sf_prescan2d_static_ws call clears the word, so read it
+ * before that. Not for hot loops. */
+sf_status sf_prescan2d_static_ws_status(void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Stage 2: gather-style sparse convolution (deterministic, atomic-free).    */
 /* ------------------------------------------------------------------------ */
@@ -233,6 +240,31 @@ sf_status sf_lif_multistep(const void* x, float* v_inout, void* spikes_out, cons
 sf_status sf_lif_multistep_events(const void* x, float* v_inout, void* spikes_out, void* spike_masks_out,
                                   const sf_lif_ms_desc* d, int32_t n, int32_t c, int32_t h, int32_t w,
                                   void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Path policy (process-wide; no counterpart in the reference, whose        */
+/* dispatch lives in Kernels/conv2d.py:1026-1178 as fixed Python rules).     */
+/* ------------------------------------------------------------------------ */
+enum {
+  /* 1x1 stride-1 convolutions: 0 automatic (tcgen05 kernel where it applies),
+   * 1 two-stage gather path (mask pass + gather kernel), 2 one-pass CUDA-core
+   * pointwise kernel. */
+  SF_POLICY_CONV1X1_PATH = 0,
+  /* Images with fewer pixels than this run 1x1/s1 on the gather kernels
+   * (default 128: one MMA tile; smaller maps leave most of a tile empty). */
+  SF_POLICY_CONV1X1_TC_MIN_HW = 1,
+  /* 3x3 convolutions: 0 automatic, 1 gather kernel only, 2 tcgen05 implicit
+   * GEMM wherever it supports the shape. */
+  SF_POLICY_CONV3X3_PATH = 2,
+  /* 1: sf_lif_multistep_events always uses its general lane-per-pixel kernel. */
+  SF_POLICY_LIF_EVENTS_GENERAL = 3,
+  SF_POLICY_COUNT = 4
+};
+/* Sets a policy value (>= 0) for every later call in this process. Returns
+ * SF_ERR_INVALID_ARG for an unknown key or a negative value. */
+sf_status sf_set_path_policy(int32_t key, int64_t value);
+/* Current value of a policy key, -1 for an unknown key. */
+int64_t sf_get_path_policy(int32_t key);
 
 /* ------------------------------------------------------------------------ */
 /* Diagnostics.                                                              */

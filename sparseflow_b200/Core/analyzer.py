@@ -110,6 +110,10 @@ def _reset_states(model: nn.Module) -> None:
     reset_net(model)
 
 
+_LEAF_LAYERS = (nn.modules.conv._ConvNd, nn.modules.batchnorm._BatchNorm, nn.modules.pooling._MaxPoolNd,
+                nn.modules.pooling._AvgPoolNd, nn.Linear)
+
+
 class NetworkAnalyzer:
     FALLBACK_SEARCH_WINDOW = 15
     MAX_BFS_DEPTH = 20
@@ -174,7 +178,20 @@ class NetworkAnalyzer:
 
     # -- mode 1: torch.fx -----------------------------------------------------------
     def _analyze_fx(self, model, shapes) -> List[ReplacementTarget]:
-        gm = torch.fx.symbolic_trace(model)
+        registry = self.registry
+
+        class _SpikeLeafTracer(torch.fx.Tracer):
+            # Spike sources, and subclasses of torch's conv / norm / pool / linear
+            # layers (multi-step wrappers that fold T into the batch), are graph
+            # leaves: their bodies branch on runtime state (membrane shape, input
+            # rank, device), which symbolic tracing cannot follow, and the
+            # analyzer only needs their call sites.
+            def is_leaf_module(self, m, qualname):
+                return (registry.is_spike_op(m) or isinstance(m, _LEAF_LAYERS)
+                        or super().is_leaf_module(m, qualname))
+
+        graph = _SpikeLeafTracer().trace(model)
+        gm = torch.fx.GraphModule(model, graph)
         modules = dict(gm.named_modules())
         is_spike = lambda node: (node.op == "call_module"  # noqa: E731
                                  and self.registry.is_spike_op(modules.get(node.target)))

@@ -1,78 +1,56 @@
-"""Spike-source and target-op registry (reference: Core/registry.py:15-109).
+"""Which modules count as spike sources for the analyzer.
 
-The default registry recognises spikingjelly's LIF/IF/ParametricLIF nodes
-when spikingjelly is importable, plus this package's own ``LIFNode``.
+Public surface kept from the reference (Core/registry.py:15-109):
+``SpikeOpRegistry.default()``, ``register`` and ``is_spike_op``. This build
+replaces only 3x3 / 1x1 Conv2d layers fed by a spike source, so the registry
+holds spike-source types and nothing else; the analyzer decides which
+convolutions qualify.
 """
 from __future__ import annotations
 
-from typing import Tuple, Type
+import functools
+from typing import Iterable, Tuple, Type
 
 import torch.nn as nn
 
-_DEFAULT_SPIKE_OPS = None
 
-
-def _get_default_spike_ops() -> Tuple[type, ...]:
-    global _DEFAULT_SPIKE_OPS
-    if _DEFAULT_SPIKE_OPS is None:
-        from ..Ops.lif_node import LIFNode
-        ops = [LIFNode]
-        try:
-            from spikingjelly.activation_based import neuron as sj_neuron
-            ops += [sj_neuron.LIFNode, sj_neuron.IFNode, sj_neuron.ParametricLIFNode]
-        except ImportError:
-            pass
-        _DEFAULT_SPIKE_OPS = tuple(ops)
-    return _DEFAULT_SPIKE_OPS
+@functools.lru_cache(maxsize=1)
+def _known_spike_sources() -> Tuple[type, ...]:
+    """This package's LIFNode, plus spikingjelly's neuron classes when that
+    package is importable (it is an optional dependency)."""
+    from ..Ops.lif_node import LIFNode
+    found = [LIFNode]
+    try:
+        from spikingjelly.activation_based import neuron
+    except ImportError:
+        return tuple(found)
+    for name in ("LIFNode", "IFNode", "ParametricLIFNode"):
+        cls = getattr(neuron, name, None)
+        if isinstance(cls, type):
+            found.append(cls)
+    return tuple(found)
 
 
 class SpikeOpRegistry:
-    def __init__(self):
-        self._spike_op_types: list = []
-        self._target_op_types: list = [nn.Conv1d, nn.Conv2d, nn.Conv3d, nn.Linear]
+    """An ordered set of module types whose outputs are spikes."""
 
-    def register(self, op_type: Type[nn.Module]):
-        if op_type not in self._spike_op_types:
-            self._spike_op_types.append(op_type)
-        return self
-
-    def register_many(self, op_types):
-        for t in op_types:
+    def __init__(self, spike_types: Iterable[Type[nn.Module]] = ()):
+        self._types: Tuple[type, ...] = ()
+        for t in spike_types:
             self.register(t)
+
+    def register(self, op_type: Type[nn.Module]) -> "SpikeOpRegistry":
+        if op_type not in self._types:
+            self._types = self._types + (op_type,)
         return self
 
-    def register_target(self, op_type: Type[nn.Module]):
-        if op_type not in self._target_op_types:
-            self._target_op_types.append(op_type)
-        return self
-
-    def is_spike_op(self, module: nn.Module) -> bool:
-        return bool(self._spike_op_types) and isinstance(module, tuple(self._spike_op_types))
-
-    def is_target_conv1d(self, module: nn.Module) -> bool:
-        return isinstance(module, nn.Conv1d)
-
-    def is_target_conv2d(self, module: nn.Module) -> bool:
-        return isinstance(module, nn.Conv2d)
-
-    def is_target_conv3d(self, module: nn.Module) -> bool:
-        return isinstance(module, nn.Conv3d)
-
-    def is_target_linear(self, module: nn.Module) -> bool:
-        return isinstance(module, nn.Linear)
-
-    def is_target_depthwise_conv2d(self, module: nn.Module) -> bool:
-        return (isinstance(module, nn.Conv2d) and module.groups == module.in_channels
-                and module.out_channels == module.in_channels)
+    def is_spike_op(self, module) -> bool:
+        return bool(self._types) and isinstance(module, self._types)
 
     @property
-    def spike_op_types(self) -> Tuple:
-        return tuple(self._spike_op_types)
-
-    @property
-    def target_op_types(self) -> Tuple:
-        return tuple(self._target_op_types)
+    def spike_op_types(self) -> Tuple[type, ...]:
+        return self._types
 
     @classmethod
     def default(cls) -> "SpikeOpRegistry":
-        return cls().register_many(_get_default_spike_ops())
+        return cls(_known_spike_sources())

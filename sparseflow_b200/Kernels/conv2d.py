@@ -193,7 +193,3 @@ def sparse_conv2d_forward(
         meta["active_tiles"] = active_tiles
     return _finalize(y, ms, avg_ratio, tile_stats, meta)
 
-
-# Reference-compatible aliases.
-choose_group_size = choose_group_size
-TILE_ZERO, TILE_SPARSE, TILE_DENSEISH = TILE_ZERO, TILE_SPARSE, TILE_DENSEISH

@@ -7,6 +7,7 @@ library is missing or a call fails, the error propagates to the caller.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import threading
 from pathlib import Path
@@ -30,6 +31,8 @@ SF_ERR_DEVICE_TIMEOUT = 6
 
 SF_DTYPE_F32, SF_DTYPE_F16, SF_DTYPE_BF16 = 0, 1, 2
 SF_LAYOUT_NCHW, SF_LAYOUT_NHWC = 0, 1
+# Path policy keys (sf_set_path_policy).
+SF_POLICY_CONV1X1_PATH, SF_POLICY_CONV1X1_TC_MIN_HW, SF_POLICY_CONV3X3_PATH, SF_POLICY_LIF_EVENTS_GENERAL = 0, 1, 2, 3
 
 _TORCH2SF = {torch.float32: SF_DTYPE_F32, torch.float16: SF_DTYPE_F16, torch.bfloat16: SF_DTYPE_BF16}
 
@@ -94,6 +97,7 @@ _SIGNATURES = {
                                       ctypes.c_size_t, _VP]),
     "sf_prescan2d_status": (ctypes.c_int32, [_VP, _VP]),
     "sf_prescan2d_static_ws": (ctypes.c_int32, [_VP, ctypes.POINTER(PrescanDesc), _VP, _VP, _VP, _VP, _VP]),
+    "sf_prescan2d_static_ws_status": (ctypes.c_int32, [_VP]),
     "sf_packed_weight_bytes": (ctypes.c_size_t, [ctypes.c_int32] * 4),
     "sf_pack_weights": (ctypes.c_int32, [_VP, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                          ctypes.c_int32, _VP, _VP]),
@@ -108,6 +112,8 @@ _SIGNATURES = {
                                                  ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _VP]),
     "sf_event_masks_bytes": (ctypes.c_size_t, [ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]),
     "sf_selftest_bounded_wait": (ctypes.c_int32, [ctypes.c_uint64, _VP]),
+    "sf_set_path_policy": (ctypes.c_int32, [ctypes.c_int32, ctypes.c_int64]),
+    "sf_get_path_policy": (ctypes.c_int64, [ctypes.c_int32]),
     "sf_sparse_conv2d_from_masks": (ctypes.c_int32, [_VP, _VP, _VP, _VP, ctypes.POINTER(ConvDesc), _VP]),
 }
 
@@ -328,3 +334,21 @@ def lif_multistep_events(x: torch.Tensor, v: torch.Tensor, spikes: torch.Tensor,
     st = load().sf_lif_multistep_events(_ptr(x), _ptr(v), _ptr(spikes), _ptr(masks), ctypes.byref(desc), n, c, h, w,
                                         _stream(x.device))
     _check("sf_lif_multistep_events", st)
+
+
+def set_path_policy(key: int, value: int) -> int:
+    """Sets a process-wide path policy value; returns the previous one."""
+    lib = load()
+    prev = int(lib.sf_get_path_policy(key))
+    _check("sf_set_path_policy", lib.sf_set_path_policy(key, int(value)))
+    return prev
+
+
+@contextlib.contextmanager
+def path_policy(key: int, value: int):
+    """with path_policy(SF_POLICY_CONV3X3_PATH, 1): ... -- the policy applies inside the block only."""
+    prev = set_path_policy(key, value)
+    try:
+        yield
+    finally:
+        set_path_policy(key, prev)

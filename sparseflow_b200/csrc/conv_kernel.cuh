@@ -79,10 +79,12 @@ inline int weight_block_cpl(int C, int K, int Co, int wsz) {
     if ((size_t)C * K * K * 32 * cpl * wsz <= kWsmemMax) return cpl;
   }
   // No block fits shared memory: weights are read from L2. Four slices per
-  // lane walk each event for 128 output channels at once (4-pixel segments);
-  // SF_CONV_L2_CPL=2 keeps 8-pixel segments with sector-complete stores.
+  // lane walk each event for 128 output channels at once (4-pixel segments).
+#ifdef SF_DEV_KNOBS
+  // Development builds: SF_CONV_L2_CPL=2 keeps 8-pixel segments.
   const char* e = getenv("SF_CONV_L2_CPL");
   if (e && atoi(e) == 2) return slices >= 2 ? 2 : 1;
+#endif
   return slices >= 4 ? 4 : (slices >= 2 ? 2 : 1);
 }
 

@@ -14,6 +14,7 @@
 #include <cmath>
 #include <cstdlib>
 #include "common.cuh"
+#include "policy.cuh"
 
 namespace sf {
 namespace {
@@ -431,7 +432,7 @@ template <typename XT, typename ST>
 sf_status launch_events_any(const void* x, float* v, void* s, void* m, int T, int N, int C, int HW,
                             const LifParams& q, cudaStream_t st) {
   sf_status status = SF_OK;
-  if (getenv("SF_LIF_EV_GENERAL") == nullptr &&
+  if (policy(SF_POLICY_LIF_EVENTS_GENERAL) == 0 &&
       launch_events_bitmap<XT, ST>(x, v, s, m, T, N, C, HW, q, st, &status))
     return status;
   return launch_events<XT, ST>(x, v, s, m, T, N, C, HW, q, st);

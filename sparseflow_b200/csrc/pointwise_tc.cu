@@ -40,6 +40,7 @@
 #include <cudaTypedefs.h>
 #include <cstdlib>
 #include "conv_kernel.cuh"
+#include "policy.cuh"
 
 namespace sf {
 namespace pwtc {
@@ -467,7 +468,7 @@ sf_status dispatch_w(int wdt, const TcParams& p, const CUtensorMap& xmap, size_t
 
 // Returns SF_ERR_UNSUPPORTED for shapes it does not take (the caller then
 // runs the two-stage path): C_out > 256, C_in > 512, images smaller than one
-// 128-pixel MMA tile (SF_CONV_TC_MIN_HW, default 128: on 8x8 maps half of
+// 128-pixel MMA tile (SF_POLICY_CONV1X1_TC_MIN_HW, default 128: on 8x8 maps half of
 // every tile would be padding and the gather kernels measured faster), H*W
 // rows that TMA cannot address (H*W*element size not a multiple of 16, x not
 // 16-byte aligned), or operands beyond shared memory.
@@ -476,8 +477,7 @@ sf_status run_pointwise_tc(const void* x, const void* w_packed, const float* bia
   if (Co > 256 || Co <= 0 || C <= 0 || C > 512) return SF_ERR_UNSUPPORTED;
   const int esz = (int)dtype_size(xdt);
   const long long HW = (long long)H * W;
-  const char* mh = getenv("SF_CONV_TC_MIN_HW");
-  if (HW < (mh ? atoll(mh) : 128)) return SF_ERR_UNSUPPORTED;
+  if (HW < policy(SF_POLICY_CONV1X1_TC_MIN_HW)) return SF_ERR_UNSUPPORTED;
   if ((HW * esz) % 16 != 0 || (reinterpret_cast<uintptr_t>(x) & 15u) != 0) return SF_ERR_UNSUPPORTED;
   auto enc = encoder();
   if (!enc) return SF_ERR_UNSUPPORTED;

@@ -796,5 +796,17 @@ extern "C" sf_status sf_prescan2d_static_ws(const void* x, const sf_prescan_desc
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(ws, 0, 8, st) != cudaSuccess) return SF_ERR_CUDA;
   if (cudaMemsetAsync(static_cast<char*>(ws) + 12, 0, 4, st) != cudaSuccess) return SF_ERR_CUDA;
-  return sf_prescan2d(x, d, ag_mask, tile_class, active_ids, active_count, ws, kStaticWsBytes, stream);
+  // Passing exactly the look-back size selects the one-pass kernel for every
+  // shape: the two-pass path would write per-pixel group words over the
+  // status words that a later one-pass call reads as predecessor state.
+  return sf_prescan2d(x, d, ag_mask, tile_class, active_ids, active_count, ws, need, stream);
+}
+
+extern "C" sf_status sf_prescan2d_static_ws_status(void* stream) {
+  uint32_t err = 0;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (cudaMemcpyFromSymbolAsync(&err, g_prescan_static_ws, 4, 12, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+    return SF_ERR_CUDA;
+  if (cudaStreamSynchronize(st) != cudaSuccess) return SF_ERR_CUDA;
+  return err ? SF_ERR_DEVICE_TIMEOUT : SF_OK;
 }

@@ -6,6 +6,7 @@
 #include <cstring>
 #include <cudaTypedefs.h>
 #include "conv_kernel.cuh"
+#include "policy.cuh"
 #include "events.cuh"
 
 namespace sf {
@@ -60,28 +61,34 @@ __global__ void pack_weights_kernel(const void* __restrict__ w, int src_dtype, W
   }
 }
 
-int env_int(const char* name) {
+// Tuning overrides for development builds only (-DSF_DEV_KNOBS): they pin
+// plan choices from the environment. Release builds read no environment.
+int dev_knob(const char* name) {
+#ifdef SF_DEV_KNOBS
   const char* v = getenv(name);
   return v ? atoi(v) : 0;
+#else
+  (void)name;
+  return 0;
+#endif
 }
 
 // Launch plan: 32-channel slices per lane (CPL, fixed by the weight packing),
 // row-segment length R, band height TH (one row segment per compute warp),
 // mask stages, and whether a block of packed weights lives in shared memory.
-// SF_CONV_TH / SF_CONV_NSTAGE / SF_CONV_NO_WSMEM (environment) pin choices for
-// tuning.
+// Development builds can pin these choices (dev_knob).
 bool make_plan(int K, int S, int C, int W, int Co, int Ho, int Wo, int nw, int wsz, int esz, bool y_tma_ok,
                bool lif, Plan& pl) {
   const int B = lif ? 1 : kRowsPerWarp;  // output rows per compute warp (matches the kernel)
-  const int force_th = env_int("SF_CONV_TH"), force_ns = env_int("SF_CONV_NSTAGE");
+  const int force_th = dev_knob("SF_CONV_TH"), force_ns = dev_knob("SF_CONV_NSTAGE");
   const int bar_bytes = (2 * kMaxStages + 1) * 8;
   const int cpl = weight_block_cpl(C, K, Co, wsz);
   const size_t w_bytes = (size_t)C * K * K * 32 * cpl * wsz;
-  const bool ws_ok = w_bytes <= kWsmemMax && env_int("SF_CONV_NO_WSMEM") == 0;
+  const bool ws_ok = w_bytes <= kWsmemMax && dev_knob("SF_CONV_NO_WSMEM") == 0;
   const int R = cpl == 4 ? 4 : 8;
   // TMA tensor stores need 16-byte row pitch and 16-byte tile rows.
   // Off unless SF_CONV_TMA_STORE=1: plain sector-complete stores measured faster.
-  const bool tma_ok = y_tma_ok && (Wo * esz) % 16 == 0 && (R * esz) % 16 == 0 && env_int("SF_CONV_TMA_STORE") == 1;
+  const bool tma_ok = y_tma_ok && (Wo * esz) % 16 == 0 && (R * esz) % 16 == 0 && dev_knob("SF_CONV_TMA_STORE") == 1;
   for (int combo = 0; combo < 4; ++combo) {
     const int wsmem = (combo < 2) ? (ws_ok ? 1 : -1) : 0;  // prefer weights in smem, then TMA stores
     const int tma = (combo % 2 == 0) ? (tma_ok ? 1 : -1) : 0;
@@ -205,7 +212,7 @@ sf_status run_conv(const void* x, const void* w_packed, const float* bias, void*
   if (!workspace && !masks_in) return SF_ERR_WORKSPACE;
   if (!aligned16(w_packed)) return SF_ERR_ALIGNMENT;
   // 1x1 stride 1: tcgen05 GEMM tiles over x streamed once (pointwise_tc.cu).
-  if (!lif && !masks_in && K == 1 && S == 1 && P == 0 && env_int("SF_CONV_TC_OFF") == 0) {
+  if (!lif && !masks_in && K == 1 && S == 1 && P == 0 && policy(SF_POLICY_CONV1X1_PATH) == 0) {
     uint32_t* err = nullptr;
     if (cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_conv_error) != cudaSuccess) return SF_ERR_CUDA;
     s = pwtc::run_pointwise_tc(x, w_packed, bias, y, err, T * N, C, H, W, Co, xdt, wdt, st);
@@ -214,8 +221,8 @@ sf_status run_conv(const void* x, const void* w_packed, const float* bias, void*
   // 1x1 stride 2: one pass over x with masks built in shared memory
   // (pointwise.cu). For stride 1 that kernel measured slower than the two
   // stages (0.74 vs 0.54 ms on the C2 cell; both issue-bound), so it runs
-  // only when SF_CONV_PW=1 asks for it.
-  if (!lif && !masks_in && K == 1 && (S == 2 || env_int("SF_CONV_PW") == 1)) {
+  // only when the SF_POLICY_CONV1X1_PATH policy asks for it.
+  if (!lif && !masks_in && K == 1 && (S == 2 || policy(SF_POLICY_CONV1X1_PATH) == 2)) {
     s = pw::run_pointwise(x, w_packed, bias, y, T * N, C, H, W, Co, Ho, Wo, S, xdt, wdt, st);
     if (s != SF_ERR_UNSUPPORTED) return s;
   }

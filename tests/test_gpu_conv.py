@@ -62,6 +62,18 @@ GRID = [
     (2, 256, 28, 28, 512, 1, 2, 0, 0.02),
     (1, 1000, 7, 7, 40, 1, 1, 0, 0.05),
     (2, 64, 56, 56, 256, 1, 1, 0, 1.0),
+    # 3x3 sweep corners: weights past shared memory (read from L2, 4 slices per lane),
+    # dense (0.2) and nearly empty (0.001) inputs
+    (2, 256, 14, 14, 256, 3, 1, 1, 0.2),
+    (1, 256, 28, 28, 256, 3, 1, 1, 0.001),
+    (1, 512, 14, 14, 512, 3, 1, 1, 0.2),
+    (1, 512, 28, 28, 512, 3, 1, 1, 0.001),
+    (2, 64, 56, 56, 64, 3, 1, 1, 0.2),
+    (2, 128, 28, 28, 128, 3, 1, 1, 0.2),
+    # every shared-memory weight block width: CPL 1 (C128->128), 2 (C64->128), 4 (C32->128)
+    (2, 128, 28, 28, 128, 3, 1, 1, 0.01),
+    (2, 64, 28, 28, 128, 3, 1, 1, 0.05),
+    (2, 32, 28, 28, 128, 3, 1, 1, 0.05),
 ]
 
 
@@ -107,6 +119,24 @@ def test_conv_bf16_weights_c2_like():
     y = sp(x.cuda())
     ref = oracle.conv2d(x.reshape(8, 256, 56, 56).numpy(), w_ref, None, 1, 0)
     _assert_close(y.reshape(8, 64, 56, 56).cpu().numpy(), ref, rtol=1e-5)
+
+
+def test_c1_full_shape_through_sparse_conv2d():
+    """BASELINE config C1 at full shape: [T=4, N=8, 64, 32, 32], Bernoulli(0.02), kaiming weights,
+    bias, block 16, through SparseConv2d (5-D in, 5-D out) against the oracle."""
+    from sparseflow_b200.Ops.sparse_conv2d import SparseConv2d
+    g = torch.Generator().manual_seed(2024)
+    conv = nn.Conv2d(64, 64, 3, 1, 1, bias=True)
+    w = torch.empty(64, 64, 3, 3)
+    nn.init.kaiming_normal_(w, generator=g)
+    conv.weight.data.copy_(w)
+    conv.bias.data.copy_(torch.randn(64, generator=g) * 0.1)
+    x = (torch.rand(4, 8, 64, 32, 32, generator=g) < 0.02).float()
+    sp = SparseConv2d.from_dense(conv.cuda(), block_size=16)
+    y = sp(x.cuda())
+    assert y.shape == (4, 8, 64, 32, 32)
+    ref = oracle.conv2d(x.reshape(32, 64, 32, 32).numpy(), w.numpy(), conv.bias.detach().cpu().numpy(), 1, 1)
+    _assert_close(y.reshape(32, 64, 32, 32).cpu().numpy(), ref)
 
 
 def test_conv_deterministic_and_5d_shape():
@@ -159,26 +189,30 @@ def test_conv_metadata_buffers_match_prescan():
 
 
 @pytest.mark.parametrize("s", [1, 2])
-def test_conv1x1_one_pass_matches_two_stage(monkeypatch, s):
-    """The one-pass 1x1 kernel and the two-stage (mask pass + gather) path give the same result."""
+def test_conv1x1_one_pass_matches_two_stage(s):
+    """The one-pass 1x1 kernel, the two-stage (mask pass + gather) path and the tcgen05 kernel agree."""
+    from sparseflow_b200 import _lib
     from sparseflow_b200.Kernels.conv2d import sparse_conv2d_forward
     g = torch.Generator().manual_seed(21)
     x = (torch.rand(4, 128, 28, 28, generator=g) < 0.03).float().cuda()
     wt = (torch.randn(64, 128, 1, 1, generator=g) * 0.1).cuda()
     y1, _ = sparse_conv2d_forward(x, wt, None, kernel_size=1, stride=1, padding=0)
-    monkeypatch.setenv("SF_CONV_PW", "1")
-    y2, _ = sparse_conv2d_forward(x, wt, None, kernel_size=1, stride=1, padding=0)
+    with _lib.path_policy(_lib.SF_POLICY_CONV1X1_PATH, 2):
+        y2, _ = sparse_conv2d_forward(x, wt, None, kernel_size=1, stride=1, padding=0)
+    with _lib.path_policy(_lib.SF_POLICY_CONV1X1_PATH, 1):
+        y4, _ = sparse_conv2d_forward(x, wt, None, kernel_size=1, stride=1, padding=0)
     torch.testing.assert_close(y1, y2, rtol=1e-6, atol=1e-6)
+    torch.testing.assert_close(y1, y4, rtol=1e-6, atol=1e-6)
     if s == 2:
-        monkeypatch.delenv("SF_CONV_PW")
         y3, _ = sparse_conv2d_forward(x, wt, None, kernel_size=1, stride=2, padding=0)
         torch.testing.assert_close(y3, y1[:, :, ::2, ::2], rtol=1e-6, atol=1e-6)
 
 
 @pytest.mark.parametrize("h,w", [(8, 8), (3, 12), (8, 16)])
-def test_conv1x1_small_images_both_paths(monkeypatch, h, w):
+def test_conv1x1_small_images_both_paths(h, w):
     """Images of fewer than 128 pixels take the gather kernels by default; forced onto the
-    tensor-core kernel (SF_CONV_TC_MIN_HW=1) its padded single sub-tile gives the same result."""
+    tensor-core kernel (SF_POLICY_CONV1X1_TC_MIN_HW = 1) its padded single sub-tile gives the same result."""
+    from sparseflow_b200 import _lib
     from sparseflow_b200.Kernels.conv2d import sparse_conv2d_forward
     g = torch.Generator().manual_seed(h * w)
     x = (torch.rand(40, 64, h, w, generator=g) < 0.05).float()
@@ -186,8 +220,8 @@ def test_conv1x1_small_images_both_paths(monkeypatch, h, w):
     b = torch.randn(256, generator=g) * 0.1
     ref = oracle.conv2d(x.numpy(), wt.numpy(), b.numpy(), 1, 0)
     y_default, _ = sparse_conv2d_forward(x.cuda(), wt.cuda(), b.cuda(), kernel_size=1, stride=1, padding=0)
-    monkeypatch.setenv("SF_CONV_TC_MIN_HW", "1")
-    y_tc, _ = sparse_conv2d_forward(x.cuda(), wt.cuda(), b.cuda(), kernel_size=1, stride=1, padding=0)
+    with _lib.path_policy(_lib.SF_POLICY_CONV1X1_TC_MIN_HW, 1):
+        y_tc, _ = sparse_conv2d_forward(x.cuda(), wt.cuda(), b.cuda(), kernel_size=1, stride=1, padding=0)
     _assert_close(y_default.cpu().numpy(), ref)
     _assert_close(y_tc.cpu().numpy(), ref)
 

@@ -150,10 +150,15 @@ def test_lif_events_drive_next_conv():
 
 
 @pytest.mark.parametrize("c,h,w,tau", [(64, 14, 14, 2.0), (32, 8, 8, 3.0), (128, 7, 8, 2.0)])
-def test_lif_events_general_kernel(c, h, w, tau, monkeypatch):
+def test_lif_events_general_kernel(c, h, w, tau):
     """The lane-per-pixel kernel that serves shapes the bitmap path does not take, forced on shapes it would."""
+    from sparseflow_b200 import _lib
+    with _lib.path_policy(_lib.SF_POLICY_LIF_EVENTS_GENERAL, 1):
+        _lif_events_general_body(c, h, w, tau)
+
+
+def _lif_events_general_body(c, h, w, tau):
     from sparseflow_b200.Ops.lif_node import LIFNode
-    monkeypatch.setenv("SF_LIF_EV_GENERAL", "1")
     g = torch.Generator().manual_seed(c)
     x = (torch.randn(3, 2, c, h, w, generator=g) * 1.5 + 0.3).cuda()
     plain = LIFNode(tau=tau, v_threshold=1.0, v_reset=0.0)

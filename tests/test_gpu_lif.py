@@ -12,11 +12,6 @@ pytestmark = pytest.mark.gpu
 LIF = load_cases("lif")
 
 
-def _check_spikes(sp, ref_sp, v_trace_ok=None):
-    mism = np.argwhere(sp != ref_sp)
-    return mism
-
-
 @pytest.mark.parametrize("case", sorted(LIF))
 def test_fused_lif_matches_reference_golden(case):
     from sparseflow_b200.Ops.sparse_fused_conv_lif import FusedSparseConvLIF
@@ -120,14 +115,10 @@ def test_fused_lif_tau_values_match_oracle(tau):
     v0 = torch.zeros(2, 24, 10, 10)
     s, v, _ = sparse_fused_conv_lif_forward(x.cuda(), v0.cuda(), w.cuda(), b.cuda(), tau, 1.0, 0.0, True,
                                             kernel_size=3, stride=1, padding=1)
-    vo = np.zeros((2, 24, 10, 10), dtype=np.float32)
-    for t in range(6):
-        cur = oracle.conv2d(x[t].numpy(), w.numpy(), b.numpy(), 1, 1).astype(np.float32)
-        so, vo = oracle.lif_step(cur.reshape(-1), vo.reshape(-1), tau, 1.0, 0.0, True)
-        vo = vo.reshape(2, 24, 10, 10)
-        got = s[t].cpu().numpy().reshape(-1)
-        # fp32 vs double conv sums: a spike may flip only where v sits within ~1e-6 of v_th
-        assert (got == so).mean() > 0.999
+    so, near, vo = oracle.conv_lif_near(x.numpy(), w.numpy(), b.numpy(), v0.numpy(), 1, 1, tau, 1.0, 0.0, True)
+    # Spikes identical except where the membrane is within 1e-5 of v_th.
+    assert oracle.spikes_match(s.cpu().numpy(), so, near)
+    assert so.mean() > 0.01
     assert np.abs(v.cpu().numpy() - vo).max() < 1e-4
 
 

@@ -71,6 +71,37 @@ def test_static_workspace_prescan_matches_regular_twice():
         _same(ref, first)
         _same(ref, second)
         assert 0 < int(first[3].item()) < n_tiles
+    from sparseflow_b200 import _lib
+    assert _lib.load().sf_prescan2d_static_ws_status(torch.cuda.current_stream().cuda_stream) == 0
+
+
+def test_static_workspace_after_other_shapes_with_nan_groups():
+    """A third shape after the two above (a different tile-row count), with
+    NaN-poisoned channel groups: bit-exact against sf_prescan2d and the oracle,
+    and the array's error word reads clear afterwards."""
+    from oracle import oracle
+    from sparseflow_b200 import _lib
+    g = torch.Generator().manual_seed(7)
+    for (n, c, h, w, p) in [(64, 64, 56, 56, 0.0003), (19, 40, 30, 30, 0.004)]:
+        x = (torch.rand(n, c, h, w, generator=g) < p).float()
+        if c == 40:
+            x[3, 17, 5, 9] = float("nan")
+            x[11, 2, 29, 0] = float("nan")
+            x[18, 39, 14, 14] = float("nan")
+        xd = x.cuda()
+        d = _desc(n, c, h, w)
+        bh, bw = d.block_h, d.block_w
+        n_tiles = n * (-(-h // bh)) * (-(-w // bw))
+        ref = _regular(xd, d, n_tiles)
+        got = _static(xd, d, n_tiles)
+        torch.cuda.synchronize()
+        _same(ref, got)
+        assert _lib.load().sf_prescan2d_static_ws_status(torch.cuda.current_stream().cuda_stream) == 0
+    oag, otc, oids = oracle.prescan2d(x.numpy(), 0, h, w, 3, 1, 1, bh, bw, 16, 1e-6)
+    ag, tc, ids, cnt = (t.cpu().numpy() for t in got)
+    np.testing.assert_array_equal(ag, oag)
+    np.testing.assert_array_equal(tc, otc)
+    np.testing.assert_array_equal(ids[: cnt[0]], oids)
 
 
 def test_static_workspace_rejects_oversize_request():
