@@ -1,0 +1,548 @@
+// 3x3 / stride 1 / pad 1 convolution of spike inputs on the tcgen05 tensor
+// cores (implicit GEMM, integer MMA).
+//
+// Reference semantics: Kernels/conv2d.py:563-886 computes y = conv2d(x, w) +
+// bias over the active (tile, channel-group) blocks, routing dense groups
+// through tensor-core dots (:607-638); Ops/sparse_conv2d.py:819-834
+// (F.conv2d) is the exact result it approximates.
+//
+// Exactness. Spikes are 0 or 1, so x is exact as a signed 8-bit integer. The
+// weights of output channel co are written in 23-bit fixed point relative to
+// s = max |w[co]|: q = rint(w / s * 2^22), split into three signed 8-bit
+// digits q = d0 * 2^16 + d1 * 2^8 + d2 (balanced digits, |d0| <= 64). Each
+// digit plane is a block of output columns of the same GEMM (N = 3 * 64), so
+// one kind::i8 MMA accumulates all three planes as exact int32 sums, and the
+// epilogue forms y = s*2^-6 * D0 + s*2^-14 * D1 + s*2^-22 * D2 + bias in
+// fp32. The weight error is at most 0.75 * s * 2^-22 per weight: fp32-level
+// precision at 1.5x the MMA cost of one bf16 plane. A unit whose input holds
+// any value other than 0 or 1 is recomputed in the epilogue with fp32 FMAs
+// from x and the fp32 / bf16 weights, and its MMA result is discarded.
+//
+// Geometry. The N images are stacked vertically into one zero-padded plane
+// of pitch Wp = W + 2: padded row R holds image (R-1) / (H+1), row
+// (R-1) % (H+1), where row H of each image (the separator) and row 0 are
+// zero, as are padded columns 0 and W + 1. Output position o = Ro * Wp + c
+// (c < W, Ro % (H+1) < H) reads input position o + kh * Wp + kw for tap
+// (kh, kw), so every tap is the A matrix shifted by kh * Wp + kw rows. A is
+// kept K-major without swizzle: for each 16-channel slice, one contiguous run
+// of 16-byte rows (one per input position), and a shift is a change of the
+// descriptor's start address. Tiles are 128 consecutive output positions; a
+// unit is U consecutive tiles of one 64-channel output block.
+//
+// Per CTA (persistent, one per SM, a contiguous range of units):
+//   warps 0-15  convert: read x (NCHW, lane = input position: coalesced rows
+//               of 32 values per channel), write the int8 A rows of a unit
+//               into one of two A buffers, flag non-binary units;
+//   warps 16-23 epilogue: per tile, tcgen05.ld the three planes (lane =
+//               position), combine, add bias, store y (lane = position: rows
+//               of NCHW written as 128-byte runs);
+//   warp 24     allocates TMEM (two accumulators of 3 * 64 columns), copies
+//               the weight digits of the current output block into shared
+//               memory, and issues 9 taps x C/32 MMAs per tile.
+// Every mbarrier wait gives up after one second (error word set, CTA
+// drains); TMEM is freed before the CTA exits. No TMA multicast.
+#include <algorithm>
+#include <cstring>
+#include "conv_kernel.cuh"
+#include "tc_common.cuh"
+#include "conv3x3_tc.cuh"
+
+namespace sf {
+namespace c3tc {
+namespace {
+
+using conv::mbar_arrive;
+
+constexpr int kConvWarps = 16;
+constexpr int kEpiWarps = 8;
+constexpr int kMmaWarp = kConvWarps + kEpiWarps;
+constexpr int kThreads = (kMmaWarp + 1) * 32;
+constexpr int kM = 128;
+constexpr int kTags = 4;
+
+struct Params {
+  const void* x;
+  const unsigned char* bimg;  // [ncob][9][kcores][N3][16] int8 digits
+  const float* scales;        // [3][ncob * CB]
+  const float* bias;
+  const void* wg;             // gather-packed weights (fallback path)
+  int cpl;
+  void* y;
+  uint32_t* err;
+  int N, C, H, W, Co, Wp, Hs;
+  int kcores, CB, N3, ncob;
+  long long ntiles, upcob, nunits, units_per_cta;
+  int U;
+  uint32_t rows_a, a_plane, a_bytes, b_bytes, a_off, bar_off, tmem_cols;
+};
+
+struct Bars {
+  uint64_t a_full[2], a_empty[2], d_full[2], d_empty[2], b_full, b_free;
+  uint32_t tmem_base;
+  uint32_t tag[kTags];  // = u + 1 when unit u holds a value other than 0 / 1
+};
+
+template <typename XT>
+__device__ __forceinline__ uint32_t raw_bits(XT v) {
+  if constexpr (sizeof(XT) == 4)
+    return __float_as_uint(v);
+  else
+    return (uint32_t)(*reinterpret_cast<const unsigned short*>(&v));
+}
+template <typename XT>
+__device__ __forceinline__ constexpr uint32_t one_bits() {
+  if constexpr (std::is_same<XT, float>::value) return 0x3f800000u;
+  if constexpr (std::is_same<XT, __half>::value) return 0x3c00u;
+  return 0x3f80u;
+}
+
+template <typename WT>
+__device__ __forceinline__ float gather_w(const Params& p, int co, int ci, int tap) {
+  const int blk = co / (32 * p.cpl), rem = co - blk * 32 * p.cpl;
+  const int j = rem >> 5, l = rem & 31;
+  const WT* w = static_cast<const WT*>(p.wg) + ((((size_t)blk * p.C + ci) * 9 + tap) * 32 + l) * p.cpl + j;
+  return DT<WT>::to_f(*w);
+}
+
+template <typename XT, typename WT>
+__global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  unsigned char* bsm = smem;
+  unsigned char* abuf = smem + p.a_off;
+  Bars* bars = reinterpret_cast<Bars*>(smem + p.bar_off);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const long long u0 = (long long)blockIdx.x * p.units_per_cta;
+  const long long u1 = min(p.nunits, u0 + p.units_per_cta);
+  const int nu = (int)max(0ll, u1 - u0);
+  const XT* __restrict__ x = static_cast<const XT*>(p.x);
+  const size_t HW = (size_t)p.H * p.W;
+
+  if (tid == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars->a_full[i], kConvWarps);
+      mbar_init(&bars->a_empty[i], 1);
+      mbar_init(&bars->d_full[i], 1);
+      mbar_init(&bars->d_empty[i], kEpiWarps);
+    }
+    mbar_init(&bars->b_full, 1);
+    mbar_init(&bars->b_free, 1);
+    for (int i = 0; i < kTags; ++i) bars->tag[i] = 0u;
+    fence_mbar_init();
+  }
+  if (warp == kMmaWarp) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&bars->tmem_base)),
+                 "r"(p.tmem_cols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  const uint32_t tmem = bars->tmem_base;
+  bool failed = false;
+
+  if (warp == kMmaWarp) {
+    if (lane == 0) {
+      const uint32_t idesc = tc::idesc_s8(kM, p.N3);
+      const uint32_t bsa = smem_u32(bsm);
+      const uint32_t lbo_b = (uint32_t)p.N3 * 16u;
+      int cur_cob = -1, bloads = 0;
+      long long g = 0;  // tiles issued by this CTA
+      for (int i = 0; i < nu && !failed; ++i) {
+        const long long u = u0 + i;
+        const int cob = (int)(u / p.upcob);
+        const long long t0 = (u - (long long)cob * p.upcob) * p.U;
+        const int nt = (int)min((long long)p.U, p.ntiles - t0);
+        if (cob != cur_cob) {
+          if (cur_cob >= 0) {
+            // Every MMA reading the old weights must finish before they are replaced.
+            tc::mma_commit(&bars->b_free);
+            if (!mbar_wait_ns(&bars->b_free, (uint32_t)((bloads - 1) & 1))) {
+              failed = true;
+              break;
+            }
+          }
+          mbar_arrive_expect_tx(&bars->b_full, p.b_bytes);
+          const unsigned char* src = p.bimg + (size_t)cob * p.b_bytes;
+          for (uint32_t off = 0; off < p.b_bytes; off += 32768u)
+            bulk_g2s(bsm + off, src + off, min(32768u, p.b_bytes - off), &bars->b_full);
+          if (!mbar_wait_ns(&bars->b_full, (uint32_t)(bloads & 1))) {
+            failed = true;
+            break;
+          }
+          ++bloads;
+          cur_cob = cob;
+        }
+        const int a = i & 1;
+        if (!mbar_wait_ns(&bars->a_full[a], (uint32_t)((i >> 1) & 1))) {
+          failed = true;
+          break;
+        }
+        tc::fence_after();
+        const uint32_t asa = smem_u32(abuf + (size_t)a * p.a_bytes);
+        for (int j = 0; j < nt; ++j, ++g) {
+          const int d = (int)(g & 1);
+          if (g >= 2 && !mbar_wait_ns(&bars->d_empty[d], (uint32_t)(((g >> 1) - 1) & 1))) {
+            failed = true;
+            break;
+          }
+          tc::fence_after();
+          const uint32_t dt = tmem + (uint32_t)(d * p.N3);
+          uint32_t acc = 0u;
+          for (int tap = 0; tap < 9; ++tap) {
+            const int kh = tap / 3, kw = tap - kh * 3;
+            const uint32_t shift = (uint32_t)(j * kM + kh * p.Wp + kw) * 16u;
+            for (int ks = 0; ks < p.kcores; ks += 2) {
+              const uint64_t ad = tc::desc_interleave(asa + (uint32_t)ks * p.a_plane + shift, p.a_plane, 128u);
+              const uint64_t bd =
+                  tc::desc_interleave(bsa + (uint32_t)(tap * p.kcores + ks) * lbo_b, lbo_b, 128u);
+              tc::mma_s8(dt, ad, bd, idesc, acc);
+              acc = 1u;
+            }
+          }
+          tc::mma_commit(&bars->d_full[d]);
+        }
+        if (failed) break;
+        tc::mma_commit(&bars->a_empty[a]);
+      }
+      if (failed) atomicExch(p.err, 1u);
+    }
+    __syncwarp();
+  } else if (warp >= kConvWarps) {
+    // Epilogue: warp w reads TMEM lane quarter w % 4 (32 positions of the
+    // tile) and half of the block's output channels.
+    const int ew = warp - kConvWarps;
+    const int qd = warp & 3;
+    const int half = ew >> 2;
+    const int cw = p.CB / 2;
+    long long g = 0;
+    for (int i = 0; i < nu && !failed; ++i) {
+      const long long u = u0 + i;
+      const int cob = (int)(u / p.upcob);
+      const long long t0 = (u - (long long)cob * p.upcob) * p.U;
+      const int nt = (int)min((long long)p.U, p.ntiles - t0);
+      for (int j = 0; j < nt; ++j, ++g) {
+        const int d = (int)(g & 1);
+        if (!mbar_wait_ns(&bars->d_full[d], (uint32_t)((g >> 1) & 1))) {
+          failed = true;
+          break;
+        }
+        tc::fence_after();
+        const bool odd = *reinterpret_cast<volatile uint32_t*>(&bars->tag[u % kTags]) == (uint32_t)(u + 1);
+        // This lane's output position.
+        const long long o = (t0 + j) * kM + qd * 32 + lane;
+        const long long Ro = o / p.Wp;
+        const int c = (int)(o - Ro * p.Wp);
+        const long long img = Ro / p.Hs;
+        const int h = (int)(Ro - img * p.Hs);
+        const bool valid = c < p.W && h < p.H && img < p.N;
+        const size_t pix = (size_t)h * p.W + c;
+        XT* ybase = static_cast<XT*>(p.y) + (size_t)img * p.Co * HW + pix;
+        const int cbeg = half * cw;
+        if (!odd) {
+          for (int cc = cbeg; cc < cbeg + cw; cc += 16) {
+            uint32_t r0[16], r1[16], r2[16];
+            const uint32_t ta = tmem + ((uint32_t)(qd * 32) << 16) + (uint32_t)(d * p.N3 + cc);
+            tc::tmem_ld16(ta, r0);
+            tc::tmem_ld16(ta + (uint32_t)p.CB, r1);
+            tc::tmem_ld16(ta + (uint32_t)(2 * p.CB), r2);
+            tc::tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const int co = cob * p.CB + cc + e;
+              if (valid && co < p.Co) {
+                const int sidx = cob * p.CB + cc + e;
+                const float b = p.bias ? __ldg(p.bias + co) : 0.f;
+                const float s0 = __ldg(p.scales + sidx);
+                const float s1 = __ldg(p.scales + p.ncob * p.CB + sidx);
+                const float s2 = __ldg(p.scales + 2 * p.ncob * p.CB + sidx);
+                float v = fmaf(s2, (float)(int)r2[e], b);
+                v = fmaf(s1, (float)(int)r1[e], v);
+                v = fmaf(s0, (float)(int)r0[e], v);
+                ybase[(size_t)co * HW] = DT<XT>::from_f(v);
+              }
+            }
+          }
+        } else if (valid) {
+          // Values other than 0 / 1: fp32 FMAs from x and the weights.
+          const XT* ximg = x + (size_t)img * p.C * HW;
+          for (int cc = cbeg; cc < cbeg + cw; ++cc) {
+            const int co = cob * p.CB + cc;
+            if (co >= p.Co) break;
+            float acc = 0.f;
+            for (int ci = 0; ci < p.C; ++ci) {
+              for (int tap = 0; tap < 9; ++tap) {
+                const int ih = h + tap / 3 - 1, iw = c + tap % 3 - 1;
+                if (ih < 0 || ih >= p.H || iw < 0 || iw >= p.W) continue;
+                const float xv = DT<XT>::to_f(ximg[(size_t)ci * HW + (size_t)ih * p.W + iw]);
+                if (xv != 0.f) acc = fmaf(xv, gather_w<WT>(p, co, ci, tap), acc);
+              }
+            }
+            ybase[(size_t)co * HW] = DT<XT>::from_f(acc + (p.bias ? __ldg(p.bias + co) : 0.f));
+          }
+        }
+        tc::fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->d_empty[d]);
+      }
+    }
+    if (failed && lane == 0) atomicExch(p.err, 1u);
+  } else {
+    // Converters: work item = (group of 32 A rows, pair of 16-channel slices).
+    const int npairs = p.kcores / 2;
+    const int items = (int)(p.rows_a / 32) * npairs;
+    for (int i = 0; i < nu && !failed; ++i) {
+      const long long u = u0 + i;
+      const int cob = (int)(u / p.upcob);
+      const long long t0 = (u - (long long)cob * p.upcob) * p.U;
+      const int a = i & 1;
+      if (i >= 2 && !mbar_wait_ns(&bars->a_empty[a], (uint32_t)(((i >> 1) - 1) & 1))) {
+        failed = true;
+        break;
+      }
+      unsigned char* ab = abuf + (size_t)a * p.a_bytes;
+      const long long q0 = t0 * kM;
+      uint32_t nb = 0u;
+      for (int it = warp; it < items; it += kConvWarps) {
+        const int grp = it / npairs, kp = it - grp * npairs;
+        const int r = grp * 32 + lane;
+        const long long q = q0 + r;
+        const long long R = q / p.Wp;
+        const int iw = (int)(q - R * p.Wp) - 1;
+        const long long R1 = R - 1;
+        const long long img = R1 >= 0 ? R1 / p.Hs : 0;
+        const int h = (int)(R1 - img * p.Hs);
+        const bool valid = R1 >= 0 && iw >= 0 && iw < p.W && h < p.H && img < p.N;
+        const int c0 = kp * 32;
+        const XT* src = x + ((size_t)img * p.C + c0) * HW + (size_t)h * p.W + iw;
+        uint32_t ub[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) ub[e] = (valid && c0 + e < p.C) ? raw_bits<XT>(src[(size_t)e * HW]) : 0u;
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t wv[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            uint32_t w = 0u;
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+              const uint32_t uu = ub[hh * 16 + k * 4 + b];
+              nb |= (uu != 0u) & (uu != one_bits<XT>());
+              w |= (uint32_t)(uu != 0u) << (8 * b);
+            }
+            wv[k] = w;
+          }
+          *reinterpret_cast<uint4*>(ab + (size_t)(2 * kp + hh) * p.a_plane + (size_t)r * 16) =
+              make_uint4(wv[0], wv[1], wv[2], wv[3]);
+        }
+      }
+      if (__any_sync(0xffffffffu, nb != 0u) && lane == 0)
+        *reinterpret_cast<volatile uint32_t*>(&bars->tag[u % kTags]) = (uint32_t)(u + 1);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->a_full[a]);
+    }
+    if (failed && lane == 0) atomicExch(p.err, 1u);
+  }
+  tc::fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc::fence_after();
+    __syncwarp();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(p.tmem_cols) : "memory");
+  }
+}
+
+// Per output channel: s = max |w[co]|, stored as the three digit scales.
+__global__ void tc_scales_kernel(const void* w, int src_dtype, int Co, int C, int ncob, int CB, float* scales) {
+  const int co = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (co >= ncob * CB) return;
+  float m = 0.f;
+  if (co < Co) {
+    for (int i = lane; i < C * 9; i += 32) {
+      const size_t idx = (size_t)co * C * 9 + i;
+      float v;
+      if (src_dtype == SF_DTYPE_F32)
+        v = static_cast<const float*>(w)[idx];
+      else if (src_dtype == SF_DTYPE_F16)
+        v = __half2float(static_cast<const __half*>(w)[idx]);
+      else
+        v = __bfloat162float(static_cast<const __nv_bfloat16*>(w)[idx]);
+      m = fmaxf(m, fabsf(v));
+    }
+  }
+  for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane == 0) {
+    const int tot = ncob * CB;
+    scales[co] = m * 0x1p-6f;
+    scales[tot + co] = m * 0x1p-14f;
+    scales[2 * tot + co] = m * 0x1p-22f;
+  }
+}
+
+// Digit bytes of the B image [cob][tap][kcore][N3][16].
+__global__ void tc_digits_kernel(const void* w, int src_dtype, int Co, int C, int ncob, int CB, int kcores,
+                                 const float* scales, signed char* bimg) {
+  const int N3 = 3 * CB;
+  const size_t total = (size_t)ncob * 9 * kcores * N3 * 16;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int b = (int)(i & 15);
+    size_t r = i >> 4;
+    const int n = (int)(r % N3);
+    r /= N3;
+    const int kc = (int)(r % kcores);
+    r /= kcores;
+    const int tap = (int)(r % 9);
+    const int cob = (int)(r / 9);
+    const int plane = n / CB;
+    const int co = cob * CB + (n - plane * CB);
+    const int ci = kc * 16 + b;
+    int digit = 0;
+    if (co < Co && ci < C) {
+      const size_t idx = ((size_t)co * C + ci) * 9 + tap;
+      float v;
+      if (src_dtype == SF_DTYPE_F32)
+        v = static_cast<const float*>(w)[idx];
+      else if (src_dtype == SF_DTYPE_F16)
+        v = __half2float(static_cast<const __half*>(w)[idx]);
+      else
+        v = __bfloat162float(static_cast<const __nv_bfloat16*>(w)[idx]);
+      const float s = scales[co] * 64.f;  // max |w[co]|, exactly
+      if (s > 0.f) {
+        const int q = __float2int_rn(__fdiv_rn(v, s) * 4194304.f);  // |q| <= 2^22
+        const int d2 = ((q + 128) & 255) - 128;
+        const int q1 = (q - d2) >> 8;
+        const int d1 = ((q1 + 128) & 255) - 128;
+        const int d0 = (q1 - d1) >> 8;
+        digit = plane == 0 ? d0 : (plane == 1 ? d1 : d2);
+      }
+    }
+    bimg[i] = (signed char)digit;
+  }
+}
+
+inline size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
+
+struct Geo {
+  int CB, ncob, N3, kcores;
+  size_t scale_bytes, b_bytes;
+};
+Geo geometry(int Co, int C) {
+  Geo g;
+  g.CB = Co <= 32 ? 32 : 64;
+  g.ncob = (Co + g.CB - 1) / g.CB;
+  g.N3 = 3 * g.CB;
+  g.kcores = (C + 31) / 32 * 2;
+  g.scale_bytes = align256((size_t)3 * g.ncob * g.CB * 4);
+  g.b_bytes = (size_t)9 * g.kcores * g.N3 * 16;
+  return g;
+}
+
+template <typename XT, typename WT>
+sf_status launch(Params p, size_t smem, cudaStream_t st) {
+  auto kern = conv3x3_tc_kernel<XT, WT>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return SF_ERR_CUDA;
+  const long long grid = (p.nunits + p.units_per_cta - 1) / p.units_per_cta;
+  kern<<<(unsigned)grid, kThreads, smem, st>>>(p);
+  return cudaGetLastError() == cudaSuccess ? SF_OK : SF_ERR_CUDA;
+}
+
+template <typename XT>
+sf_status dispatch_w(int wdt, const Params& p, size_t smem, cudaStream_t st) {
+  if (wdt == SF_DTYPE_F32) return launch<XT, float>(p, smem, st);
+  if (wdt == SF_DTYPE_BF16) return launch<XT, __nv_bfloat16>(p, smem, st);
+  return SF_ERR_UNSUPPORTED;
+}
+
+}  // namespace
+
+bool tc3_packs(int Co, int C, int K) { return K == 3 && C >= 1 && C <= kTcMaxC && Co >= 1; }
+
+size_t tc3_section_bytes(int Co, int C) {
+  const Geo g = geometry(Co, C);
+  return g.scale_bytes + (size_t)g.ncob * g.b_bytes;
+}
+
+sf_status tc3_pack(const void* w, int src_dtype, int Co, int C, void* section, cudaStream_t st) {
+  const Geo g = geometry(Co, C);
+  float* scales = static_cast<float*>(section);
+  signed char* bimg = static_cast<signed char*>(section) + g.scale_bytes;
+  const int warps = g.ncob * g.CB;
+  tc_scales_kernel<<<(warps + 7) / 8, 256, 0, st>>>(w, src_dtype, Co, C, g.ncob, g.CB, scales);
+  if (cudaGetLastError() != cudaSuccess) return SF_ERR_CUDA;
+  const size_t total = (size_t)g.ncob * g.b_bytes;
+  const int blocks = (int)std::min<size_t>((total + 255) / 256, 4096);
+  tc_digits_kernel<<<blocks, 256, 0, st>>>(w, src_dtype, Co, C, g.ncob, g.CB, g.kcores, scales, bimg);
+  return cudaGetLastError() == cudaSuccess ? SF_OK : SF_ERR_CUDA;
+}
+
+sf_status run_conv3x3_tc(const void* x, const void* w_gather, int cpl, const void* section, const float* bias,
+                         void* y, uint32_t* err, int N, int C, int H, int W, int Co, int xdt, int wdt,
+                         cudaStream_t st) {
+  if (!tc3_packs(Co, C, 3)) return SF_ERR_UNSUPPORTED;
+  if (wdt != SF_DTYPE_F32 && wdt != SF_DTYPE_BF16) return SF_ERR_UNSUPPORTED;
+  const Geo g = geometry(Co, C);
+  Params p;
+  memset(&p, 0, sizeof(p));
+  p.x = x;
+  p.scales = static_cast<const float*>(section);
+  p.bimg = static_cast<const unsigned char*>(section) + g.scale_bytes;
+  p.bias = bias;
+  p.wg = w_gather;
+  p.cpl = cpl;
+  p.y = y;
+  p.err = err;
+  p.N = N; p.C = C; p.H = H; p.W = W; p.Co = Co;
+  p.Wp = W + 2;
+  p.Hs = H + 1;
+  p.kcores = g.kcores;
+  p.CB = g.CB;
+  p.N3 = g.N3;
+  p.ncob = g.ncob;
+  const long long positions = (long long)N * p.Hs * p.Wp;
+  p.ntiles = (positions + kM - 1) / kM;
+  if (p.ntiles >= (1ll << 30)) return SF_ERR_UNSUPPORTED;
+  p.b_bytes = (uint32_t)g.b_bytes;
+  const size_t limit = 227 * 1024;
+  size_t smem = 0;
+  int U = 0;
+  for (int u = 4; u >= 1; --u) {
+    const uint32_t rows = (uint32_t)((u * kM + 2 * p.Wp + 2 + 31) / 32 * 32);
+    const size_t a_bytes = (size_t)rows * 16 * g.kcores;
+    const size_t a_off = (g.b_bytes + 127) / 128 * 128;
+    const size_t bar_off = a_off + 2 * a_bytes;
+    const size_t total = bar_off + sizeof(Bars);
+    if (total <= limit) {
+      U = u;
+      p.rows_a = rows;
+      p.a_plane = rows * 16;
+      p.a_bytes = (uint32_t)a_bytes;
+      p.a_off = (uint32_t)a_off;
+      p.bar_off = (uint32_t)bar_off;
+      smem = total;
+      break;
+    }
+  }
+  if (U == 0) return SF_ERR_UNSUPPORTED;
+  smem = std::max<size_t>(smem, 120 * 1024);  // one CTA (and one TMEM allocation) per SM
+  p.U = U;
+  p.upcob = (p.ntiles + U - 1) / U;
+  p.nunits = p.upcob * p.ncob;
+  uint32_t cols = 32;
+  while (cols < (uint32_t)(2 * p.N3)) cols <<= 1;
+  p.tmem_cols = cols;
+  const long long ctas = std::min<long long>(p.nunits, (long long)num_sms_current_device());
+  p.units_per_cta = (p.nunits + ctas - 1) / ctas;
+  switch (xdt) {
+    case SF_DTYPE_F32: return dispatch_w<float>(wdt, p, smem, st);
+    case SF_DTYPE_F16: return dispatch_w<__half>(wdt, p, smem, st);
+    case SF_DTYPE_BF16: return dispatch_w<__nv_bfloat16>(wdt, p, smem, st);
+  }
+  return SF_ERR_INVALID_ARG;
+}
+
+}  // namespace c3tc
+}  // namespace sf

@@ -1,0 +1,25 @@
+// Host interface of the tcgen05 3x3 convolution (conv3x3_tc.cu) and of the
+// weight section it reads, appended to the gather-packed weights.
+#pragma once
+#include "common.cuh"
+
+namespace sf {
+namespace c3tc {
+
+// Input channels the kernel takes (its weight digits stay in shared memory).
+constexpr int kTcMaxC = 64;
+
+// Whether sf_pack_weights appends the tensor-core section for this layer.
+bool tc3_packs(int Co, int C, int K);
+// Bytes of that section: per-channel digit scales [3][ncob * CB] (fp32) and
+// the int8 digit image [ncob][9][kcores][3 * CB][16].
+size_t tc3_section_bytes(int Co, int C);
+// Writes the section from OIHW weights of any supported dtype.
+sf_status tc3_pack(const void* w_oihw, int src_dtype, int Co, int C, void* section, cudaStream_t st);
+// Runs the convolution; SF_ERR_UNSUPPORTED for shapes it does not take.
+sf_status run_conv3x3_tc(const void* x, const void* w_gather, int cpl, const void* section, const float* bias,
+                         void* y, uint32_t* err, int N, int C, int H, int W, int Co, int xdt, int wdt,
+                         cudaStream_t st);
+
+}  // namespace c3tc
+}  // namespace sf

@@ -8,6 +8,7 @@
 #include "conv_kernel.cuh"
 #include "policy.cuh"
 #include "events.cuh"
+#include "conv3x3_tc.cuh"
 
 namespace sf {
 namespace pwtc {
@@ -199,6 +200,16 @@ sf_status check_geometry(int T, int N, int C, int H, int W, int Co, int Ho, int 
   return SF_OK;
 }
 
+// Bytes of the gather layout alone; the tensor-core section (3x3 layers the
+// tcgen05 kernel takes) follows it at the next 256-byte boundary.
+size_t gather_bytes(int c_out, int c_in, int kernel, int wsz) {
+  const int cpl = weight_block_cpl(c_in, kernel, c_out, wsz);
+  return (size_t)weight_blocks(c_out, cpl) * cpl * 32 * c_in * kernel * kernel * wsz;
+}
+size_t tc_section_offset(int c_out, int c_in, int kernel, int wsz) {
+  return (gather_bytes(c_out, c_in, kernel, wsz) + 255) & ~(size_t)255;
+}
+
 // Stage 1 + stage 2 for T*N images; the LIF variant when lif is set.
 // masks_in: events of x precomputed by a fused conv + LIF (binary spikes;
 // x itself is then not read). mask_out: LIF only, the output spikes' events.
@@ -216,6 +227,18 @@ sf_status run_conv(const void* x, const void* w_packed, const float* bias, void*
     uint32_t* err = nullptr;
     if (cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_conv_error) != cudaSuccess) return SF_ERR_CUDA;
     s = pwtc::run_pointwise_tc(x, w_packed, bias, y, err, T * N, C, H, W, Co, xdt, wdt, st);
+    if (s != SF_ERR_UNSUPPORTED) return s;
+  }
+  // 3x3 stride 1: integer tcgen05 implicit GEMM over x streamed once
+  // (conv3x3_tc.cu), unless the policy asks for the gather kernel.
+  if (!lif && !masks_in && K == 3 && S == 1 && P == 1 && policy(SF_POLICY_CONV3X3_PATH) != 1 &&
+      c3tc::tc3_packs(Co, C, K)) {
+    uint32_t* err = nullptr;
+    if (cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_conv_error) != cudaSuccess) return SF_ERR_CUDA;
+    const int wsz = (int)dtype_size(wdt);
+    const void* section = static_cast<const char*>(w_packed) + tc_section_offset(Co, C, K, wsz);
+    s = c3tc::run_conv3x3_tc(x, w_packed, weight_block_cpl(C, K, Co, wsz), section, bias, y, err, T * N, C, H, W,
+                             Co, xdt, wdt, st);
     if (s != SF_ERR_UNSUPPORTED) return s;
   }
   // 1x1 stride 2: one pass over x with masks built in shared memory
@@ -322,8 +345,10 @@ using namespace sf::conv;
 extern "C" size_t sf_packed_weight_bytes(int32_t c_out, int32_t c_in, int32_t kernel, int32_t w_dst_dtype) {
   if (c_out <= 0 || c_in <= 0 || kernel <= 0) return 0;
   const int wsz = (int)dtype_size(w_dst_dtype);
-  const int cpl = weight_block_cpl(c_in, kernel, c_out, wsz);
-  return (size_t)weight_blocks(c_out, cpl) * cpl * 32 * c_in * kernel * kernel * wsz;
+  if (wsz == 0) return 0;
+  if (c3tc::tc3_packs(c_out, c_in, kernel))
+    return tc_section_offset(c_out, c_in, kernel, wsz) + c3tc::tc3_section_bytes(c_out, c_in);
+  return gather_bytes(c_out, c_in, kernel, wsz);
 }
 
 extern "C" sf_status sf_pack_weights(const void* w_oihw, int32_t w_src_dtype, int32_t c_out, int32_t c_in,
@@ -343,7 +368,12 @@ extern "C" sf_status sf_pack_weights(const void* w_oihw, int32_t w_src_dtype, in
   else
     pack_weights_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(
         w_oihw, w_src_dtype, static_cast<__nv_bfloat16*>(w_packed), c_out, c_in, KK, blocks_w, cpl);
-  return cudaGetLastError() == cudaSuccess ? SF_OK : SF_ERR_CUDA;
+  if (cudaGetLastError() != cudaSuccess) return SF_ERR_CUDA;
+  if (c3tc::tc3_packs(c_out, c_in, kernel)) {
+    const size_t off = tc_section_offset(c_out, c_in, kernel, (int)dtype_size(w_dst_dtype));
+    return c3tc::tc3_pack(w_oihw, w_src_dtype, c_out, c_in, static_cast<char*>(w_packed) + off, st);
+  }
+  return SF_OK;
 }
 
 extern "C" size_t sf_sparse_conv2d_workspace_size(const sf_conv_desc* d) {

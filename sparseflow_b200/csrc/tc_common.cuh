@@ -1,0 +1,59 @@
+// tcgen05 helpers for the tensor-core kernels: MMA commit, thread-sync
+// fences around tcgen05 operations, TMEM -> register loads, shared-memory
+// matrix descriptors and the kind::i8 MMA.
+#pragma once
+#include "common.cuh"
+
+namespace sf {
+namespace tc {
+
+// Arrives on `bar` once every tcgen05 operation issued so far by this thread
+// has completed.
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+// 16 consecutive 32-bit TMEM columns of this warp's lane quarter (lane = row).
+// Completes only after tmem_wait_ld().
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor, K-major, no swizzle ("interleaved"):
+// core matrices of 8 rows x 16 bytes; rows of one core matrix 16 B apart,
+// 8-row groups `sbo` bytes apart, the two 16-byte K halves of one kind::i8
+// MMA `lbo` bytes apart. With sbo = 128 the rows of a K half form one
+// contiguous run of 16-byte rows, so moving the start address by r * 16
+// bytes gives the same matrix shifted by r rows.
+__device__ __forceinline__ uint64_t desc_interleave(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3fffu);
+  d |= (uint64_t)((lbo >> 4) & 0x3fffu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3fffu) << 32;
+  d |= (uint64_t)1u << 46;  // descriptor version (sm_100)
+  return d;                 // layout type 0: no swizzle
+}
+
+// Instruction descriptor, kind::i8: D s32, A and B signed 8-bit, both K-major.
+__host__ __device__ constexpr uint32_t idesc_s8(int m, int n) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_s8(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+}  // namespace tc
+}  // namespace sf

@@ -1,0 +1,117 @@
+"""The tcgen05 3x3 convolution (integer MMA over 0/1 spikes, 3-digit weights) vs the oracle,
+against the gather kernel, and on the fallback for inputs that are not 0/1."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+RTOL = 1e-5
+
+
+def _close(y, ref, rtol=RTOL):
+    y = np.asarray(y, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    scale = max(np.abs(ref).max(), 1e-6)
+    err = np.abs(y - ref).max()
+    assert err <= rtol * scale, f"max abs err {err} > {rtol} * {scale}"
+
+
+def _run(x, w, b, path):
+    from sparseflow_b200 import _lib
+    from sparseflow_b200.Kernels.conv2d import sparse_conv2d_forward
+    with _lib.path_policy(_lib.SF_POLICY_CONV3X3_PATH, path):
+        y, _ = sparse_conv2d_forward(x, w, b, kernel_size=3, stride=1, padding=1)
+    return y
+
+
+GEOM = [
+    # n, c, h, w, co, density
+    (2, 64, 56, 56, 64, 0.01),
+    (3, 64, 32, 32, 64, 0.2),
+    (4, 16, 8, 8, 32, 0.1),
+    (2, 3, 17, 9, 8, 0.5),
+    (2, 40, 13, 30, 24, 0.1),
+    (1, 64, 20, 250, 64, 0.05),
+    (5, 32, 7, 7, 100, 0.3),
+    (2, 64, 28, 28, 128, 0.05),
+    (3, 48, 1, 1, 16, 0.5),
+    (2, 64, 15, 3, 64, 0.0),
+    (64, 64, 8, 8, 64, 0.02),
+    (1, 33, 57, 57, 65, 0.03),
+]
+
+
+@pytest.mark.parametrize("n,c,h,w,co,density", GEOM)
+def test_tc3x3_vs_oracle_and_gather(n, c, h, w, co, density):
+    g = torch.Generator().manual_seed(n * 1000 + c * 7 + co + h)
+    x = (torch.rand(n, c, h, w, generator=g) < density).float()
+    wt = torch.randn(co, c, 3, 3, generator=g) * (2.0 / (c * 9)) ** 0.5
+    b = torch.randn(co, generator=g) * 0.1
+    ref = oracle.conv2d(x.numpy(), wt.numpy(), b.numpy(), 1, 1)
+    y_tc = _run(x.cuda(), wt.cuda(), b.cuda(), 2)
+    y_g = _run(x.cuda(), wt.cuda(), b.cuda(), 1)
+    _close(y_tc.cpu().numpy(), ref)
+    _close(y_g.cpu().numpy(), ref)
+    # deterministic: integer sums, fixed combine order
+    assert torch.equal(y_tc, _run(x.cuda(), wt.cuda(), b.cuda(), 2))
+
+
+@pytest.mark.parametrize("xdt", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("wdt", [torch.float32, torch.bfloat16])
+def test_tc3x3_dtypes(xdt, wdt):
+    g = torch.Generator().manual_seed(17)
+    x = (torch.rand(4, 64, 28, 28, generator=g) < 0.05).float().to(xdt)
+    wt = (torch.randn(64, 64, 3, 3, generator=g) * 0.06).to(wdt)
+    y = _run(x.cuda(), wt.cuda(), None, 2)
+    assert y.dtype == xdt
+    ref = oracle.conv2d(x.float().numpy(), wt.float().numpy(), None, 1, 1)
+    _close(y.float().cpu().numpy(), ref, rtol=RTOL if xdt == torch.float32 else 1e-2)
+
+
+def test_tc3x3_non_binary_units_take_the_fp32_path():
+    """Real values in some images: their units are recomputed with fp32 FMAs, the rest stay on the MMA."""
+    g = torch.Generator().manual_seed(5)
+    x = (torch.rand(6, 32, 20, 20, generator=g) < 0.1).float()
+    x[2] *= torch.randn(32, 20, 20, generator=g)
+    x[5, 3, 7, 7] = 0.5
+    x[0, 0, 0, 0] = 2.0  # an integer that is not 0/1
+    wt = torch.randn(48, 32, 3, 3, generator=g) * 0.1
+    b = torch.randn(48, generator=g)
+    ref = oracle.conv2d(x.numpy(), wt.numpy(), b.numpy(), 1, 1)
+    _close(_run(x.cuda(), wt.cuda(), b.cuda(), 2).cpu().numpy(), ref)
+
+
+def test_tc3x3_extreme_weight_ranges():
+    """Per-channel fixed point: channels of very different scale, an all-zero channel, tiny weights."""
+    g = torch.Generator().manual_seed(8)
+    x = (torch.rand(2, 64, 16, 16, generator=g) < 0.2).float()
+    wt = torch.randn(64, 64, 3, 3, generator=g)
+    wt[0] *= 1e-30
+    wt[1] = 0
+    wt[2] *= 1e6
+    wt[3, :, 1, 1] = 1e-3  # one large weight per input channel dominates the scale
+    wt[3, 0, 0, 0] = 5.0
+    ref = oracle.conv2d(x.numpy(), wt.numpy(), None, 1, 1)
+    y = _run(x.cuda(), wt.cuda(), None, 2).cpu().numpy()
+    for co in range(64):
+        _close(y[:, co], ref[:, co])
+
+
+def test_tc3x3_full_size_c5_cell_vs_cudnn_fp32():
+    """Headline workload (1024 images, C64 56x56, p=0.01) on the tensor-core path vs cuDNN fp32."""
+    g = torch.Generator(device="cuda").manual_seed(2)
+    x = (torch.rand(1024, 64, 56, 56, device="cuda", generator=g) < 0.01).float()
+    w = torch.randn(64, 64, 3, 3, device="cuda", generator=g) * 0.06
+    b = torch.randn(64, device="cuda", generator=g) * 0.1
+    y = _run(x, w, b, 2)
+    prev = torch.backends.cudnn.allow_tf32
+    torch.backends.cudnn.allow_tf32 = False
+    try:
+        ref = torch.nn.functional.conv2d(x, w, b, 1, 1)
+    finally:
+        torch.backends.cudnn.allow_tf32 = prev
+    assert (y - ref).abs().max().item() <= RTOL * ref.abs().max().item()
+    from sparseflow_b200 import _lib
+    assert _lib.conv_status(x.device) == 0

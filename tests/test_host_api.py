@@ -159,7 +159,10 @@ def test_native_argument_checks_without_gpu():
     assert lib.sf_prescan2d(None, ctypes.byref(d), None, None, None, None, None, 0, None) == _lib.SF_ERR_INVALID_ARG
     cd = _lib.ConvDesc(1, 8, 8, 8, 8, 8, 8, 5, 1, 2, 0, 0, 0)
     assert lib.sf_sparse_conv2d(16, 16, None, 16, ctypes.byref(cd), 16, 1 << 20, None) == _lib.SF_ERR_UNSUPPORTED
-    assert lib.sf_packed_weight_bytes(64, 32, 3, 0) == 32 * 9 * 64 * 4
+    # gather layout, then (3x3, C_in <= 64) the tensor-core section at the next 256-byte boundary:
+    # digit scales [3][64] fp32 and the digit image [9 taps][2 slices of 16 ch][3 * 64 rows][16 B]
+    assert lib.sf_packed_weight_bytes(64, 32, 3, 0) == 32 * 9 * 64 * 4 + 3 * 64 * 4 + 9 * 2 * 192 * 16
+    assert lib.sf_packed_weight_bytes(64, 256, 1, 0) == 256 * 64 * 4
     assert lib.sf_packed_weight_bytes(128, 128, 3, 0) == 128 * 9 * 128 * 4
     cd = _lib.ConvDesc(2, 64, 56, 56, 64, 56, 56, 3, 1, 1, 0, 0, 1)
     assert lib.sf_sparse_conv2d_workspace_size(ctypes.byref(cd)) == 2 * 56 * 56 * 8 + 256
