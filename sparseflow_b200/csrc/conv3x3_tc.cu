@@ -30,13 +30,13 @@
 // unit is U consecutive tiles of one 64-channel output block.
 //
 // Per CTA (persistent, one per SM, a contiguous range of units):
-//   warps 0-15  convert: read x (NCHW, lane = input position: coalesced rows
+//   warps 0-11  convert: read x (NCHW, lane = input position: coalesced rows
 //               of 32 values per channel), write the int8 A rows of a unit
 //               into one of two A buffers, flag non-binary units;
-//   warps 16-23 epilogue: per tile, tcgen05.ld the three planes (lane =
+//   warps 12-27 epilogue: per tile, tcgen05.ld the three planes (lane =
 //               position), combine, add bias, store y (lane = position: rows
 //               of NCHW written as 128-byte runs);
-//   warp 24     allocates TMEM (two accumulators of 3 * 64 columns), copies
+//   warp 28     allocates TMEM (two accumulators of 3 * 64 columns), copies
 //               the weight digits of the current output block into shared
 //               memory, and issues 9 taps x C/32 MMAs per tile.
 // Every mbarrier wait gives up after one second (error word set, CTA
@@ -53,12 +53,31 @@ namespace {
 
 using conv::mbar_arrive;
 
-constexpr int kConvWarps = 16;
-constexpr int kEpiWarps = 8;
+#ifndef SF_C3TC_EXP
+#define SF_C3TC_EXP 0
+#endif
+constexpr int kConvWarps = 12;
+constexpr int kEpiWarps = 16;
 constexpr int kMmaWarp = kConvWarps + kEpiWarps;
 constexpr int kThreads = (kMmaWarp + 1) * 32;
 constexpr int kM = 128;
 constexpr int kTags = 4;
+
+// Division of n < 2^31 by a fixed divisor d >= 1 with a multiply-high
+// (round-up reciprocal m = floor(2^32 (2^s - d) / d) + 1, s = ceil(log2 d)):
+// q = (umulhi(m, n) + n) >> s.
+struct FastDiv {
+  uint32_t d, m, s;
+};
+inline FastDiv make_fastdiv(uint32_t d) {
+  uint32_t s = 0;
+  while ((1ull << s) < d) ++s;
+  const uint64_t m = ((1ull << 32) * ((1ull << s) - d)) / d + 1;
+  return FastDiv{d, (uint32_t)m, s};
+}
+__device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv& f) {
+  return (__umulhi(f.m, n) + n) >> f.s;
+}
 
 struct Params {
   const void* x;
@@ -70,6 +89,7 @@ struct Params {
   void* y;
   uint32_t* err;
   int N, C, H, W, Co, Wp, Hs;
+  FastDiv fd_wp, fd_hs;  // by Wp and by H + 1
   int kcores, CB, N3, ncob;
   long long ntiles, upcob, nunits, units_per_cta;
   int U;
@@ -80,6 +100,7 @@ struct Bars {
   uint64_t a_full[2], a_empty[2], d_full[2], d_empty[2], b_full, b_free;
   uint32_t tmem_base;
   uint32_t tag[kTags];  // = u + 1 when unit u holds a value other than 0 / 1
+  float2 tab[kEpiWarps][16];
 };
 
 template <typename XT>
@@ -197,7 +218,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
               const uint64_t ad = tc::desc_interleave(asa + (uint32_t)ks * p.a_plane + shift, p.a_plane, 128u);
               const uint64_t bd =
                   tc::desc_interleave(bsa + (uint32_t)(tap * p.kcores + ks) * lbo_b, lbo_b, 128u);
-              tc::mma_s8(dt, ad, bd, idesc, acc);
+              if (SF_C3TC_EXP != 3) tc::mma_s8(dt, ad, bd, idesc, acc);
               acc = 1u;
             }
           }
@@ -211,17 +232,30 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
     __syncwarp();
   } else if (warp >= kConvWarps) {
     // Epilogue: warp w reads TMEM lane quarter w % 4 (32 positions of the
-    // tile) and half of the block's output channels.
+    // tile) and a quarter of the block's output channels.
     const int ew = warp - kConvWarps;
     const int qd = warp & 3;
-    const int half = ew >> 2;
-    const int cw = p.CB / 2;
+    const int cwq = p.CB / 4;        // channels of this warp: 16 (CB 64) or 8 (CB 32)
+    const int cbeg = (ew >> 2) * cwq;
+    float2* tab = bars->tab[ew];     // (scale of digit 2, bias) of this warp's channels
+    int tab_cob = -1;
     long long g = 0;
     for (int i = 0; i < nu && !failed; ++i) {
       const long long u = u0 + i;
       const int cob = (int)(u / p.upcob);
       const long long t0 = (u - (long long)cob * p.upcob) * p.U;
       const int nt = (int)min((long long)p.U, p.ntiles - t0);
+      const int cbase = cob * p.CB + cbeg;
+      if (cob != tab_cob) {
+        if (lane < cwq) {
+          const int co = cbase + lane;
+          tab[lane] = co < p.Co ? make_float2(__ldg(p.scales + 2 * p.ncob * p.CB + co), p.bias ? __ldg(p.bias + co) : 0.f)
+                                : make_float2(0.f, 0.f);
+        }
+        __syncwarp();
+        tab_cob = cob;
+      }
+      const int nco = min(cwq, p.Co - cbase);  // valid channels of this warp (may be <= 0)
       for (int j = 0; j < nt; ++j, ++g) {
         const int d = (int)(g & 1);
         if (!mbar_wait_ns(&bars->d_full[d], (uint32_t)((g >> 1) & 1))) {
@@ -231,45 +265,50 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
         tc::fence_after();
         const bool odd = *reinterpret_cast<volatile uint32_t*>(&bars->tag[u % kTags]) == (uint32_t)(u + 1);
         // This lane's output position.
-        const long long o = (t0 + j) * kM + qd * 32 + lane;
-        const long long Ro = o / p.Wp;
+        const uint32_t o = (uint32_t)((t0 + j) * kM) + qd * 32 + lane;
+        const uint32_t Ro = fdiv(o, p.fd_wp);
         const int c = (int)(o - Ro * p.Wp);
-        const long long img = Ro / p.Hs;
+        const uint32_t img = fdiv(Ro, p.fd_hs);
         const int h = (int)(Ro - img * p.Hs);
-        const bool valid = c < p.W && h < p.H && img < p.N;
-        const size_t pix = (size_t)h * p.W + c;
-        XT* ybase = static_cast<XT*>(p.y) + (size_t)img * p.Co * HW + pix;
-        const int cbeg = half * cw;
+        const bool valid = c < p.W && h < p.H && img < (uint32_t)p.N;
+        XT* yp = static_cast<XT*>(p.y) + ((size_t)img * p.Co + cbase) * HW + (size_t)h * p.W + c;
+#if SF_C3TC_EXP == 1
+        if (false) {
+#else
         if (!odd) {
-          for (int cc = cbeg; cc < cbeg + cw; cc += 16) {
-            uint32_t r0[16], r1[16], r2[16];
-            const uint32_t ta = tmem + ((uint32_t)(qd * 32) << 16) + (uint32_t)(d * p.N3 + cc);
-            tc::tmem_ld16(ta, r0);
-            tc::tmem_ld16(ta + (uint32_t)p.CB, r1);
-            tc::tmem_ld16(ta + (uint32_t)(2 * p.CB), r2);
+#endif
+          for (int c8 = 0; c8 < cwq; c8 += 8) {
+            uint32_t r0[8], r1[8], r2[8];
+            const uint32_t ta = tmem + ((uint32_t)(qd * 32) << 16) + (uint32_t)(d * p.N3 + cbeg + c8);
+            tc::tmem_ld8(ta, r0);
+            tc::tmem_ld8(ta + (uint32_t)p.CB, r1);
+            tc::tmem_ld8(ta + (uint32_t)(2 * p.CB), r2);
             tc::tmem_wait_ld();
+            if (valid) {
+              XT* yq = yp + (size_t)c8 * HW;
 #pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const int co = cob * p.CB + cc + e;
-              if (valid && co < p.Co) {
-                const int sidx = cob * p.CB + cc + e;
-                const float b = p.bias ? __ldg(p.bias + co) : 0.f;
-                const float s0 = __ldg(p.scales + sidx);
-                const float s1 = __ldg(p.scales + p.ncob * p.CB + sidx);
-                const float s2 = __ldg(p.scales + 2 * p.ncob * p.CB + sidx);
-                float v = fmaf(s2, (float)(int)r2[e], b);
-                v = fmaf(s1, (float)(int)r1[e], v);
-                v = fmaf(s0, (float)(int)r0[e], v);
-                ybase[(size_t)co * HW] = DT<XT>::from_f(v);
+              for (int e = 0; e < 8; ++e, yq += HW) {
+                if (c8 + e < nco) {
+                  // |D| < 2^22, so adding 1.5 * 2^23 to the bits gives the float
+                  // 1.5 * 2^23 + D exactly (no conversion instruction); the scaled
+                  // digit sums are then exact, and only their sum rounds.
+                  const float a0 = __int_as_float((int)r0[e] + 0x4B400000);
+                  const float a1 = __int_as_float((int)r1[e] + 0x4B400000);
+                  const float a2 = __int_as_float((int)r2[e] + 0x4B400000);
+                  const float x0 = fmaf(a0, 65536.f, -12582912.f * 65536.f);
+                  const float x1 = fmaf(a1, 256.f, -12582912.f * 256.f);
+                  const float x2 = a2 - 12582912.f;
+                  const float2 sb = tab[c8 + e];
+                  *yq = DT<XT>::from_f(fmaf(sb.x, (x0 + x1) + x2, sb.y));
+                }
               }
             }
           }
-        } else if (valid) {
+        } else if (valid && SF_C3TC_EXP != 1) {
           // Values other than 0 / 1: fp32 FMAs from x and the weights.
           const XT* ximg = x + (size_t)img * p.C * HW;
-          for (int cc = cbeg; cc < cbeg + cw; ++cc) {
-            const int co = cob * p.CB + cc;
-            if (co >= p.Co) break;
+          for (int cc = 0; cc < nco; ++cc) {
+            const int co = cbase + cc;
             float acc = 0.f;
             for (int ci = 0; ci < p.C; ++ci) {
               for (int tap = 0; tap < 9; ++tap) {
@@ -279,7 +318,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
                 if (xv != 0.f) acc = fmaf(xv, gather_w<WT>(p, co, ci, tap), acc);
               }
             }
-            ybase[(size_t)co * HW] = DT<XT>::from_f(acc + (p.bias ? __ldg(p.bias + co) : 0.f));
+            yp[(size_t)cc * HW] = DT<XT>::from_f(acc + (p.bias ? __ldg(p.bias + co) : 0.f));
           }
         }
         tc::fence_before();
@@ -289,53 +328,69 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
     }
     if (failed && lane == 0) atomicExch(p.err, 1u);
   } else {
-    // Converters: work item = (group of 32 A rows, pair of 16-channel slices).
-    const int npairs = p.kcores / 2;
-    const int items = (int)(p.rows_a / 32) * npairs;
+    // Converters: work item = (group of 32 A rows, 16-channel slice); lane =
+    // row. The loads of a warp's next item are issued before the current one
+    // is converted, so x reads stay in flight while the warp packs bytes.
+    const int kc_n = p.kcores;
+    const int items = (int)(p.rows_a / 32) * kc_n;
     for (int i = 0; i < nu && !failed; ++i) {
       const long long u = u0 + i;
       const int cob = (int)(u / p.upcob);
       const long long t0 = (u - (long long)cob * p.upcob) * p.U;
+      const long long q0 = t0 * kM;
+      auto load_item = [&](int it, uint32_t (&ub)[16]) {
+        const int grp = it / kc_n, kc = it - grp * kc_n;
+        const uint32_t q = (uint32_t)q0 + grp * 32 + lane;
+        const uint32_t R = fdiv(q, p.fd_wp);
+        const int iw = (int)(q - R * p.Wp) - 1;
+        const uint32_t R1 = R - 1;  // wraps past 2^31 for the top padding row
+        const uint32_t img = fdiv(R1 & 0x7fffffffu, p.fd_hs);
+        const int h = (int)(R1 - img * p.Hs);
+        const bool valid = R >= 1 && iw >= 0 && iw < p.W && h < p.H && img < (uint32_t)p.N;
+        const int c0 = kc * 16;
+        const XT* src = x + ((size_t)img * p.C + c0) * HW + (size_t)h * p.W + iw;
+        const int ne = valid ? min(16, p.C - c0) : 0;
+#pragma unroll
+        for (int e = 0; e < 16; ++e, src += HW)
+          ub[e] = (SF_C3TC_EXP != 2 && e < ne) ? raw_bits<XT>(*src) : 0u;
+      };
       const int a = i & 1;
+      uint32_t cur[16], nxt[16];
+      int it = warp;
+      if (it < items) load_item(it, cur);
       if (i >= 2 && !mbar_wait_ns(&bars->a_empty[a], (uint32_t)(((i >> 1) - 1) & 1))) {
         failed = true;
         break;
       }
       unsigned char* ab = abuf + (size_t)a * p.a_bytes;
-      const long long q0 = t0 * kM;
       uint32_t nb = 0u;
-      for (int it = warp; it < items; it += kConvWarps) {
-        const int grp = it / npairs, kp = it - grp * npairs;
-        const int r = grp * 32 + lane;
-        const long long q = q0 + r;
-        const long long R = q / p.Wp;
-        const int iw = (int)(q - R * p.Wp) - 1;
-        const long long R1 = R - 1;
-        const long long img = R1 >= 0 ? R1 / p.Hs : 0;
-        const int h = (int)(R1 - img * p.Hs);
-        const bool valid = R1 >= 0 && iw >= 0 && iw < p.W && h < p.H && img < p.N;
-        const int c0 = kp * 32;
-        const XT* src = x + ((size_t)img * p.C + c0) * HW + (size_t)h * p.W + iw;
-        uint32_t ub[32];
+      for (; it < items; it += kConvWarps) {
+        const int nx = it + kConvWarps;
+        if (nx < items) load_item(nx, nxt);
+        uint32_t wv[4];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) ub[e] = (valid && c0 + e < p.C) ? raw_bits<XT>(src[(size_t)e * HW]) : 0u;
+        for (int k = 0; k < 4; ++k) {
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          uint32_t wv[4];
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            uint32_t w = 0u;
-#pragma unroll
-            for (int b = 0; b < 4; ++b) {
-              const uint32_t uu = ub[hh * 16 + k * 4 + b];
-              nb |= (uu != 0u) & (uu != one_bits<XT>());
-              w |= (uint32_t)(uu != 0u) << (8 * b);
-            }
-            wv[k] = w;
+          for (int b = 0; b < 4; ++b) {
+            const uint32_t uu = cur[4 * k + b];
+            nb |= min(uu, uu ^ one_bits<XT>());  // 0 exactly when uu is 0 or 1
           }
-          *reinterpret_cast<uint4*>(ab + (size_t)(2 * kp + hh) * p.a_plane + (size_t)r * 16) =
-              make_uint4(wv[0], wv[1], wv[2], wv[3]);
+          if constexpr (std::is_same<XT, __half>::value) {
+            wv[k] = (uint32_t)(cur[4 * k] != 0u) | ((uint32_t)(cur[4 * k + 1] != 0u) << 8) |
+                    ((uint32_t)(cur[4 * k + 2] != 0u) << 16) | ((uint32_t)(cur[4 * k + 3] != 0u) << 24);
+          } else {
+            // The high byte of 1.0 (0x3f in fp32 and bf16) has bit 0 set; of 0.0, clear.
+            constexpr uint32_t sel = sizeof(XT) == 4 ? 0x0073u : 0x0051u;
+            const uint32_t lo = __byte_perm(cur[4 * k], cur[4 * k + 1], sel);
+            const uint32_t hi = __byte_perm(cur[4 * k + 2], cur[4 * k + 3], sel);
+            wv[k] = __byte_perm(lo, hi, 0x5410) & 0x01010101u;
+          }
         }
+        const int grp = it / kc_n, kc = it - grp * kc_n;
+        *reinterpret_cast<uint4*>(ab + (size_t)kc * p.a_plane + (size_t)(grp * 32 + lane) * 16) =
+            make_uint4(wv[0], wv[1], wv[2], wv[3]);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) cur[e] = nxt[e];
       }
       if (__any_sync(0xffffffffu, nb != 0u) && lane == 0)
         *reinterpret_cast<volatile uint32_t*>(&bars->tag[u % kTags]) = (uint32_t)(u + 1);
@@ -498,13 +553,16 @@ sf_status run_conv3x3_tc(const void* x, const void* w_gather, int cpl, const voi
   p.N = N; p.C = C; p.H = H; p.W = W; p.Co = Co;
   p.Wp = W + 2;
   p.Hs = H + 1;
+  p.fd_wp = make_fastdiv((uint32_t)p.Wp);
+  p.fd_hs = make_fastdiv((uint32_t)p.Hs);
   p.kcores = g.kcores;
   p.CB = g.CB;
   p.N3 = g.N3;
   p.ncob = g.ncob;
   const long long positions = (long long)N * p.Hs * p.Wp;
   p.ntiles = (positions + kM - 1) / kM;
-  if (p.ntiles >= (1ll << 30)) return SF_ERR_UNSUPPORTED;
+  // Positions (and the A rows past the last tile) are decoded in 32 bits.
+  if (p.ntiles * kM + 4ll * kM + 2ll * p.Wp >= (1ll << 31)) return SF_ERR_UNSUPPORTED;
   p.b_bytes = (uint32_t)g.b_bytes;
   const size_t limit = 227 * 1024;
   size_t smem = 0;
