@@ -30,13 +30,13 @@
 // unit is U consecutive tiles of one 64-channel output block.
 //
 // Per CTA (persistent, one per SM, a contiguous range of units):
-//   warps 0-11  convert: read x (NCHW, lane = input position: coalesced rows
+//   warps 0-7   convert: read x (NCHW, lane = input position: coalesced rows
 //               of 32 values per channel), write the int8 A rows of a unit
 //               into one of two A buffers, flag non-binary units;
-//   warps 12-27 epilogue: per tile, tcgen05.ld the three planes (lane =
+//   warps 8-23  epilogue: per tile, tcgen05.ld the three planes (lane =
 //               position), combine, add bias, store y (lane = position: rows
 //               of NCHW written as 128-byte runs);
-//   warp 28     allocates TMEM (two accumulators of 3 * 64 columns), copies
+//   warp 24     allocates TMEM (two accumulators of 3 * 64 columns), copies
 //               the weight digits of the current output block into shared
 //               memory, and issues 9 taps x C/32 MMAs per tile.
 // Every mbarrier wait gives up after one second (error word set, CTA
@@ -53,10 +53,7 @@ namespace {
 
 using conv::mbar_arrive;
 
-#ifndef SF_C3TC_EXP
-#define SF_C3TC_EXP 0
-#endif
-constexpr int kConvWarps = 12;
+constexpr int kConvWarps = 8;
 constexpr int kEpiWarps = 16;
 constexpr int kMmaWarp = kConvWarps + kEpiWarps;
 constexpr int kThreads = (kMmaWarp + 1) * 32;
@@ -100,7 +97,7 @@ struct Bars {
   uint64_t a_full[2], a_empty[2], d_full[2], d_empty[2], b_full, b_free;
   uint32_t tmem_base;
   uint32_t tag[kTags];  // = u + 1 when unit u holds a value other than 0 / 1
-  float2 tab[kEpiWarps][16];
+  alignas(16) float2 tab[kEpiWarps][16];
 };
 
 template <typename XT>
@@ -125,7 +122,134 @@ __device__ __forceinline__ float gather_w(const Params& p, int co, int ci, int t
   return DT<WT>::to_f(*w);
 }
 
-template <typename XT, typename WT>
+// Converter work for one unit, scalar form (any W, any dtype): item =
+// (group of 32 A rows, 16-channel slice), lane = A row.
+template <typename XT>
+__device__ __forceinline__ void convert_unit_scalar(const Params& p, const XT* __restrict__ x, unsigned char* ab,
+                                                    long long q0, int warp, int lane, uint32_t& nb) {
+  const size_t HW = (size_t)p.H * p.W;
+  const int kc_n = p.kcores;
+  const int items = (int)(p.rows_a / 32) * kc_n;
+  for (int it = warp; it < items; it += kConvWarps) {
+    const int grp = it / kc_n, kc = it - grp * kc_n;
+    const uint32_t q = (uint32_t)q0 + grp * 32 + lane;
+    const uint32_t R = fdiv(q, p.fd_wp);
+    const int iw = (int)(q - R * p.Wp) - 1;
+    const uint32_t R1 = R - 1;  // wraps for the top padding row; R >= 1 is tested below
+    const uint32_t img = fdiv(R1 & 0x7fffffffu, p.fd_hs);
+    const int h = (int)(R1 - img * p.Hs);
+    const bool valid = R >= 1 && iw >= 0 && iw < p.W && h < p.H && img < (uint32_t)p.N;
+    const int c0 = kc * 16;
+    const XT* src = x + ((size_t)img * p.C + c0) * HW + (size_t)h * p.W + iw;
+    const int ne = valid ? min(16, p.C - c0) : 0;
+    uint32_t ub[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) ub[e] = e < ne ? raw_bits<XT>(src[(uint32_t)e * (uint32_t)HW]) : 0u;
+    uint32_t wv[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      uint32_t w = 0u;
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const uint32_t uu = ub[4 * k + b];
+        nb |= min(uu, uu ^ one_bits<XT>());  // 0 exactly when uu is 0 or 1
+        w |= (uint32_t)(uu != 0u) << (8 * b);
+      }
+      wv[k] = w;
+    }
+    *reinterpret_cast<uint4*>(ab + (size_t)kc * p.a_plane + (size_t)(grp * 32 + lane) * 16) =
+        make_uint4(wv[0], wv[1], wv[2], wv[3]);
+  }
+}
+
+// Converter work for one unit, fp32 rows of a multiple of 4 values (16-byte
+// aligned): lane task = (padded row, quad of 4 columns), item = 32 tasks x
+// 8 channels (half of a 16-channel slice); each lane loads 8 float4 (4
+// positions x 8 channels), tests x*x == x (true exactly for 0 and 1; -0
+// counts as 0, NaN fails) and writes the 8-byte halves of four A rows. The
+// two padding columns of each row are written as zeros by a separate loop.
+__device__ __forceinline__ void convert_unit_vec4(const Params& p, const float* __restrict__ x, unsigned char* ab,
+                                                  long long q0, int warp, int lane, uint32_t& nb) {
+  const uint32_t HW = (uint32_t)(p.H * p.W);
+  const int kh_n = p.kcores * 2;  // 8-channel halves
+  const uint32_t R0 = fdiv((uint32_t)q0, p.fd_wp);
+  const uint32_t Rl = fdiv((uint32_t)q0 + p.rows_a - 1, p.fd_wp);
+  const int nrows = (int)(Rl - R0) + 1;
+  const int qw = p.W >> 2;
+  const int ntask = nrows * qw;
+  const int ngrp = (ntask + 31) >> 5;
+  const int items = ngrp * kh_n;
+  const int rows_a = (int)p.rows_a;
+  for (int it = warp; it < items; it += kConvWarps) {
+    const int grp = it / kh_n, kh = it - grp * kh_n;
+    const int t = grp * 32 + lane;
+    const int rr = t / qw, k4 = t - rr * qw;
+    const uint32_t R = R0 + rr;
+    const int r = (int)(R * p.Wp + 1 + 4 * k4 - (uint32_t)q0);  // A row of column 4 * k4
+    const uint32_t R1 = R - 1;
+    const uint32_t img = fdiv(R1 & 0x7fffffffu, p.fd_hs);
+    const int h = (int)(R1 - img * p.Hs);
+    const bool inside = t < ntask && r + 3 >= 0 && r < rows_a;
+    const bool valid = inside && R >= 1 && h < p.H && img < (uint32_t)p.N;
+    const int c0 = kh * 8;
+    float4 v[8];
+    if (valid) {
+      const float4* src =
+          reinterpret_cast<const float4*>(x + ((size_t)img * p.C + c0) * HW + (size_t)h * p.W) + k4;
+      const uint32_t step = HW >> 2;
+      const int ne = min(8, p.C - c0);
+      if (ne == 8) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = __ldg(src + e * step);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = e < ne ? __ldg(src + e * step) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    uint32_t chk = 0u;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      chk |= __float_as_uint(fmaf(v[e].x, v[e].x, -v[e].x)) | __float_as_uint(fmaf(v[e].y, v[e].y, -v[e].y)) |
+             __float_as_uint(fmaf(v[e].z, v[e].z, -v[e].z)) | __float_as_uint(fmaf(v[e].w, v[e].w, -v[e].w));
+    }
+    nb |= chk;
+    if (inside) {
+      unsigned char* dst = ab + (size_t)(kh >> 1) * p.a_plane + (size_t)(kh & 1) * 8;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint32_t wv[2];
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk) {
+          const float* a0 = reinterpret_cast<const float*>(&v[4 * kk]);
+          const float* a1 = reinterpret_cast<const float*>(&v[4 * kk + 1]);
+          const float* a2 = reinterpret_cast<const float*>(&v[4 * kk + 2]);
+          const float* a3 = reinterpret_cast<const float*>(&v[4 * kk + 3]);
+          // The high byte of 1.0f (0x3f) has bit 0 set; of 0.0f, clear.
+          const uint32_t lo = __byte_perm(__float_as_uint(a0[j]), __float_as_uint(a1[j]), 0x0073u);
+          const uint32_t hi = __byte_perm(__float_as_uint(a2[j]), __float_as_uint(a3[j]), 0x0073u);
+          wv[kk] = __byte_perm(lo, hi, 0x5410u) & 0x01010101u;
+        }
+        if (r + j >= 0 && r + j < rows_a)
+          *reinterpret_cast<uint2*>(dst + (size_t)(r + j) * 16) = make_uint2(wv[0], wv[1]);
+      }
+    }
+  }
+  // Padding columns 0 and W + 1 of every padded row the unit touches.
+  const int kc_n = p.kcores;
+  const int npad = nrows * 2 * kc_n;
+  for (int t = warp * 32 + lane; t < npad; t += kConvWarps * 32) {
+    const int rr = t / (2 * kc_n), rem = t - rr * 2 * kc_n;
+    const int side = rem / kc_n, kc = rem - side * kc_n;
+    const int r = (int)((R0 + rr) * p.Wp + (side ? p.W + 1 : 0) - (uint32_t)q0);
+    if (r >= 0 && r < rows_a)
+      *reinterpret_cast<uint4*>(ab + (size_t)kc * p.a_plane + (size_t)r * 16) = make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+
+template <typename XT, typename WT, bool VEC>
 __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p) {
   extern __shared__ __align__(128) unsigned char smem[];
   unsigned char* bsm = smem;
@@ -179,7 +303,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
           if (cur_cob >= 0) {
             // Every MMA reading the old weights must finish before they are replaced.
             tc::mma_commit(&bars->b_free);
-            if (!mbar_wait_ns(&bars->b_free, (uint32_t)((bloads - 1) & 1))) {
+            if (!tc::mbar_wait_sleep(&bars->b_free, (uint32_t)((bloads - 1) & 1))) {
               failed = true;
               break;
             }
@@ -188,7 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
           const unsigned char* src = p.bimg + (size_t)cob * p.b_bytes;
           for (uint32_t off = 0; off < p.b_bytes; off += 32768u)
             bulk_g2s(bsm + off, src + off, min(32768u, p.b_bytes - off), &bars->b_full);
-          if (!mbar_wait_ns(&bars->b_full, (uint32_t)(bloads & 1))) {
+          if (!tc::mbar_wait_sleep(&bars->b_full, (uint32_t)(bloads & 1))) {
             failed = true;
             break;
           }
@@ -196,7 +320,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
           cur_cob = cob;
         }
         const int a = i & 1;
-        if (!mbar_wait_ns(&bars->a_full[a], (uint32_t)((i >> 1) & 1))) {
+        if (!tc::mbar_wait_sleep(&bars->a_full[a], (uint32_t)((i >> 1) & 1))) {
           failed = true;
           break;
         }
@@ -204,7 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
         const uint32_t asa = smem_u32(abuf + (size_t)a * p.a_bytes);
         for (int j = 0; j < nt; ++j, ++g) {
           const int d = (int)(g & 1);
-          if (g >= 2 && !mbar_wait_ns(&bars->d_empty[d], (uint32_t)(((g >> 1) - 1) & 1))) {
+          if (g >= 2 && !tc::mbar_wait_sleep(&bars->d_empty[d], (uint32_t)(((g >> 1) - 1) & 1))) {
             failed = true;
             break;
           }
@@ -218,7 +342,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
               const uint64_t ad = tc::desc_interleave(asa + (uint32_t)ks * p.a_plane + shift, p.a_plane, 128u);
               const uint64_t bd =
                   tc::desc_interleave(bsa + (uint32_t)(tap * p.kcores + ks) * lbo_b, lbo_b, 128u);
-              if (SF_C3TC_EXP != 3) tc::mma_s8(dt, ad, bd, idesc, acc);
+              tc::mma_s8(dt, ad, bd, idesc, acc);
               acc = 1u;
             }
           }
@@ -232,12 +356,13 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
     __syncwarp();
   } else if (warp >= kConvWarps) {
     // Epilogue: warp w reads TMEM lane quarter w % 4 (32 positions of the
-    // tile) and a quarter of the block's output channels.
+    // tile) and a quarter of the block's output channels (16, or 8 when the
+    // block is 32 wide).
     const int ew = warp - kConvWarps;
     const int qd = warp & 3;
-    const int cwq = p.CB / 4;        // channels of this warp: 16 (CB 64) or 8 (CB 32)
+    const int cwq = p.CB / 4;
     const int cbeg = (ew >> 2) * cwq;
-    float2* tab = bars->tab[ew];     // (scale of digit 2, bias) of this warp's channels
+    float2* tab = bars->tab[ew];  // (scale of digit 2, bias) of this warp's channels
     int tab_cob = -1;
     long long g = 0;
     for (int i = 0; i < nu && !failed; ++i) {
@@ -247,10 +372,11 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
       const int nt = (int)min((long long)p.U, p.ntiles - t0);
       const int cbase = cob * p.CB + cbeg;
       if (cob != tab_cob) {
-        if (lane < cwq) {
+        if (lane < 16) {
           const int co = cbase + lane;
-          tab[lane] = co < p.Co ? make_float2(__ldg(p.scales + 2 * p.ncob * p.CB + co), p.bias ? __ldg(p.bias + co) : 0.f)
-                                : make_float2(0.f, 0.f);
+          tab[lane] = (lane < cwq && co < p.Co)
+                          ? make_float2(__ldg(p.scales + 2 * p.ncob * p.CB + co), p.bias ? __ldg(p.bias + co) : 0.f)
+                          : make_float2(0.f, 0.f);
         }
         __syncwarp();
         tab_cob = cob;
@@ -258,7 +384,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
       const int nco = min(cwq, p.Co - cbase);  // valid channels of this warp (may be <= 0)
       for (int j = 0; j < nt; ++j, ++g) {
         const int d = (int)(g & 1);
-        if (!mbar_wait_ns(&bars->d_full[d], (uint32_t)((g >> 1) & 1))) {
+        if (!tc::mbar_wait_sleep(&bars->d_full[d], (uint32_t)((g >> 1) & 1))) {
           failed = true;
           break;
         }
@@ -272,39 +398,36 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
         const int h = (int)(Ro - img * p.Hs);
         const bool valid = c < p.W && h < p.H && img < (uint32_t)p.N;
         XT* yp = static_cast<XT*>(p.y) + ((size_t)img * p.Co + cbase) * HW + (size_t)h * p.W + c;
-#if SF_C3TC_EXP == 1
-        if (false) {
-#else
         if (!odd) {
-#endif
-          for (int c8 = 0; c8 < cwq; c8 += 8) {
-            uint32_t r0[8], r1[8], r2[8];
-            const uint32_t ta = tmem + ((uint32_t)(qd * 32) << 16) + (uint32_t)(d * p.N3 + cbeg + c8);
-            tc::tmem_ld8(ta, r0);
-            tc::tmem_ld8(ta + (uint32_t)p.CB, r1);
-            tc::tmem_ld8(ta + (uint32_t)(2 * p.CB), r2);
-            tc::tmem_wait_ld();
-            if (valid) {
-              XT* yq = yp + (size_t)c8 * HW;
+          uint32_t r0[16], r1[16], r2[16];
+          const uint32_t ta = tmem + ((uint32_t)(qd * 32) << 16) + (uint32_t)(d * p.N3 + cbeg);
+          tc::tmem_ld16(ta, r0);
+          tc::tmem_ld16(ta + (uint32_t)p.CB, r1);
+          tc::tmem_ld16(ta + (uint32_t)(2 * p.CB), r2);
+          tc::tmem_wait_ld();
+          if (valid) {
+            const float4* tb = reinterpret_cast<const float4*>(tab);
+            // |D| < 2^22, so adding 1.5 * 2^23 to the bits gives the float
+            // 1.5 * 2^23 + D exactly (no conversion instruction); the scaled
+            // digit sums are then exact, and only their sum rounds.
 #pragma unroll
-              for (int e = 0; e < 8; ++e, yq += HW) {
-                if (c8 + e < nco) {
-                  // |D| < 2^22, so adding 1.5 * 2^23 to the bits gives the float
-                  // 1.5 * 2^23 + D exactly (no conversion instruction); the scaled
-                  // digit sums are then exact, and only their sum rounds.
-                  const float a0 = __int_as_float((int)r0[e] + 0x4B400000);
-                  const float a1 = __int_as_float((int)r1[e] + 0x4B400000);
-                  const float a2 = __int_as_float((int)r2[e] + 0x4B400000);
-                  const float x0 = fmaf(a0, 65536.f, -12582912.f * 65536.f);
-                  const float x1 = fmaf(a1, 256.f, -12582912.f * 256.f);
-                  const float x2 = a2 - 12582912.f;
-                  const float2 sb = tab[c8 + e];
-                  *yq = DT<XT>::from_f(fmaf(sb.x, (x0 + x1) + x2, sb.y));
-                }
+            for (int e = 0; e < 16; e += 2) {
+              if (e >= nco) break;
+              const float4 sb = tb[e >> 1];
+#pragma unroll
+              for (int f = 0; f < 2; ++f) {
+                const float a0 = __int_as_float((int)r0[e + f] + 0x4B400000);
+                const float a1 = __int_as_float((int)r1[e + f] + 0x4B400000);
+                const float a2 = __int_as_float((int)r2[e + f] + 0x4B400000);
+                const float x0 = fmaf(a0, 65536.f, -12582912.f * 65536.f);
+                const float x1 = fmaf(a1, 256.f, -12582912.f * 256.f);
+                const float x2 = a2 - 12582912.f;
+                const float v = fmaf(f ? sb.z : sb.x, (x0 + x1) + x2, f ? sb.w : sb.y);
+                if (e + f < nco) yp[(uint32_t)(e + f) * (uint32_t)HW] = DT<XT>::from_f(v);
               }
             }
           }
-        } else if (valid && SF_C3TC_EXP != 1) {
+        } else if (valid) {
           // Values other than 0 / 1: fp32 FMAs from x and the weights.
           const XT* ximg = x + (size_t)img * p.C * HW;
           for (int cc = 0; cc < nco; ++cc) {
@@ -328,70 +451,21 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
     }
     if (failed && lane == 0) atomicExch(p.err, 1u);
   } else {
-    // Converters: work item = (group of 32 A rows, 16-channel slice); lane =
-    // row. The loads of a warp's next item are issued before the current one
-    // is converted, so x reads stay in flight while the warp packs bytes.
-    const int kc_n = p.kcores;
-    const int items = (int)(p.rows_a / 32) * kc_n;
     for (int i = 0; i < nu && !failed; ++i) {
       const long long u = u0 + i;
       const int cob = (int)(u / p.upcob);
       const long long t0 = (u - (long long)cob * p.upcob) * p.U;
-      const long long q0 = t0 * kM;
-      auto load_item = [&](int it, uint32_t (&ub)[16]) {
-        const int grp = it / kc_n, kc = it - grp * kc_n;
-        const uint32_t q = (uint32_t)q0 + grp * 32 + lane;
-        const uint32_t R = fdiv(q, p.fd_wp);
-        const int iw = (int)(q - R * p.Wp) - 1;
-        const uint32_t R1 = R - 1;  // wraps past 2^31 for the top padding row
-        const uint32_t img = fdiv(R1 & 0x7fffffffu, p.fd_hs);
-        const int h = (int)(R1 - img * p.Hs);
-        const bool valid = R >= 1 && iw >= 0 && iw < p.W && h < p.H && img < (uint32_t)p.N;
-        const int c0 = kc * 16;
-        const XT* src = x + ((size_t)img * p.C + c0) * HW + (size_t)h * p.W + iw;
-        const int ne = valid ? min(16, p.C - c0) : 0;
-#pragma unroll
-        for (int e = 0; e < 16; ++e, src += HW)
-          ub[e] = (SF_C3TC_EXP != 2 && e < ne) ? raw_bits<XT>(*src) : 0u;
-      };
       const int a = i & 1;
-      uint32_t cur[16], nxt[16];
-      int it = warp;
-      if (it < items) load_item(it, cur);
-      if (i >= 2 && !mbar_wait_ns(&bars->a_empty[a], (uint32_t)(((i >> 1) - 1) & 1))) {
+      if (i >= 2 && !tc::mbar_wait_sleep(&bars->a_empty[a], (uint32_t)(((i >> 1) - 1) & 1))) {
         failed = true;
         break;
       }
       unsigned char* ab = abuf + (size_t)a * p.a_bytes;
       uint32_t nb = 0u;
-      for (; it < items; it += kConvWarps) {
-        const int nx = it + kConvWarps;
-        if (nx < items) load_item(nx, nxt);
-        uint32_t wv[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-#pragma unroll
-          for (int b = 0; b < 4; ++b) {
-            const uint32_t uu = cur[4 * k + b];
-            nb |= min(uu, uu ^ one_bits<XT>());  // 0 exactly when uu is 0 or 1
-          }
-          if constexpr (std::is_same<XT, __half>::value) {
-            wv[k] = (uint32_t)(cur[4 * k] != 0u) | ((uint32_t)(cur[4 * k + 1] != 0u) << 8) |
-                    ((uint32_t)(cur[4 * k + 2] != 0u) << 16) | ((uint32_t)(cur[4 * k + 3] != 0u) << 24);
-          } else {
-            // The high byte of 1.0 (0x3f in fp32 and bf16) has bit 0 set; of 0.0, clear.
-            constexpr uint32_t sel = sizeof(XT) == 4 ? 0x0073u : 0x0051u;
-            const uint32_t lo = __byte_perm(cur[4 * k], cur[4 * k + 1], sel);
-            const uint32_t hi = __byte_perm(cur[4 * k + 2], cur[4 * k + 3], sel);
-            wv[k] = __byte_perm(lo, hi, 0x5410) & 0x01010101u;
-          }
-        }
-        const int grp = it / kc_n, kc = it - grp * kc_n;
-        *reinterpret_cast<uint4*>(ab + (size_t)kc * p.a_plane + (size_t)(grp * 32 + lane) * 16) =
-            make_uint4(wv[0], wv[1], wv[2], wv[3]);
-#pragma unroll
-        for (int e = 0; e < 16; ++e) cur[e] = nxt[e];
-      }
+      if constexpr (VEC)
+        convert_unit_vec4(p, reinterpret_cast<const float*>(x), ab, t0 * kM, warp, lane, nb);
+      else
+        convert_unit_scalar<XT>(p, x, ab, t0 * kM, warp, lane, nb);
       if (__any_sync(0xffffffffu, nb != 0u) && lane == 0)
         *reinterpret_cast<volatile uint32_t*>(&bars->tag[u % kTags]) = (uint32_t)(u + 1);
       fence_proxy_async_smem();
@@ -497,7 +571,10 @@ Geo geometry(int Co, int C) {
 
 template <typename XT, typename WT>
 sf_status launch(Params p, size_t smem, cudaStream_t st) {
-  auto kern = conv3x3_tc_kernel<XT, WT>;
+  // 16-byte row loads: fp32 rows of a multiple of 4 values, 16-byte aligned x.
+  const bool vec = std::is_same<XT, float>::value && p.W % 4 == 0 &&
+                   (reinterpret_cast<uintptr_t>(p.x) & 15u) == 0;
+  auto kern = vec ? conv3x3_tc_kernel<XT, WT, true> : conv3x3_tc_kernel<XT, WT, false>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return SF_ERR_CUDA;
   const long long grid = (p.nunits + p.units_per_cta - 1) / p.units_per_cta;

@@ -61,5 +61,28 @@ __device__ __forceinline__ void mma_s8(uint32_t d_tmem, uint64_t a, uint64_t b, 
       : "memory");
 }
 
+// mbarrier wait that suspends the waiting thread in hardware (up to
+// `hint_ns` per try) instead of spinning, so idle warps leave the issue slots
+// to working ones; gives up (returns false) after `limit_ns` of wall time.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, uint64_t limit_ns = 1000000000ull) {
+  if (mbar_try_wait_hint(bar, parity, 20000u)) return true;
+  const uint64_t t0 = global_ns();
+  for (;;) {
+    if (mbar_try_wait_hint(bar, parity, 20000u)) return true;
+    if (global_ns() - t0 > limit_ns) return false;
+  }
+}
+
 }  // namespace tc
 }  // namespace sf
