@@ -30,13 +30,13 @@
 // unit is U consecutive tiles of one 64-channel output block.
 //
 // Per CTA (persistent, one per SM, a contiguous range of units):
-//   warps 0-7   convert: read x (NCHW, lane = input position: coalesced rows
+//   warps 0-14  convert: read x (NCHW, lane = input position: coalesced rows
 //               of 32 values per channel), write the int8 A rows of a unit
 //               into one of two A buffers, flag non-binary units;
-//   warps 8-23  epilogue: per tile, tcgen05.ld the three planes (lane =
+//   warps 15-30 epilogue: per tile, tcgen05.ld the three planes (lane =
 //               position), combine, add bias, store y (lane = position: rows
 //               of NCHW written as 128-byte runs);
-//   warp 24     allocates TMEM (two accumulators of 3 * 64 columns), copies
+//   warp 31     allocates TMEM (two accumulators of 3 * 64 columns), copies
 //               the weight digits of the current output block into shared
 //               memory, and issues 9 taps x C/32 MMAs per tile.
 // Every mbarrier wait gives up after one second (error word set, CTA
@@ -53,7 +53,7 @@ namespace {
 
 using conv::mbar_arrive;
 
-constexpr int kConvWarps = 8;
+constexpr int kConvWarps = 15;
 constexpr int kEpiWarps = 16;
 constexpr int kMmaWarp = kConvWarps + kEpiWarps;
 constexpr int kThreads = (kMmaWarp + 1) * 32;
@@ -399,31 +399,33 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
         const bool valid = c < p.W && h < p.H && img < (uint32_t)p.N;
         XT* yp = static_cast<XT*>(p.y) + ((size_t)img * p.Co + cbase) * HW + (size_t)h * p.W + c;
         if (!odd) {
-          uint32_t r0[16], r1[16], r2[16];
-          const uint32_t ta = tmem + ((uint32_t)(qd * 32) << 16) + (uint32_t)(d * p.N3 + cbeg);
-          tc::tmem_ld16(ta, r0);
-          tc::tmem_ld16(ta + (uint32_t)p.CB, r1);
-          tc::tmem_ld16(ta + (uint32_t)(2 * p.CB), r2);
-          tc::tmem_wait_ld();
-          if (valid) {
-            const float4* tb = reinterpret_cast<const float4*>(tab);
-            // |D| < 2^22, so adding 1.5 * 2^23 to the bits gives the float
-            // 1.5 * 2^23 + D exactly (no conversion instruction); the scaled
-            // digit sums are then exact, and only their sum rounds.
+          const float4* tb = reinterpret_cast<const float4*>(tab);
+          for (int c8 = 0; c8 < cwq; c8 += 8) {
+            uint32_t r0[8], r1[8], r2[8];
+            const uint32_t ta = tmem + ((uint32_t)(qd * 32) << 16) + (uint32_t)(d * p.N3 + cbeg + c8);
+            tc::tmem_ld8(ta, r0);
+            tc::tmem_ld8(ta + (uint32_t)p.CB, r1);
+            tc::tmem_ld8(ta + (uint32_t)(2 * p.CB), r2);
+            tc::tmem_wait_ld();
+            if (valid) {
+              // |D| < 2^22, so adding 1.5 * 2^23 to the bits gives the float
+              // 1.5 * 2^23 + D exactly (no conversion instruction); the scaled
+              // digit sums are then exact, and only their sum rounds.
 #pragma unroll
-            for (int e = 0; e < 16; e += 2) {
-              if (e >= nco) break;
-              const float4 sb = tb[e >> 1];
+              for (int e = 0; e < 8; e += 2) {
+                if (c8 + e >= nco) break;
+                const float4 sb = tb[(c8 + e) >> 1];
 #pragma unroll
-              for (int f = 0; f < 2; ++f) {
-                const float a0 = __int_as_float((int)r0[e + f] + 0x4B400000);
-                const float a1 = __int_as_float((int)r1[e + f] + 0x4B400000);
-                const float a2 = __int_as_float((int)r2[e + f] + 0x4B400000);
-                const float x0 = fmaf(a0, 65536.f, -12582912.f * 65536.f);
-                const float x1 = fmaf(a1, 256.f, -12582912.f * 256.f);
-                const float x2 = a2 - 12582912.f;
-                const float v = fmaf(f ? sb.z : sb.x, (x0 + x1) + x2, f ? sb.w : sb.y);
-                if (e + f < nco) yp[(uint32_t)(e + f) * (uint32_t)HW] = DT<XT>::from_f(v);
+                for (int f = 0; f < 2; ++f) {
+                  const float a0 = __int_as_float((int)r0[e + f] + 0x4B400000);
+                  const float a1 = __int_as_float((int)r1[e + f] + 0x4B400000);
+                  const float a2 = __int_as_float((int)r2[e + f] + 0x4B400000);
+                  const float x0 = fmaf(a0, 65536.f, -12582912.f * 65536.f);
+                  const float x1 = fmaf(a1, 256.f, -12582912.f * 256.f);
+                  const float x2 = a2 - 12582912.f;
+                  const float v = fmaf(f ? sb.z : sb.x, (x0 + x1) + x2, f ? sb.w : sb.y);
+                  if (c8 + e + f < nco) yp[(uint32_t)(c8 + e + f) * (uint32_t)HW] = DT<XT>::from_f(v);
+                }
               }
             }
           }
