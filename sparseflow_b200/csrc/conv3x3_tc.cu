@@ -249,6 +249,20 @@ __device__ __forceinline__ void convert_unit_vec4(const Params& p, const float* 
   }
 }
 
+#ifdef SF_C3TC_PROF
+// Development builds only: cycles each role spends in mbarrier waits.
+__device__ unsigned long long g_c3tc_prof[8];
+#define PROF_WAIT(slot, expr)                                             \
+  ([&]() {                                                                \
+    const long long t_ = clock64();                                       \
+    const bool ok_ = (expr);                                              \
+    if (lane == 0) atomicAdd(&g_c3tc_prof[slot], (unsigned long long)(clock64() - t_)); \
+    return ok_;                                                           \
+  }())
+#else
+#define PROF_WAIT(slot, expr) (expr)
+#endif
+
 template <typename XT, typename WT, bool VEC>
 __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p) {
   extern __shared__ __align__(128) unsigned char smem[];
@@ -292,6 +306,13 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
       const uint32_t idesc = tc::idesc_s8(kM, p.N3);
       const uint32_t bsa = smem_u32(bsm);
       const uint32_t lbo_b = (uint32_t)p.N3 * 16u;
+      // The MMAs of one tile walk tap (kh, kw) x pair of 16-channel slices.
+      // Descriptors advance by adding to their address fields (16-byte
+      // units; no offset here carries out of the 14-bit field): B by one
+      // slice pair per MMA, A by the tap's row shift plus one slice pair.
+      const int pk = p.kcores / 2;
+      const uint64_t astep = (uint64_t)(2u * p.a_plane) >> 4, bstep = (uint64_t)(2u * lbo_b) >> 4;
+      const uint64_t bbase = tc::desc_interleave(bsa, lbo_b, 128u);
       int cur_cob = -1, bloads = 0;
       long long g = 0;  // tiles issued by this CTA
       for (int i = 0; i < nu && !failed; ++i) {
@@ -320,7 +341,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
           cur_cob = cob;
         }
         const int a = i & 1;
-        if (!tc::mbar_wait_sleep(&bars->a_full[a], (uint32_t)((i >> 1) & 1))) {
+        if (!PROF_WAIT(0, tc::mbar_wait_sleep(&bars->a_full[a], (uint32_t)((i >> 1) & 1)))) {
           failed = true;
           break;
         }
@@ -328,22 +349,26 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
         const uint32_t asa = smem_u32(abuf + (size_t)a * p.a_bytes);
         for (int j = 0; j < nt; ++j, ++g) {
           const int d = (int)(g & 1);
-          if (g >= 2 && !tc::mbar_wait_sleep(&bars->d_empty[d], (uint32_t)(((g >> 1) - 1) & 1))) {
+          if (g >= 2 && !PROF_WAIT(1, tc::mbar_wait_sleep(&bars->d_empty[d], (uint32_t)(((g >> 1) - 1) & 1)))) {
             failed = true;
             break;
           }
           tc::fence_after();
           const uint32_t dt = tmem + (uint32_t)(d * p.N3);
+          const uint64_t abase = tc::desc_interleave(asa + (uint32_t)(j * kM) * 16u, p.a_plane, 128u);
+          uint64_t bd = bbase;
           uint32_t acc = 0u;
-          for (int tap = 0; tap < 9; ++tap) {
-            const int kh = tap / 3, kw = tap - kh * 3;
-            const uint32_t shift = (uint32_t)(j * kM + kh * p.Wp + kw) * 16u;
-            for (int ks = 0; ks < p.kcores; ks += 2) {
-              const uint64_t ad = tc::desc_interleave(asa + (uint32_t)ks * p.a_plane + shift, p.a_plane, 128u);
-              const uint64_t bd =
-                  tc::desc_interleave(bsa + (uint32_t)(tap * p.kcores + ks) * lbo_b, lbo_b, 128u);
+          for (int kh = 0; kh < 3; ++kh) {
+#pragma unroll
+            for (int kw = 0; kw < 3; ++kw) {
+              uint64_t ad = abase + (uint64_t)(kh * p.Wp + kw);
               tc::mma_s8(dt, ad, bd, idesc, acc);
               acc = 1u;
+              bd += bstep;
+              if (pk == 2) {
+                tc::mma_s8(dt, ad + astep, bd, idesc, 1u);
+                bd += bstep;
+              }
             }
           }
           tc::mma_commit(&bars->d_full[d]);
@@ -384,7 +409,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
       const int nco = min(cwq, p.Co - cbase);  // valid channels of this warp (may be <= 0)
       for (int j = 0; j < nt; ++j, ++g) {
         const int d = (int)(g & 1);
-        if (!tc::mbar_wait_sleep(&bars->d_full[d], (uint32_t)((g >> 1) & 1))) {
+        if (!PROF_WAIT(2, tc::mbar_wait_sleep(&bars->d_full[d], (uint32_t)((g >> 1) & 1)))) {
           failed = true;
           break;
         }
@@ -458,7 +483,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
       const int cob = (int)(u / p.upcob);
       const long long t0 = (u - (long long)cob * p.upcob) * p.U;
       const int a = i & 1;
-      if (i >= 2 && !tc::mbar_wait_sleep(&bars->a_empty[a], (uint32_t)(((i >> 1) - 1) & 1))) {
+      if (i >= 2 && !PROF_WAIT(3, tc::mbar_wait_sleep(&bars->a_empty[a], (uint32_t)(((i >> 1) - 1) & 1)))) {
         failed = true;
         break;
       }
@@ -592,6 +617,14 @@ sf_status dispatch_w(int wdt, const Params& p, size_t smem, cudaStream_t st) {
 }
 
 }  // namespace
+
+#ifdef SF_C3TC_PROF
+extern "C" int sf_dev_c3tc_prof(unsigned long long* out) {
+  cudaMemcpyFromSymbol(out, g_c3tc_prof, sizeof(g_c3tc_prof));
+  unsigned long long z[8] = {0};
+  return (int)cudaMemcpyToSymbol(g_c3tc_prof, z, sizeof(z));
+}
+#endif
 
 bool tc3_packs(int Co, int C, int K) { return K == 3 && C >= 1 && C <= kTcMaxC && Co >= 1; }
 
