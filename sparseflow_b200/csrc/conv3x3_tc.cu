@@ -86,7 +86,7 @@ struct Params {
   void* y;
   uint32_t* err;
   int N, C, H, W, Co, Wp, Hs;
-  FastDiv fd_wp, fd_hs;  // by Wp and by H + 1
+  FastDiv fd_wp, fd_hs, fd_upcob;  // by Wp, by H + 1, by units per output block
   int kcores, CB, N3, ncob;
   long long ntiles, upcob, nunits, units_per_cta;
   int U;
@@ -256,7 +256,7 @@ __device__ unsigned long long g_c3tc_prof[8];
   ([&]() {                                                                \
     const long long t_ = clock64();                                       \
     const bool ok_ = (expr);                                              \
-    if (lane == 0) atomicAdd(&g_c3tc_prof[slot], (unsigned long long)(clock64() - t_)); \
+    prof_w[(slot) & 1] += (unsigned long long)(clock64() - t_);           \
     return ok_;                                                           \
   }())
 #else
@@ -300,6 +300,9 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
   tc::fence_after();
   const uint32_t tmem = bars->tmem_base;
   bool failed = false;
+#ifdef SF_C3TC_PROF
+  unsigned long long prof_w[2] = {0ull, 0ull};
+#endif
 
   if (warp == kMmaWarp) {
     if (lane == 0) {
@@ -317,7 +320,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
       long long g = 0;  // tiles issued by this CTA
       for (int i = 0; i < nu && !failed; ++i) {
         const long long u = u0 + i;
-        const int cob = (int)(u / p.upcob);
+        const int cob = (int)fdiv((uint32_t)u, p.fd_upcob);
         const long long t0 = (u - (long long)cob * p.upcob) * p.U;
         const int nt = (int)min((long long)p.U, p.ntiles - t0);
         if (cob != cur_cob) {
@@ -358,6 +361,9 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
           const uint64_t abase = tc::desc_interleave(asa + (uint32_t)(j * kM) * 16u, p.a_plane, 128u);
           uint64_t bd = bbase;
           uint32_t acc = 0u;
+#ifdef SF_C3TC_PROF
+          const long long tm0 = clock64();
+#endif
           for (int kh = 0; kh < 3; ++kh) {
 #pragma unroll
             for (int kw = 0; kw < 3; ++kw) {
@@ -371,6 +377,9 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
               }
             }
           }
+#ifdef SF_C3TC_PROF
+          atomicAdd(&g_c3tc_prof[4], (unsigned long long)(clock64() - tm0));
+#endif
           tc::mma_commit(&bars->d_full[d]);
         }
         if (failed) break;
@@ -392,7 +401,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
     long long g = 0;
     for (int i = 0; i < nu && !failed; ++i) {
       const long long u = u0 + i;
-      const int cob = (int)(u / p.upcob);
+      const int cob = (int)fdiv((uint32_t)u, p.fd_upcob);
       const long long t0 = (u - (long long)cob * p.upcob) * p.U;
       const int nt = (int)min((long long)p.U, p.ntiles - t0);
       const int cbase = cob * p.CB + cbeg;
@@ -480,7 +489,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
   } else {
     for (int i = 0; i < nu && !failed; ++i) {
       const long long u = u0 + i;
-      const int cob = (int)(u / p.upcob);
+      const int cob = (int)fdiv((uint32_t)u, p.fd_upcob);
       const long long t0 = (u - (long long)cob * p.upcob) * p.U;
       const int a = i & 1;
       if (i >= 2 && !PROF_WAIT(3, tc::mbar_wait_sleep(&bars->a_empty[a], (uint32_t)(((i >> 1) - 1) & 1)))) {
@@ -501,6 +510,18 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
     }
     if (failed && lane == 0) atomicExch(p.err, 1u);
   }
+#ifdef SF_C3TC_PROF
+  if (lane == 0) {
+    if (warp == kMmaWarp) {
+      atomicAdd(&g_c3tc_prof[0], prof_w[0]);
+      atomicAdd(&g_c3tc_prof[1], prof_w[1]);
+    } else if (warp >= kConvWarps) {
+      atomicAdd(&g_c3tc_prof[2], prof_w[0]);
+    } else {
+      atomicAdd(&g_c3tc_prof[3], prof_w[1]);
+    }
+  }
+#endif
   tc::fence_before();
   __syncthreads();
   if (warp == kMmaWarp) {
@@ -679,27 +700,35 @@ sf_status run_conv3x3_tc(const void* x, const void* w_gather, int cpl, const voi
   const size_t limit = 227 * 1024;
   size_t smem = 0;
   int U = 0;
-  for (int u = 4; u >= 1; --u) {
-    const uint32_t rows = (uint32_t)((u * kM + 2 * p.Wp + 2 + 31) / 32 * 32);
-    const size_t a_bytes = (size_t)rows * 16 * g.kcores;
-    const size_t a_off = (g.b_bytes + 127) / 128 * 128;
-    const size_t bar_off = a_off + 2 * a_bytes;
-    const size_t total = bar_off + sizeof(Bars);
-    if (total <= limit) {
-      U = u;
-      p.rows_a = rows;
-      p.a_plane = rows * 16;
-      p.a_bytes = (uint32_t)a_bytes;
-      p.a_off = (uint32_t)a_off;
-      p.bar_off = (uint32_t)bar_off;
-      smem = total;
-      break;
+  // Units of up to 6 tiles (the halo rows a unit converts twice shrink with
+  // U) within 200 KB of shared memory: past that the L1 left beside it is too
+  // small and the x stream slows (U = 6 at 226 KB measured 24 % slower on the
+  // C64 56x56 cell than U = 4 at 191 KB). The full 227 KB only when nothing
+  // smaller fits.
+  for (size_t budget : {(size_t)200 * 1024, limit}) {
+    for (int u = 6; u >= 1 && U == 0; --u) {
+      const uint32_t rows = (uint32_t)((u * kM + 2 * p.Wp + 2 + 31) / 32 * 32);
+      const size_t a_bytes = (size_t)rows * 16 * g.kcores;
+      const size_t a_off = (g.b_bytes + 127) / 128 * 128;
+      const size_t bar_off = a_off + 2 * a_bytes;
+      const size_t total = bar_off + sizeof(Bars);
+      if (total <= budget) {
+        U = u;
+        p.rows_a = rows;
+        p.a_plane = rows * 16;
+        p.a_bytes = (uint32_t)a_bytes;
+        p.a_off = (uint32_t)a_off;
+        p.bar_off = (uint32_t)bar_off;
+        smem = total;
+      }
     }
+    if (U) break;
   }
   if (U == 0) return SF_ERR_UNSUPPORTED;
   smem = std::max<size_t>(smem, 120 * 1024);  // one CTA (and one TMEM allocation) per SM
   p.U = U;
   p.upcob = (p.ntiles + U - 1) / U;
+  p.fd_upcob = make_fastdiv((uint32_t)p.upcob);
   p.nunits = p.upcob * p.ncob;
   uint32_t cols = 32;
   while (cols < (uint32_t)(2 * p.N3)) cols <<= 1;
