@@ -21,7 +21,7 @@ import torch
 import torch.nn.functional as F
 
 from .. import _lib
-from ..Utils.config import PRESCAN_ACTIVITY_EPS, SPARSE_DENSE_RATIO_THRESHOLD, TC_MIN_PIXELS
+from ..Utils.config import PRESCAN_ACTIVITY_EPS, SPARSE_DENSE_RATIO_THRESHOLD, TC3X3_MAX_CIN
 from ..Utils.sparse_helpers import (TILE_DENSEISH, TILE_SPARSE, TILE_ZERO, choose_group_size, popcount_buf,
                                     select_tile_sizes)
 from ._prescan_common import prescan2d
@@ -58,6 +58,26 @@ def pack_weight(weight: torch.Tensor) -> torch.Tensor:
     exactly to fp32), bf16 stays bf16."""
     out_dtype = torch.bfloat16 if weight.dtype == torch.bfloat16 else torch.float32
     return _lib.pack_weights(weight, out_dtype)
+
+
+def uses_event_masks(c_in: int, h_in: int, w_in: int, kernel_size: int, stride: int, padding: int) -> bool:
+    """Whether a convolution handed its input's event masks runs from them.
+
+    1x1/s2 has no mask-driven kernel. The tensor-core kernels read the spikes
+    themselves faster than the gather kernel reads masks: 1x1/s1 on images of
+    at least one 128-pixel MMA tile, and 3x3/s1 with C_in <= 64 (measured on
+    the C64 56x56 cell: 0.38 ms from the spikes against 0.46 ms for the
+    gather kernel from masks; 0.027 against 0.06 ms on 8x8 maps)."""
+    if (kernel_size, stride) == (1, 2):
+        return False
+    lib = _lib.load()
+    if kernel_size == 1 and stride == 1 and lib.sf_get_path_policy(_lib.SF_POLICY_CONV1X1_PATH) == 0 and \
+            h_in * w_in >= lib.sf_get_path_policy(_lib.SF_POLICY_CONV1X1_TC_MIN_HW):
+        return False
+    if (kernel_size, stride, padding) == (3, 1, 1) and c_in <= TC3X3_MAX_CIN and \
+            lib.sf_get_path_policy(_lib.SF_POLICY_CONV3X3_PATH) != 1:
+        return False
+    return True
 
 
 def sparse_conv2d_forward(
@@ -168,10 +188,7 @@ def sparse_conv2d_forward(
     if return_ms:
         se, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         se.record()
-    # 1x1/s2 has no mask-driven kernel; a 1x1/s1 layer on images of at least one 128-pixel MMA tile
-    # runs faster on the tensor-core kernel from x itself than from the masks.
-    used_masks = (event_masks is not None and (kernel_size, stride) != (1, 2)
-                  and not (kernel_size == 1 and stride == 1 and h_in * w_in >= TC_MIN_PIXELS))
+    used_masks = event_masks is not None and uses_event_masks(c_in, h_in, w_in, kernel_size, stride, padding)
     if used_masks:
         _lib.sparse_conv2d_from_masks(event_masks, tuple(x.shape), x.dtype, w_packed, b, y, kernel_size, stride,
                                       padding)

@@ -23,10 +23,9 @@ DISPATCH_R_MARGIN = 0.0
 DISPATCH_TAU_MARGIN = 0.0
 DISPATCH_MIN_CONFIDENCE = 0.60
 
-# Images of at least this many pixels run 1x1/s1 convolutions on the tcgen05 kernel (the library's
-# SF_CONV_TC_MIN_HW default); below it, and for masks handed over by a spike producer, the gather
-# kernels run.
-TC_MIN_PIXELS = 128
+# 3x3/s1 convolutions with at most this many input channels run on the tcgen05 implicit-GEMM kernel
+# (its weight digits stay in shared memory; the library's limit for that kernel).
+TC3X3_MAX_CIN = 64
 
 # optimize(): the LIF nodes whose spikes feed a replaced convolution write those spikes' event masks
 # (LIFNode.emit_event_masks), so the convolution skips its mask pass. Results are identical either

@@ -38,12 +38,15 @@ def optimize(model, sample_input=None, block_sizes=None, verbose=True, threshold
 
 
 def _enable_event_masks(model, targets):
-    """Spike sources (this package's LIFNode) of replaced convolutions emit the next layer's event masks.
+    """Spike sources (this package's LIFNode) of replaced convolutions emit the next layer's event masks,
+    where that convolution runs from masks (uses_event_masks: not where a tensor-core kernel reads the
+    spikes faster).
 
     Other spike sources (a spikingjelly neuron, say) have no such switch and are left alone; a source
     whose output is modified before the convolution sees it loses nothing, the masks are then unused.
     """
     import os
+    from .Kernels.conv2d import uses_event_masks
     from .Ops.sparse_conv2d import SparseConv2d
     from .Utils.config import EMIT_EVENT_MASKS
     if not EMIT_EVENT_MASKS or os.environ.get("SF_EMIT_EVENT_MASKS", "1") == "0":
@@ -54,7 +57,9 @@ def _enable_event_masks(model, targets):
             src = model.get_submodule(t.spike_name) if t.spike_name else None
         except AttributeError:
             continue
-        if isinstance(conv, SparseConv2d) and src is not None and hasattr(src, "emit_event_masks"):
+        if isinstance(conv, SparseConv2d) and src is not None and hasattr(src, "emit_event_masks") and \
+                uses_event_masks(conv.in_channels, t.input_h, t.input_w, conv.kernel_size[0], conv.stride[0],
+                                 conv.padding[0]):
             src.emit_event_masks = True
 
 

@@ -51,13 +51,19 @@ def test_next_conv_runs_from_masks(c_mid, k2, hw):
     conv2.weight.data = torch.randn(48, c_mid, k2, k2, generator=g) * 0.1
     second = SparseConv2d.from_dense(conv2.cuda())
     s = first(x)
-    y_masks = second(s)
-    assert second._last_used_event_masks
-    y_plain = second(s.clone())  # a new tensor: no masks attached, mask pass runs
-    assert not second._last_used_event_masks
-    # Both runs use the same gather kernel (1x1 on images below one 128-pixel MMA tile
-    # too): bit-identical.
+    # The gather kernel on both runs (3x3 with C_in <= 64 would otherwise take the tensor-core
+    # kernel from the spikes, and 1x1 on images below one 128-pixel MMA tile is gathered anyway).
+    from sparseflow_b200 import _lib
+    with _lib.path_policy(_lib.SF_POLICY_CONV3X3_PATH, 1):
+        y_masks = second(s)
+        assert second._last_used_event_masks
+        y_plain = second(s.clone())  # a new tensor: no masks attached, mask pass runs
+        assert not second._last_used_event_masks
     torch.testing.assert_close(y_masks, y_plain, rtol=0, atol=0)
+    if k2 == 3 and c_mid <= 64:
+        y_tc = second(s)  # default policy: the tensor-core kernel reads the spikes, masks unused
+        assert not second._last_used_event_masks
+        torch.testing.assert_close(y_tc, y_plain, rtol=1e-5, atol=1e-5)
 
 
 def test_1x1_on_large_images_ignores_masks():
@@ -142,10 +148,12 @@ def test_lif_events_drive_next_conv():
     conv.weight.data = torch.randn(48, 64, 3, 3, generator=torch.Generator().manual_seed(1)) * 0.1
     sc = SparseConv2d.from_dense(conv.cuda())
     s = ev(x)
-    y_masks = sc(s)
-    assert sc._last_used_event_masks
-    y_plain = sc(s.clone())
-    assert not sc._last_used_event_masks
+    from sparseflow_b200 import _lib
+    with _lib.path_policy(_lib.SF_POLICY_CONV3X3_PATH, 1):  # gather kernel, from masks or spikes
+        y_masks = sc(s)
+        assert sc._last_used_event_masks
+        y_plain = sc(s.clone())
+        assert not sc._last_used_event_masks
     torch.testing.assert_close(y_masks, y_plain, rtol=0, atol=0)
 
 
