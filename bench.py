@@ -101,57 +101,51 @@ def make_conv(c, co, k, s, p, bias, seed, wdtype=torch.float32, device="cuda"):
 
 
 class ClockSampler:
-    """nvidia-smi sampling of SM clock and throttle reasons while the GPU is busy."""
+    """SM clock and throttle reasons sampled through NVML every 5 ms while the GPU works
+    (reading only; nothing is set)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4}
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
-        self.proc = None
-        self.lines = []
+        self.samples = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self.thread = None
 
     def start(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
-                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
-        except (FileNotFoundError, OSError):
-            self.proc = None
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+        except Exception:  # noqa: BLE001 -- no NVML: the line reports clocks as null
+            return
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+        def run():
+            while not self._stop.is_set():
+                try:
+                    mhz = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                    reasons = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    util = pynvml.nvmlDeviceGetUtilizationRates(h).gpu
+                    self.samples.append((float(mhz), int(reasons), int(util)))
+                except Exception:  # noqa: BLE001
+                    pass
+                time.sleep(0.005)
+        self.thread = threading.Thread(target=run, daemon=True)
+        self.thread.start()
 
     def stop(self):
-        if self.proc is None:
+        if self.thread is None:
             return None
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
+        self._stop.set()
         self.thread.join(timeout=2)
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
-            except ValueError:
-                continue
-            for nm, v in zip(names, parts[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(nm)
-        if not sm:
+        if not self.samples:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        busy = [smp for smp in self.samples if smp[2] > 0] or self.samples
+        reasons = sorted(nm for nm, bit in self.REASONS.items() if any(smp[1] & bit for smp in busy))
+        return {"sm_mhz": statistics.median(smp[0] for smp in busy), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(busy), "source": "NVML, 5 ms"}
 
 
 def cuda_time(fn, steps, warmup, dist=None):
@@ -177,53 +171,56 @@ def cuda_time(fn, steps, warmup, dist=None):
     return ms
 
 
-def cpu_baseline(conv_cpu, x_sample, bytes_sample):
+def time_reference_cpu(steps, warmup, n_img=T_STEPS * N_BATCH):
+    """The reference's own CPU path for this layer (SparseConv2d on a CPU tensor = F.conv2d,
+    Ops/sparse_conv2d.py:819-834) on the headline workload (same shapes, density, weight init),
+    all host threads. Returns (GB/s, threads, seconds per step, steps)."""
     from oracle import oracle
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    with torch.no_grad():
-        oracle.reference_cpu_conv2d(x_sample, conv_cpu.weight, conv_cpu.bias, 1, 1)  # warm-up
-        times = []
-        t_end = time.perf_counter() + 15.0
-        while len(times) < 3 or (time.perf_counter() < t_end and len(times) < 10):
-            t0 = time.perf_counter()
-            oracle.reference_cpu_conv2d(x_sample, conv_cpu.weight, conv_cpu.bias, 1, 1)
-            times.append(time.perf_counter() - t0)
-    sec = statistics.median(times)
-    return bytes_sample / sec / 1e9, threads, sec
-
-
-def run_reference(args):
-    """The reference's own CPU implementation of the path (F.conv2d, Ops/sparse_conv2d.py:819-834)."""
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
-        return
     g = torch.Generator().manual_seed(0)
     conv = make_conv(C, C, 3, 1, 1, True, 1, device="cpu")
-    n_img = 16  # 16 of the 1024 (T*N) images per step
     x = (torch.rand(n_img, C, H, W, generator=g) < DENSITY).float()
     nbytes = conv_bytes(n_img, C, H, W, C, H, W, 3)
-    from oracle import oracle
-    torch.set_num_threads(os.cpu_count() or 1)
     with torch.no_grad():
-        for _ in range(max(1, min(args.warmup, 3))):
+        for _ in range(max(1, warmup)):
             oracle.reference_cpu_conv2d(x, conv.weight, conv.bias, 1, 1)
         t0 = time.perf_counter()
-        steps = max(1, min(args.steps, 20))
         for _ in range(steps):
             oracle.reference_cpu_conv2d(x, conv.weight, conv.bias, 1, 1)
         sec = (time.perf_counter() - t0) / steps
-    val = nbytes / sec / 1e9
-    sample = f"{n_img} of {T_STEPS * N_BATCH} images (T*N) per step, same shapes/density/weights init"
-    print(json.dumps({
-        "impl": "reference", "metric": METRIC, "value": round(val, 3), "unit": "GB/s", "n_gpus": args.gpus,
-        "steps": steps, "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "C5 cell conv3x3 C64 56x56 T16 N64 p0.01 (CPU sample)", "sample": sample},
-        "cpu_baseline": {"value": round(val, 3), "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
-                         "sample": sample + "; torch F.conv2d = the reference SparseConv2d CPU path"},
-        "e2e": {"value": round(val, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }))
+    return nbytes / sec / 1e9, threads, sec, steps
+
+
+def run_reference(args):
+    """--impl reference: rank 0 times the reference's CPU path on the full per-GPU workload; under
+    torchrun the other ranks wait at a gloo barrier (idle, not competing for the host cores) and exit."""
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    pg = None
+    if world > 1:
+        import torch.distributed as tdist
+        tdist.init_process_group("gloo")
+        pg = tdist
+        pg.barrier()  # every rank has started (imports done) before rank 0 times
+    if rank == 0:
+        steps = max(1, min(args.steps, 20))
+        val, cores, sec, steps = time_reference_cpu(steps, min(args.warmup, 3))
+        sample = (f"the full step: {T_STEPS * N_BATCH} images (T*N) of C64 56x56, same shapes/density/weight init; "
+                  "torch F.conv2d = the reference SparseConv2d CPU path (Ops/sparse_conv2d.py:819-834)")
+        print(json.dumps({
+            "impl": "reference", "metric": METRIC, "value": round(val, 3), "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": steps, "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "C5 cell: SparseConv2d 3x3/s1/p1 C64->64, T16 N64 56x56, Bernoulli(0.01) fp32 "
+                                   "spikes, block 16 (per GPU)", "sample": sample,
+                       "note": "one host CPU for all N: the reference's CPU path does not shard across GPUs"},
+            "cpu_baseline": {"value": round(val, 3), "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": round(val, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }), flush=True)
+    if pg is not None:
+        pg.barrier()
+        pg.destroy_process_group()
 
 
 def extras(dev, hbm_peak, steps):
@@ -397,6 +394,28 @@ def c4_resnet(dev, iters=3):
             "note": "same random-init model and input; every LIF node is one launch of the multi-step LIF kernel (with event masks where it feeds a replaced convolution)"}
 
 
+def c4_sharded(dev, dist, world, iters=5):
+    """C4 N-sharded: every rank runs Spiking-ResNet50 (after optimize()) on its own 128 images,
+    T16 3x32x32 N(0,1); img/s = 128 * world / (max over ranks of the device time per forward)."""
+    import sparseflow_b200
+    from sparseflow_b200.snn import spiking_resnet50
+    from sparseflow_b200.Ops.lif_node import reset_net
+    torch.manual_seed(5)
+    model = spiking_resnet50().to(dev).eval()
+    rank = dist.get_rank() if dist is not None else 0
+    img = torch.randn(128, 3, 32, 32, generator=torch.Generator().manual_seed(6 + rank)).to(dev)
+    x = img.unsqueeze(0).repeat(16, 1, 1, 1, 1)
+    sparseflow_b200.optimize(model, sample_input=x[:, :2], verbose=False)
+
+    def fwd():
+        reset_net(model)
+        return model(x)
+    with torch.no_grad():
+        ms = cuda_time(fwd, iters, 2, dist) / iters
+    return {"img_per_s": round(128 * world / (ms / 1e3), 1), "ms_per_forward_max_over_ranks": round(ms, 3),
+            "images_per_rank": 128, "ranks": world, "scaling": "weak", "eager": True}
+
+
 def run_sweep(args):
     """C5: conv3x3/s1/p1 C->C over C in {64,128,256,512}, H=W in {14,28,56}, density in
     {0.001,0.01,0.05,0.2}; block size per the H->block rule (inert in the kernels). Bytes = x + y + w + b."""
@@ -563,7 +582,7 @@ def main():
 
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
     phys = int(vis.split(",")[local]) if vis and vis.split(",")[local].strip().isdigit() else local
-    sampler = ClockSampler(phys)
+    sampler = ClockSampler(phys)  # NVML index (CUDA_VISIBLE_DEVICES maps local ranks to physical GPUs)
     sampler.start()
     with torch.no_grad():
         ms_total = cuda_time(lambda: mod(x), args.steps, args.warmup, dist)
@@ -643,7 +662,13 @@ def main():
         # The downloaded output is the module's output (spot check of one chunk).
         assert torch.equal(y_host[:8].to(dev), mod(x_dev[:8]))
     e2e_val = world * step_bytes / (e2e_ms / 1e3) / 1e9
+    # The host-side ceiling of that figure: every rank copying its 822 MB of pinned spikes to its
+    # GPU at once (all ranks' copies share the host's memory and PCIe), max over ranks.
+    with torch.no_grad():
+        h2d_ms = cuda_time(lambda: x_dev.copy_(x_host, non_blocking=True), 3, 1, dist) / 3
+    h2d_agg = world * x_host.numel() * 4 / (h2d_ms / 1e3) / 1e9
     del x_host, y_host, x_dev
+    c4 = c4_sharded(dev, dist, world)
 
     extra = None
     if not args.no_extra and rank == 0:
@@ -652,12 +677,11 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1:
-        conv_cpu = make_conv(C, C, 3, 1, 1, True, 1, device="cpu")
-        xs = x.reshape(n_img, C, H, W)[:16].cpu()
-        val, cores, sec = cpu_baseline(conv_cpu, xs, conv_bytes(16, C, H, W, C, H, W, 3))
+        val, cores, sec, nsteps = time_reference_cpu(3, 1)
         cpu = {"value": round(val, 3), "unit": "GB/s", "cores": cores, "kind": "port",
-               "sample": f"16 of {n_img} images per call ({sec * 1e3:.1f} ms median); torch F.conv2d on CPU = "
-                         "the reference SparseConv2d CPU path (Ops/sparse_conv2d.py:819-834)"}
+               "sample": f"the full step ({T_STEPS * N_BATCH} images), {nsteps} calls, {sec * 1e3:.0f} ms each; "
+                         "torch F.conv2d on CPU = the reference SparseConv2d CPU path (Ops/sparse_conv2d.py:819-834); "
+                         "the same helper as --impl reference"}
 
     traffic = None
     tf = ROOT / "profiles" / "sparse_conv_c5.traffic.json"
@@ -675,22 +699,25 @@ def main():
                        "l2": "inputs (822 MB) and outputs larger than L2; no flush"},
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": x.numel() * 4,
                     "d2h_bytes_per_step": x.numel() * 4, "ms_per_step": round(e2e_ms, 3),
-                    "pipeline": f"{E2E_CHUNKS} chunks on upload / compute / download streams"},
+                    "pipeline": f"{E2E_CHUNKS} chunks on upload / compute / download streams",
+                    "h2d_copy_GBps_all_ranks": round(h2d_agg, 1),
+                    "h2d_copy_GBps_per_rank": round(h2d_agg / world, 1)},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                          else "fallback 6650 GB/s",
-                         "kernel": "one sf_sparse_conv2d call = spike_masks_kernel<float,4> + "
-                                   "sparse_conv_kernel<3,1,2,8,1,float,float,false,true>",
+                         "kernel": "one sf_sparse_conv2d call = conv3x3_tc_kernel<float,float,true> "
+                                   "(tcgen05 kind::i8 implicit GEMM, x read once, y written once)",
                          "algorithmic_bytes_per_launch": step_bytes,
                          "bytes_model": "x read once + y written once + weights + bias"},
             "speedup_vs_cudnn": {"cudnn_default_ms": round(cud_ms, 4), "cudnn_fp32_no_tf32_ms": round(cud32_ms, 4),
                                  "ours_ms": round(ms_step, 4), "vs_default": round(cud_ms / ms_step, 2),
                                  "vs_fp32": round(cud32_ms / ms_step, 2)},
-            "gpu_launches": 2 * args.steps,  # spike_masks_kernel + sparse_conv_kernel per step (+1 memset)
+            "gpu_launches": args.steps,  # one conv3x3_tc_kernel launch per step
             "clocks": clocks,
             "cpu_baseline": cpu,
             "extra": extra,
+            "c4_spiking_resnet50_sharded": c4,
         }
         print(json.dumps(line))
     if dist is not None:
