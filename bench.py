@@ -684,7 +684,7 @@ def main():
                          "the same helper as --impl reference"}
 
     traffic = None
-    tf = ROOT / "profiles" / "sparse_conv_c5.traffic.json"
+    tf = ROOT / "profiles" / "conv3x3_tc_c5.traffic.json"
     if tf.exists():
         traffic = json.loads(tf.read_text()).get("dram_bytes_per_launch")
 
