@@ -53,10 +53,13 @@ namespace {
 
 using conv::mbar_arrive;
 
-constexpr int kConvWarps = 15;
+// Warp roles (1024 threads): converters 0..14 (0..13 when the weights are
+// streamed, warp 14 then copies weight stages), epilogue 15..30, MMA 31.
+constexpr int kEpi0 = 15;
 constexpr int kEpiWarps = 16;
-constexpr int kMmaWarp = kConvWarps + kEpiWarps;
+constexpr int kMmaWarp = kEpi0 + kEpiWarps;
 constexpr int kThreads = (kMmaWarp + 1) * 32;
+constexpr int kMaxBStages = 4;
 constexpr int kM = 128;
 constexpr int kTags = 4;
 
@@ -91,10 +94,15 @@ struct Params {
   long long ntiles, upcob, nunits, units_per_cta;
   int U;
   uint32_t rows_a, a_plane, a_bytes, b_bytes, a_off, bar_off, tmem_cols;
+  // Streamed weights (C_in > 64): nA A buffers, nbs weight stages of kch
+  // 16-channel slices of one tap of one 32-channel output block.
+  int nA, nbs, kch;
+  uint32_t b_off, bstage_bytes;
 };
 
 struct Bars {
   uint64_t a_full[2], a_empty[2], d_full[2], d_empty[2], b_full, b_free;
+  uint64_t s_full[kMaxBStages], s_empty[kMaxBStages];
   uint32_t tmem_base;
   uint32_t tag[kTags];  // = u + 1 when unit u holds a value other than 0 / 1
   alignas(16) float2 tab[kEpiWarps][16];
@@ -132,11 +140,11 @@ __device__ __forceinline__ float gather_w(const Params& p, int co, int ci, int t
 // (group of 32 A rows, 16-channel slice), lane = A row.
 template <typename XT>
 __device__ __forceinline__ void convert_unit_scalar(const Params& p, const XT* __restrict__ x, unsigned char* ab,
-                                                    long long q0, int warp, int lane, uint32_t& nb) {
+                                                    long long q0, int warp, int lane, int nconv, uint32_t& nb) {
   const size_t HW = (size_t)p.H * p.W;
   const int kc_n = p.kcores;
   const int items = (int)(p.rows_a / 32) * kc_n;
-  for (int it = warp; it < items; it += kConvWarps) {
+  for (int it = warp; it < items; it += nconv) {
     const int grp = it / kc_n, kc = it - grp * kc_n;
     const uint32_t q = (uint32_t)q0 + grp * 32 + lane;
     const uint32_t R = fdiv(q, p.fd_wp);
@@ -175,7 +183,7 @@ __device__ __forceinline__ void convert_unit_scalar(const Params& p, const XT* _
 // counts as 0, NaN fails) and writes the 8-byte halves of four A rows. The
 // two padding columns of each row are written as zeros by a separate loop.
 __device__ __forceinline__ void convert_unit_vec4(const Params& p, const float* __restrict__ x, unsigned char* ab,
-                                                  long long q0, int warp, int lane, uint32_t& nb) {
+                                                  long long q0, int warp, int lane, int nconv, uint32_t& nb) {
   const uint32_t HW = (uint32_t)(p.H * p.W);
   const int kh_n = p.kcores * 2;  // 8-channel halves
   const uint32_t R0 = fdiv((uint32_t)q0, p.fd_wp);
@@ -186,7 +194,7 @@ __device__ __forceinline__ void convert_unit_vec4(const Params& p, const float* 
   const int ngrp = (ntask + 31) >> 5;
   const int items = ngrp * kh_n;
   const int rows_a = (int)p.rows_a;
-  for (int it = warp; it < items; it += kConvWarps) {
+  for (int it = warp; it < items; it += nconv) {
     const int grp = it / kh_n, kh = it - grp * kh_n;
     const int t = grp * 32 + lane;
     const int rr = t / qw, k4 = t - rr * qw;
@@ -246,7 +254,7 @@ __device__ __forceinline__ void convert_unit_vec4(const Params& p, const float* 
   // Padding columns 0 and W + 1 of every padded row the unit touches.
   const int kc_n = p.kcores;
   const int npad = nrows * 2 * kc_n;
-  for (int t = warp * 32 + lane; t < npad; t += kConvWarps * 32) {
+  for (int t = warp * 32 + lane; t < npad; t += nconv * 32) {
     const int rr = t / (2 * kc_n), rem = t - rr * 2 * kc_n;
     const int side = rem / kc_n, kc = rem - side * kc_n;
     const int r = (int)((R0 + rr) * p.Wp + (side ? p.W + 1 : 0) - (uint32_t)q0);
@@ -255,24 +263,82 @@ __device__ __forceinline__ void convert_unit_vec4(const Params& p, const float* 
   }
 }
 
-#ifdef SF_C3TC_PROF
-// Development builds only: cycles each role spends in mbarrier waits.
-__device__ unsigned long long g_c3tc_prof[8];
-#define PROF_WAIT(slot, expr)                                             \
-  ([&]() {                                                                \
-    const long long t_ = clock64();                                       \
-    const bool ok_ = (expr);                                              \
-    prof_w[(slot) & 1] += (unsigned long long)(clock64() - t_);           \
-    return ok_;                                                           \
-  }())
-#else
-#define PROF_WAIT(slot, expr) (expr)
-#endif
+// One tile's epilogue for the warp's channels [cbeg, cbeg + cwq) of output
+// block cob: D (three digit planes at TMEM column dcol) -> y, or, for a unit
+// holding values other than 0 / 1, fp32 FMAs from x and the weights.
+template <typename XT, typename WT>
+__device__ __forceinline__ void epilogue_tile(const Params& p, const XT* __restrict__ x, uint32_t tmem, uint32_t dcol,
+                                              long long tile, int cob, int qd, int lane, int cbeg, int cwq, int nco,
+                                              const float2* tab, bool odd) {
+  const size_t HW = (size_t)p.H * p.W;
+  const uint32_t o = (uint32_t)(tile * kM) + qd * 32 + lane;
+  const uint32_t Ro = fdiv(o, p.fd_wp);
+  const int c = (int)(o - Ro * p.Wp);
+  const uint32_t img = fdiv(Ro, p.fd_hs);
+  const int h = (int)(Ro - img * p.Hs);
+  const bool valid = c < p.W && h < p.H && img < (uint32_t)p.N;
+  const int cbase = cob * p.CB + cbeg;
+  XT* yp = static_cast<XT*>(p.y) + ((size_t)img * p.Co + cbase) * HW + (size_t)h * p.W + c;
+  if (!odd) {
+    const float4* tb = reinterpret_cast<const float4*>(tab);
+    for (int c8 = 0; c8 < cwq; c8 += 8) {
+      uint32_t r0[8], r1[8], r2[8];
+      const uint32_t ta = tmem + ((uint32_t)(qd * 32) << 16) + dcol + (uint32_t)(cbeg + c8);
+      tc::tmem_ld8(ta, r0);
+      tc::tmem_ld8(ta + (uint32_t)p.CB, r1);
+      tc::tmem_ld8(ta + (uint32_t)(2 * p.CB), r2);
+      tc::tmem_wait_ld();
+      if (valid) {
+        // |D| < 2^22, so adding 1.5 * 2^23 to the bits gives the float
+        // 1.5 * 2^23 + D exactly (no conversion instruction); the scaled
+        // digit sums are then exact, and only their sum rounds.
+#pragma unroll
+        for (int e = 0; e < 8; e += 2) {
+          if (c8 + e >= nco) break;
+          const float4 sb = tb[(c8 + e) >> 1];
+#pragma unroll
+          for (int f = 0; f < 2; ++f) {
+            const float a0 = __int_as_float((int)r0[e + f] + 0x4B400000);
+            const float a1 = __int_as_float((int)r1[e + f] + 0x4B400000);
+            const float a2 = __int_as_float((int)r2[e + f] + 0x4B400000);
+            const float x0 = fmaf(a0, 65536.f, -12582912.f * 65536.f);
+            const float x1 = fmaf(a1, 256.f, -12582912.f * 256.f);
+            const float x2 = a2 - 12582912.f;
+            const float v = fmaf(f ? sb.z : sb.x, (x0 + x1) + x2, f ? sb.w : sb.y);
+            // Evict-first stores: y is not read again here (1.7 % faster on the C5 cell).
+            if (c8 + e + f < nco) st_cs(yp + (uint32_t)(c8 + e + f) * (uint32_t)HW, DT<XT>::from_f(v));
+          }
+        }
+      }
+    }
+  } else if (valid) {
+    const XT* ximg = x + (size_t)img * p.C * HW;
+    for (int cc = 0; cc < nco; ++cc) {
+      const int co = cbase + cc;
+      float acc = 0.f;
+      for (int ci = 0; ci < p.C; ++ci) {
+        for (int tap = 0; tap < 9; ++tap) {
+          const int ih = h + tap / 3 - 1, iw = c + tap % 3 - 1;
+          if (ih < 0 || ih >= p.H || iw < 0 || iw >= p.W) continue;
+          const float xv = DT<XT>::to_f(ximg[(size_t)ci * HW + (size_t)ih * p.W + iw]);
+          if (xv != 0.f) acc = fmaf(xv, gather_w<WT>(p, co, ci, tap), acc);
+        }
+      }
+      yp[(size_t)cc * HW] = DT<XT>::from_f(acc + (p.bias ? __ldg(p.bias + co) : 0.f));
+    }
+  }
+}
 
-template <typename XT, typename WT, bool VEC>
+// STREAM = false: the weight digits of one output block stay in shared
+// memory (C_in <= 64); D per tile, double buffered. STREAM = true: weight
+// stages stream past the resident A of a unit once per output block; D per
+// (unit, block) group of U tiles, double buffered.
+template <typename XT, typename WT, bool VEC, bool STREAM>
 __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p) {
+  constexpr int kConv = STREAM ? kEpi0 - 1 : kEpi0;  // converter warps
+  constexpr int kProducer = kEpi0 - 1;              // weight-stage copier (STREAM)
   extern __shared__ __align__(128) unsigned char smem[];
-  unsigned char* bsm = smem;
+  unsigned char* bsm = smem + p.b_off;
   unsigned char* abuf = smem + p.a_off;
   Bars* bars = reinterpret_cast<Bars*>(smem + p.bar_off);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -280,14 +346,24 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
   const long long u1 = min(p.nunits, u0 + p.units_per_cta);
   const int nu = (int)max(0ll, u1 - u0);
   const XT* __restrict__ x = static_cast<const XT*>(p.x);
-  const size_t HW = (size_t)p.H * p.W;
+  // Unit u: tiles [t0, t0 + nt) of output block cob (resident weights), or of
+  // every block in turn (streamed weights: then cob of the unit is 0).
+  auto unit_of = [&](long long u, int& cob, long long& t0, int& nt) {
+    cob = STREAM ? 0 : (int)fdiv((uint32_t)u, p.fd_upcob);
+    t0 = (u - (long long)cob * p.upcob) * p.U;
+    nt = (int)min((long long)p.U, p.ntiles - t0);
+  };
 
   if (tid == 0) {
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&bars->a_full[i], kConvWarps);
+      mbar_init(&bars->a_full[i], kConv);
       mbar_init(&bars->a_empty[i], 1);
       mbar_init(&bars->d_full[i], 1);
       mbar_init(&bars->d_empty[i], kEpiWarps);
+    }
+    for (int i = 0; i < kMaxBStages; ++i) {
+      mbar_init(&bars->s_full[i], 1);
+      mbar_init(&bars->s_empty[i], 1);
     }
     mbar_init(&bars->b_full, 1);
     mbar_init(&bars->b_free, 1);
@@ -306,209 +382,246 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
   tc::fence_after();
   const uint32_t tmem = bars->tmem_base;
   bool failed = false;
-#ifdef SF_C3TC_PROF
-  unsigned long long prof_w[2] = {0ull, 0ull};
-#endif
 
   if (warp == kMmaWarp) {
     if (lane == 0) {
       const uint32_t idesc = tc::idesc_s8(kM, p.N3);
       const uint32_t bsa = smem_u32(bsm);
       const uint32_t lbo_b = (uint32_t)p.N3 * 16u;
-      // The MMAs of one tile walk tap (kh, kw) x pair of 16-channel slices.
       // Descriptors advance by adding to their address fields (16-byte
-      // units; no offset here carries out of the 14-bit field): B by one
-      // slice pair per MMA, A by the tap's row shift plus one slice pair.
-      const int pk = p.kcores / 2;
+      // units; no offset here carries out of the 14-bit field).
       const uint64_t astep = (uint64_t)(2u * p.a_plane) >> 4, bstep = (uint64_t)(2u * lbo_b) >> 4;
-      const uint64_t bbase = tc::desc_interleave(bsa, lbo_b, 128u);
-      int cur_cob = -1, bloads = 0;
-      long long g = 0;  // tiles issued by this CTA
-      for (int i = 0; i < nu && !failed; ++i) {
-        const long long u = u0 + i;
-        const int cob = (int)fdiv((uint32_t)u, p.fd_upcob);
-        const long long t0 = (u - (long long)cob * p.upcob) * p.U;
-        const int nt = (int)min((long long)p.U, p.ntiles - t0);
-        if (cob != cur_cob) {
-          if (cur_cob >= 0) {
-            // Every MMA reading the old weights must finish before they are replaced.
-            tc::mma_commit(&bars->b_free);
-            if (!tc::mbar_wait_sleep(&bars->b_free, (uint32_t)((bloads - 1) & 1))) {
+      if constexpr (!STREAM) {
+        // The MMAs of one tile walk tap (kh, kw) x pair of 16-channel slices;
+        // B advances by one slice pair per MMA, A by the tap's row shift plus
+        // one slice pair.
+        const int pk = p.kcores / 2;
+        const uint64_t bbase = tc::desc_interleave(bsa, lbo_b, 128u);
+        int cur_cob = -1, bloads = 0;
+        long long g = 0;  // tiles issued by this CTA
+        for (int i = 0; i < nu && !failed; ++i) {
+          int cob, nt;
+          long long t0;
+          unit_of(u0 + i, cob, t0, nt);
+          if (cob != cur_cob) {
+            if (cur_cob >= 0) {
+              // Every MMA reading the old weights must finish before they are replaced.
+              tc::mma_commit(&bars->b_free);
+              if (!tc::mbar_wait_sleep(&bars->b_free, (uint32_t)((bloads - 1) & 1))) {
+                failed = true;
+                break;
+              }
+            }
+            mbar_arrive_expect_tx(&bars->b_full, p.b_bytes);
+            const unsigned char* src = p.bimg + (size_t)cob * p.b_bytes;
+            for (uint32_t off = 0; off < p.b_bytes; off += 32768u)
+              bulk_g2s(bsm + off, src + off, min(32768u, p.b_bytes - off), &bars->b_full);
+            if (!tc::mbar_wait_sleep(&bars->b_full, (uint32_t)(bloads & 1))) {
               failed = true;
               break;
             }
+            ++bloads;
+            cur_cob = cob;
           }
-          mbar_arrive_expect_tx(&bars->b_full, p.b_bytes);
-          const unsigned char* src = p.bimg + (size_t)cob * p.b_bytes;
-          for (uint32_t off = 0; off < p.b_bytes; off += 32768u)
-            bulk_g2s(bsm + off, src + off, min(32768u, p.b_bytes - off), &bars->b_full);
-          if (!tc::mbar_wait_sleep(&bars->b_full, (uint32_t)(bloads & 1))) {
-            failed = true;
-            break;
-          }
-          ++bloads;
-          cur_cob = cob;
-        }
-        const int a = i & 1;
-        if (!PROF_WAIT(0, tc::mbar_wait_sleep(&bars->a_full[a], (uint32_t)((i >> 1) & 1)))) {
-          failed = true;
-          break;
-        }
-        tc::fence_after();
-        const uint32_t asa = smem_u32(abuf + (size_t)a * p.a_bytes);
-        for (int j = 0; j < nt; ++j, ++g) {
-          const int d = (int)(g & 1);
-          if (g >= 2 && !PROF_WAIT(1, tc::mbar_wait_sleep(&bars->d_empty[d], (uint32_t)(((g >> 1) - 1) & 1)))) {
+          const int a = i & 1;
+          if (!tc::mbar_wait_sleep(&bars->a_full[a], (uint32_t)((i >> 1) & 1))) {
             failed = true;
             break;
           }
           tc::fence_after();
-          const uint32_t dt = tmem + (uint32_t)(d * p.N3);
-          const uint64_t abase = tc::desc_interleave(asa + (uint32_t)(j * kM) * 16u, p.a_plane, 128u);
-          uint64_t bd = bbase;
-          uint32_t acc = 0u;
-#ifdef SF_C3TC_PROF
-          const long long tm0 = clock64();
-#endif
-          for (int kh = 0; kh < 3; ++kh) {
+          const uint32_t asa = smem_u32(abuf + (size_t)a * p.a_bytes);
+          for (int j = 0; j < nt; ++j, ++g) {
+            const int d = (int)(g & 1);
+            if (g >= 2 && !tc::mbar_wait_sleep(&bars->d_empty[d], (uint32_t)(((g >> 1) - 1) & 1))) {
+              failed = true;
+              break;
+            }
+            tc::fence_after();
+            const uint32_t dt = tmem + (uint32_t)(d * p.N3);
+            const uint64_t abase = tc::desc_interleave(asa + (uint32_t)(j * kM) * 16u, p.a_plane, 128u);
+            uint64_t bd = bbase;
+            uint32_t acc = 0u;
+            for (int kh = 0; kh < 3; ++kh) {
 #pragma unroll
-            for (int kw = 0; kw < 3; ++kw) {
-              uint64_t ad = abase + (uint64_t)(kh * p.Wp + kw);
-              tc::mma_s8(dt, ad, bd, idesc, acc);
-              acc = 1u;
-              bd += bstep;
-              if (pk == 2) {
-                tc::mma_s8(dt, ad + astep, bd, idesc, 1u);
+              for (int kw = 0; kw < 3; ++kw) {
+                uint64_t ad = abase + (uint64_t)(kh * p.Wp + kw);
+                tc::mma_s8(dt, ad, bd, idesc, acc);
+                acc = 1u;
                 bd += bstep;
+                if (pk == 2) {
+                  tc::mma_s8(dt, ad + astep, bd, idesc, 1u);
+                  bd += bstep;
+                }
               }
             }
+            tc::mma_commit(&bars->d_full[d]);
           }
-#ifdef SF_C3TC_PROF
-          atomicAdd(&g_c3tc_prof[4], (unsigned long long)(clock64() - tm0));
-#endif
-          tc::mma_commit(&bars->d_full[d]);
+          if (failed) break;
+          tc::mma_commit(&bars->a_empty[a]);
         }
-        if (failed) break;
-        tc::mma_commit(&bars->a_empty[a]);
+      } else {
+        const int nkc = p.kcores / p.kch;  // weight stages per tap
+        const int pkc = p.kch / 2;          // MMAs per tile per stage
+        long long g = 0, st = 0;            // (unit, block) groups and weight stages consumed
+        for (int i = 0; i < nu && !failed; ++i) {
+          int cob0, nt;
+          long long t0;
+          unit_of(u0 + i, cob0, t0, nt);
+          const int a = i % p.nA;
+          if (!tc::mbar_wait_sleep(&bars->a_full[a], (uint32_t)((i / p.nA) & 1))) {
+            failed = true;
+            break;
+          }
+          tc::fence_after();
+          const uint32_t asa = smem_u32(abuf + (size_t)a * p.a_bytes);
+          for (int cob = 0; cob < p.ncob && !failed; ++cob, ++g) {
+            const int gb = (int)(g & 1);
+            if (g >= 2 && !tc::mbar_wait_sleep(&bars->d_empty[gb], (uint32_t)(((g >> 1) - 1) & 1))) {
+              failed = true;
+              break;
+            }
+            tc::fence_after();
+            for (int tap = 0; tap < 9 && !failed; ++tap) {
+              const int kh = tap / 3, kw = tap - kh * 3;
+              for (int kc = 0; kc < nkc; ++kc, ++st) {
+                const int s = (int)(st % p.nbs);
+                if (!tc::mbar_wait_sleep(&bars->s_full[s], (uint32_t)((st / p.nbs) & 1))) {
+                  failed = true;
+                  break;
+                }
+                tc::fence_after();
+                const uint64_t bstage = tc::desc_interleave(bsa + (uint32_t)s * p.bstage_bytes, lbo_b, 128u);
+                for (int j = 0; j < nt; ++j) {
+                  const uint32_t dt = tmem + (uint32_t)((gb * p.U + j) * p.N3);
+                  uint64_t ad = tc::desc_interleave(asa + (uint32_t)(j * kM + kh * p.Wp + kw) * 16u +
+                                                        (uint32_t)(kc * p.kch) * p.a_plane,
+                                                    p.a_plane, 128u);
+                  uint64_t bd = bstage;
+                  for (int kp = 0; kp < pkc; ++kp) {
+                    tc::mma_s8(dt, ad, bd, idesc, (tap | kc | kp) != 0 ? 1u : 0u);
+                    ad += astep;
+                    bd += bstep;
+                  }
+                }
+                tc::mma_commit(&bars->s_empty[s]);
+              }
+            }
+            if (failed) break;
+            tc::mma_commit(&bars->d_full[gb]);
+          }
+          if (failed) break;
+          tc::mma_commit(&bars->a_empty[a]);
+        }
       }
       if (failed) atomicExch(p.err, 1u);
     }
     __syncwarp();
-  } else if (warp >= kConvWarps) {
+  } else if (warp >= kEpi0) {
     // Epilogue: warp w reads TMEM lane quarter w % 4 (32 positions of the
     // tile) and a quarter of the block's output channels (16, or 8 when the
     // block is 32 wide).
-    const int ew = warp - kConvWarps;
+    const int ew = warp - kEpi0;
     const int qd = warp & 3;
     const int cwq = p.CB / 4;
     const int cbeg = (ew >> 2) * cwq;
     float2* tab = bars->tab[ew];  // (scale of digit 2, bias) of this warp's channels
     int tab_cob = -1;
     long long g = 0;
+    auto load_tab = [&](int cob) {
+      if (cob == tab_cob) return;
+      if (lane < 16) {
+        const int co = cob * p.CB + cbeg + lane;
+        tab[lane] = (lane < cwq && co < p.Co)
+                        ? make_float2(__ldg(p.scales + 2 * p.ncob * p.CB + co), p.bias ? __ldg(p.bias + co) : 0.f)
+                        : make_float2(0.f, 0.f);
+      }
+      __syncwarp();
+      tab_cob = cob;
+    };
     for (int i = 0; i < nu && !failed; ++i) {
       const long long u = u0 + i;
-      const int cob = (int)fdiv((uint32_t)u, p.fd_upcob);
-      const long long t0 = (u - (long long)cob * p.upcob) * p.U;
-      const int nt = (int)min((long long)p.U, p.ntiles - t0);
-      const int cbase = cob * p.CB + cbeg;
-      if (cob != tab_cob) {
-        if (lane < 16) {
-          const int co = cbase + lane;
-          tab[lane] = (lane < cwq && co < p.Co)
-                          ? make_float2(__ldg(p.scales + 2 * p.ncob * p.CB + co), p.bias ? __ldg(p.bias + co) : 0.f)
-                          : make_float2(0.f, 0.f);
-        }
-        __syncwarp();
-        tab_cob = cob;
-      }
-      const int nco = min(cwq, p.Co - cbase);  // valid channels of this warp (may be <= 0)
-      for (int j = 0; j < nt; ++j, ++g) {
-        const int d = (int)(g & 1);
-        if (!PROF_WAIT(2, tc::mbar_wait_sleep(&bars->d_full[d], (uint32_t)((g >> 1) & 1)))) {
-          failed = true;
-          break;
-        }
-        tc::fence_after();
-        const bool odd = *reinterpret_cast<volatile uint32_t*>(&bars->tag[u % kTags]) == (uint32_t)(u + 1);
-        // This lane's output position.
-        const uint32_t o = (uint32_t)((t0 + j) * kM) + qd * 32 + lane;
-        const uint32_t Ro = fdiv(o, p.fd_wp);
-        const int c = (int)(o - Ro * p.Wp);
-        const uint32_t img = fdiv(Ro, p.fd_hs);
-        const int h = (int)(Ro - img * p.Hs);
-        const bool valid = c < p.W && h < p.H && img < (uint32_t)p.N;
-        XT* yp = static_cast<XT*>(p.y) + ((size_t)img * p.Co + cbase) * HW + (size_t)h * p.W + c;
-        if (!odd) {
-          const float4* tb = reinterpret_cast<const float4*>(tab);
-          for (int c8 = 0; c8 < cwq; c8 += 8) {
-            uint32_t r0[8], r1[8], r2[8];
-            const uint32_t ta = tmem + ((uint32_t)(qd * 32) << 16) + (uint32_t)(d * p.N3 + cbeg + c8);
-            tc::tmem_ld8(ta, r0);
-            tc::tmem_ld8(ta + (uint32_t)p.CB, r1);
-            tc::tmem_ld8(ta + (uint32_t)(2 * p.CB), r2);
-            tc::tmem_wait_ld();
-            if (valid) {
-              // |D| < 2^22, so adding 1.5 * 2^23 to the bits gives the float
-              // 1.5 * 2^23 + D exactly (no conversion instruction); the scaled
-              // digit sums are then exact, and only their sum rounds.
-#pragma unroll
-              for (int e = 0; e < 8; e += 2) {
-                if (c8 + e >= nco) break;
-                const float4 sb = tb[(c8 + e) >> 1];
-#pragma unroll
-                for (int f = 0; f < 2; ++f) {
-                  const float a0 = __int_as_float((int)r0[e + f] + 0x4B400000);
-                  const float a1 = __int_as_float((int)r1[e + f] + 0x4B400000);
-                  const float a2 = __int_as_float((int)r2[e + f] + 0x4B400000);
-                  const float x0 = fmaf(a0, 65536.f, -12582912.f * 65536.f);
-                  const float x1 = fmaf(a1, 256.f, -12582912.f * 256.f);
-                  const float x2 = a2 - 12582912.f;
-                  const float v = fmaf(f ? sb.z : sb.x, (x0 + x1) + x2, f ? sb.w : sb.y);
-                  // Evict-first stores: y is not read again here (1.7 % faster on the C5 cell).
-                  if (c8 + e + f < nco) st_cs(yp + (uint32_t)(c8 + e + f) * (uint32_t)HW, DT<XT>::from_f(v));
-                }
-              }
-            }
+      int cob0, nt;
+      long long t0;
+      unit_of(u, cob0, t0, nt);
+      if constexpr (!STREAM) {
+        load_tab(cob0);
+        const int nco = min(cwq, p.Co - (cob0 * p.CB + cbeg));  // valid channels of this warp (may be <= 0)
+        for (int j = 0; j < nt; ++j, ++g) {
+          const int d = (int)(g & 1);
+          if (!tc::mbar_wait_sleep(&bars->d_full[d], (uint32_t)((g >> 1) & 1))) {
+            failed = true;
+            break;
           }
-        } else if (valid) {
-          // Values other than 0 / 1: fp32 FMAs from x and the weights.
-          const XT* ximg = x + (size_t)img * p.C * HW;
-          for (int cc = 0; cc < nco; ++cc) {
-            const int co = cbase + cc;
-            float acc = 0.f;
-            for (int ci = 0; ci < p.C; ++ci) {
-              for (int tap = 0; tap < 9; ++tap) {
-                const int ih = h + tap / 3 - 1, iw = c + tap % 3 - 1;
-                if (ih < 0 || ih >= p.H || iw < 0 || iw >= p.W) continue;
-                const float xv = DT<XT>::to_f(ximg[(size_t)ci * HW + (size_t)ih * p.W + iw]);
-                if (xv != 0.f) acc = fmaf(xv, gather_w<WT>(p, co, ci, tap), acc);
-              }
-            }
-            yp[(size_t)cc * HW] = DT<XT>::from_f(acc + (p.bias ? __ldg(p.bias + co) : 0.f));
-          }
+          tc::fence_after();
+          const bool odd = *reinterpret_cast<volatile uint32_t*>(&bars->tag[u % kTags]) == (uint32_t)(u + 1);
+          epilogue_tile<XT, WT>(p, x, tmem, (uint32_t)(d * p.N3), t0 + j, cob0, qd, lane, cbeg, cwq, nco, tab, odd);
+          tc::fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars->d_empty[d]);
         }
-        tc::fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars->d_empty[d]);
+      } else {
+        for (int cob = 0; cob < p.ncob && !failed; ++cob, ++g) {
+          load_tab(cob);
+          const int nco = min(cwq, p.Co - (cob * p.CB + cbeg));
+          const int gb = (int)(g & 1);
+          if (!tc::mbar_wait_sleep(&bars->d_full[gb], (uint32_t)((g >> 1) & 1))) {
+            failed = true;
+            break;
+          }
+          tc::fence_after();
+          const bool odd = *reinterpret_cast<volatile uint32_t*>(&bars->tag[u % kTags]) == (uint32_t)(u + 1);
+          for (int j = 0; j < nt; ++j)
+            epilogue_tile<XT, WT>(p, x, tmem, (uint32_t)((gb * p.U + j) * p.N3), t0 + j, cob, qd, lane, cbeg, cwq,
+                                  nco, tab, odd);
+          tc::fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars->d_empty[gb]);
+        }
       }
     }
     if (failed && lane == 0) atomicExch(p.err, 1u);
+  } else if (STREAM && warp == kProducer) {
+    if (lane == 0) {
+      const int nkc = p.kcores / p.kch;
+      long long st = 0;
+      for (int i = 0; i < nu && !failed; ++i) {
+        for (int cob = 0; cob < p.ncob && !failed; ++cob) {
+          for (int tap = 0; tap < 9 && !failed; ++tap) {
+            for (int kc = 0; kc < nkc; ++kc, ++st) {
+              const int s = (int)(st % p.nbs);
+              if (st >= p.nbs && !tc::mbar_wait_sleep(&bars->s_empty[s], (uint32_t)(((st / p.nbs) - 1) & 1))) {
+                failed = true;
+                break;
+              }
+              mbar_arrive_expect_tx(&bars->s_full[s], p.bstage_bytes);
+              const unsigned char* src =
+                  p.bimg + (((size_t)cob * 9 + tap) * p.kcores + (size_t)kc * p.kch) * p.N3 * 16;
+              bulk_g2s(bsm + (size_t)s * p.bstage_bytes, src, p.bstage_bytes, &bars->s_full[s]);
+            }
+          }
+        }
+      }
+      if (failed) atomicExch(p.err, 1u);
+    }
+    __syncwarp();
   } else {
     for (int i = 0; i < nu && !failed; ++i) {
       const long long u = u0 + i;
-      const int cob = (int)fdiv((uint32_t)u, p.fd_upcob);
-      const long long t0 = (u - (long long)cob * p.upcob) * p.U;
-      const int a = i & 1;
-      if (i >= 2 && !PROF_WAIT(3, tc::mbar_wait_sleep(&bars->a_empty[a], (uint32_t)(((i >> 1) - 1) & 1)))) {
+      int cob, nt;
+      long long t0;
+      unit_of(u, cob, t0, nt);
+      const int na = STREAM ? p.nA : 2;
+      const int a = i % na;
+      if (i >= na && !tc::mbar_wait_sleep(&bars->a_empty[a], (uint32_t)(((i / na) - 1) & 1))) {
         failed = true;
         break;
       }
       unsigned char* ab = abuf + (size_t)a * p.a_bytes;
       uint32_t nb = 0u;
       if constexpr (VEC)
-        convert_unit_vec4(p, reinterpret_cast<const float*>(x), ab, t0 * kM, warp, lane, nb);
+        convert_unit_vec4(p, reinterpret_cast<const float*>(x), ab, t0 * kM, warp, lane, kConv, nb);
       else
-        convert_unit_scalar<XT>(p, x, ab, t0 * kM, warp, lane, nb);
+        convert_unit_scalar<XT>(p, x, ab, t0 * kM, warp, lane, kConv, nb);
       if (__any_sync(0xffffffffu, nb != 0u) && lane == 0)
         *reinterpret_cast<volatile uint32_t*>(&bars->tag[u % kTags]) = (uint32_t)(u + 1);
       fence_proxy_async_smem();
@@ -517,18 +630,6 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
     }
     if (failed && lane == 0) atomicExch(p.err, 1u);
   }
-#ifdef SF_C3TC_PROF
-  if (lane == 0) {
-    if (warp == kMmaWarp) {
-      atomicAdd(&g_c3tc_prof[0], prof_w[0]);
-      atomicAdd(&g_c3tc_prof[1], prof_w[1]);
-    } else if (warp >= kConvWarps) {
-      atomicAdd(&g_c3tc_prof[2], prof_w[0]);
-    } else {
-      atomicAdd(&g_c3tc_prof[3], prof_w[1]);
-    }
-  }
-#endif
   tc::fence_before();
   __syncthreads();
   if (warp == kMmaWarp) {
@@ -615,7 +716,10 @@ struct Geo {
 };
 Geo geometry(int Co, int C) {
   Geo g;
-  g.CB = Co <= 32 ? 32 : 64;
+  // 64-channel output blocks (N = 192) when the weights stay resident; 32
+  // (N = 96) when they stream (C_in > 64), so two tiles' D of two blocks
+  // fit TMEM.
+  g.CB = (Co <= 32 || C > kTcResidentMaxC) ? 32 : 64;
   g.ncob = (Co + g.CB - 1) / g.CB;
   g.N3 = 3 * g.CB;
   g.kcores = (C + 31) / 32 * 2;
@@ -629,7 +733,9 @@ sf_status launch(Params p, size_t smem, cudaStream_t st) {
   // 16-byte row loads: fp32 rows of a multiple of 4 values, 16-byte aligned x.
   const bool vec = std::is_same<XT, float>::value && p.W % 4 == 0 &&
                    (reinterpret_cast<uintptr_t>(p.x) & 15u) == 0;
-  auto kern = vec ? conv3x3_tc_kernel<XT, WT, true> : conv3x3_tc_kernel<XT, WT, false>;
+  const bool stream = p.nbs > 0;
+  auto kern = stream ? (vec ? conv3x3_tc_kernel<XT, WT, true, true> : conv3x3_tc_kernel<XT, WT, false, true>)
+                     : (vec ? conv3x3_tc_kernel<XT, WT, true, false> : conv3x3_tc_kernel<XT, WT, false, false>);
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return SF_ERR_CUDA;
   const long long grid = (p.nunits + p.units_per_cta - 1) / p.units_per_cta;
@@ -646,15 +752,7 @@ sf_status dispatch_w(int wdt, const Params& p, size_t smem, cudaStream_t st) {
 
 }  // namespace
 
-#ifdef SF_C3TC_PROF
-extern "C" int sf_dev_c3tc_prof(unsigned long long* out) {
-  cudaMemcpyFromSymbol(out, g_c3tc_prof, sizeof(g_c3tc_prof));
-  unsigned long long z[8] = {0};
-  return (int)cudaMemcpyToSymbol(g_c3tc_prof, z, sizeof(z));
-}
-#endif
-
-bool tc3_packs(int Co, int C, int K) { return K == 3 && C >= 1 && C <= kTcMaxC && Co >= 1; }
+bool tc3_packs(int Co, int C, int K) { return K == 3 && C >= 1 && C <= kTcMaxC && Co >= 1 && Co <= 4096; }
 
 size_t tc3_section_bytes(int Co, int C) {
   const Geo g = geometry(Co, C);
@@ -707,39 +805,86 @@ sf_status run_conv3x3_tc(const void* x, const void* w_gather, int cpl, const voi
   const size_t limit = 227 * 1024;
   size_t smem = 0;
   int U = 0;
-  // Units of up to 6 tiles (the halo rows a unit converts twice shrink with
-  // U) within 200 KB of shared memory: past that the L1 left beside it is too
-  // small and the x stream slows (U = 6 at 226 KB measured 24 % slower on the
-  // C64 56x56 cell than U = 4 at 191 KB). The full 227 KB only when nothing
-  // smaller fits.
-  for (size_t budget : {(size_t)200 * 1024, limit}) {
-    for (int u = 6; u >= 1 && U == 0; --u) {
-      const uint32_t rows = (uint32_t)((u * kM + 2 * p.Wp + 2 + 31) / 32 * 32);
-      const size_t a_bytes = (size_t)rows * 16 * g.kcores;
-      const size_t a_off = (g.b_bytes + 127) / 128 * 128;
-      const size_t bar_off = a_off + 2 * a_bytes;
-      const size_t total = bar_off + sizeof(Bars);
-      if (total <= budget) {
-        U = u;
-        p.rows_a = rows;
-        p.a_plane = rows * 16;
-        p.a_bytes = (uint32_t)a_bytes;
-        p.a_off = (uint32_t)a_off;
-        p.bar_off = (uint32_t)bar_off;
-        smem = total;
+  auto rows_for = [&](int u) { return (uint32_t)((u * kM + 2 * p.Wp + 2 + 31) / 32 * 32); };
+  if (C <= kTcResidentMaxC) {
+    // Resident weights: [B digits][2 A buffers][barriers]. Units of up to 6
+    // tiles (the halo rows a unit converts twice shrink with U) within 200 KB
+    // of shared memory: past that the L1 left beside it is too small and the
+    // x stream slows (U = 6 at 226 KB measured 24 % slower on the C64 56x56
+    // cell than U = 4 at 191 KB). The full 227 KB only when nothing smaller
+    // fits.
+    for (size_t budget : {(size_t)200 * 1024, limit}) {
+      for (int u = 6; u >= 1 && U == 0; --u) {
+        const uint32_t rows = rows_for(u);
+        const size_t a_bytes = (size_t)rows * 16 * g.kcores;
+        const size_t a_off = (g.b_bytes + 127) / 128 * 128;
+        const size_t bar_off = a_off + 2 * a_bytes;
+        const size_t total = bar_off + sizeof(Bars);
+        if (total <= budget) {
+          U = u;
+          p.rows_a = rows;
+          p.a_plane = rows * 16;
+          p.a_bytes = (uint32_t)a_bytes;
+          p.b_off = 0;
+          p.a_off = (uint32_t)a_off;
+          p.bar_off = (uint32_t)bar_off;
+          p.nA = 2;
+          p.nbs = 0;
+          smem = total;
+        }
       }
+      if (U) break;
     }
-    if (U) break;
+  } else {
+    // Streamed weights: [nA A buffers][nbs weight stages][barriers]. A stage
+    // holds kch 16-channel slices of one tap of one 32-channel block. Prefer
+    // two tiles per unit (each weight stage feeds both), then double-buffered
+    // A, then more stages.
+    p.kch = std::min(g.kcores, 16);
+    p.bstage_bytes = (uint32_t)(p.kch * g.N3 * 16);
+    const int cand[4][2] = {{2, 2}, {2, 1}, {1, 2}, {1, 1}};
+    for (size_t budget : {(size_t)200 * 1024, limit}) {
+      for (int ci = 0; ci < 4 && U == 0; ++ci) {
+        for (int nbs = kMaxBStages; nbs >= 2 && U == 0; --nbs) {
+          const int u = cand[ci][0], na = cand[ci][1];
+          const uint32_t rows = rows_for(u);
+          const size_t a_bytes = (size_t)rows * 16 * g.kcores;
+          const size_t b_off = (size_t)na * a_bytes;
+          const size_t bar_off = (b_off + (size_t)nbs * p.bstage_bytes + 127) / 128 * 128;
+          const size_t total = bar_off + sizeof(Bars);
+          if (total <= budget && (nbs >= 3 || budget == limit)) {
+            U = u;
+            p.rows_a = rows;
+            p.a_plane = rows * 16;
+            p.a_bytes = (uint32_t)a_bytes;
+            p.a_off = 0;
+            p.b_off = (uint32_t)b_off;
+            p.bar_off = (uint32_t)bar_off;
+            p.nA = na;
+            p.nbs = nbs;
+            smem = total;
+          }
+        }
+      }
+      if (U) break;
+    }
   }
   if (U == 0) return SF_ERR_UNSUPPORTED;
   smem = std::max<size_t>(smem, 120 * 1024);  // one CTA (and one TMEM allocation) per SM
   p.U = U;
-  p.upcob = (p.ntiles + U - 1) / U;
+  if (p.nbs > 0) {
+    p.upcob = (p.ntiles + U - 1) / U;  // units cover every block in turn
+    p.nunits = p.upcob;
+  } else {
+    p.upcob = (p.ntiles + U - 1) / U;
+    p.nunits = p.upcob * p.ncob;
+  }
   p.fd_upcob = make_fastdiv((uint32_t)p.upcob);
-  p.nunits = p.upcob * p.ncob;
   uint32_t cols = 32;
+  while (cols < (uint32_t)(2 * U * p.N3) && p.nbs > 0) cols <<= 1;
   while (cols < (uint32_t)(2 * p.N3)) cols <<= 1;
   p.tmem_cols = cols;
+  if (cols > 512) return SF_ERR_UNSUPPORTED;
   const long long ctas = std::min<long long>(p.nunits, (long long)num_sms_current_device());
   p.units_per_cta = (p.nunits + ctas - 1) / ctas;
   switch (xdt) {

@@ -6,8 +6,11 @@
 namespace sf {
 namespace c3tc {
 
-// Input channels the kernel takes (its weight digits stay in shared memory).
-constexpr int kTcMaxC = 64;
+// Input channels the kernel takes; up to kTcResidentMaxC the weight digits
+// of an output block stay in shared memory, above it they stream through a
+// ring of stages while the unit's converted input stays resident.
+constexpr int kTcMaxC = 512;
+constexpr int kTcResidentMaxC = 64;
 
 // Whether sf_pack_weights appends the tensor-core section for this layer.
 bool tc3_packs(int Co, int C, int K);

@@ -40,6 +40,14 @@ GEOM = [
     (2, 64, 15, 3, 64, 0.0),
     (64, 64, 8, 8, 64, 0.02),
     (1, 33, 57, 57, 65, 0.03),
+    # C_in > 64: weight stages stream past the resident input (32-channel output blocks)
+    (2, 128, 28, 28, 128, 0.05),
+    (2, 96, 13, 30, 40, 0.1),
+    (1, 130, 9, 9, 200, 0.2),
+    (1, 256, 14, 14, 256, 0.2),
+    (1, 512, 14, 14, 512, 0.01),
+    (1, 512, 56, 56, 32, 0.01),
+    (3, 256, 7, 7, 64, 0.3),
 ]
 
 

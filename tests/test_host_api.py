@@ -163,7 +163,8 @@ def test_native_argument_checks_without_gpu():
     # digit scales [3][64] fp32 and the digit image [9 taps][2 slices of 16 ch][3 * 64 rows][16 B]
     assert lib.sf_packed_weight_bytes(64, 32, 3, 0) == 32 * 9 * 64 * 4 + 3 * 64 * 4 + 9 * 2 * 192 * 16
     assert lib.sf_packed_weight_bytes(64, 256, 1, 0) == 256 * 64 * 4
-    assert lib.sf_packed_weight_bytes(128, 128, 3, 0) == 128 * 9 * 128 * 4
+    # C_in > 64: 32-channel output blocks (N = 96), digit image [4 blocks][9][8 slices][96][16]
+    assert lib.sf_packed_weight_bytes(128, 128, 3, 0) == 128 * 9 * 128 * 4 + 3 * 128 * 4 + 4 * 9 * 8 * 96 * 16
     cd = _lib.ConvDesc(2, 64, 56, 56, 64, 56, 56, 3, 1, 1, 0, 0, 1)
     assert lib.sf_sparse_conv2d_workspace_size(ctypes.byref(cd)) == 2 * 56 * 56 * 8 + 256
 
