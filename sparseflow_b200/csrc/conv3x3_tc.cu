@@ -59,7 +59,7 @@ constexpr int kEpi0 = 15;
 constexpr int kEpiWarps = 16;
 constexpr int kMmaWarp = kEpi0 + kEpiWarps;
 constexpr int kThreads = (kMmaWarp + 1) * 32;
-constexpr int kMaxBStages = 4;
+constexpr int kMaxBStages = 8;
 constexpr int kM = 128;
 constexpr int kTags = 4;
 
@@ -329,6 +329,15 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const XT* __restr
   }
 }
 
+#ifdef SF_C3TC_PROF
+__device__ unsigned long long g_c3tc_prof[8];
+#define PROF_T0() const long long pt0_ = clock64()
+#define PROF_ADD(slot) atomicAdd(&g_c3tc_prof[slot], (unsigned long long)(clock64() - pt0_))
+#else
+#define PROF_T0()
+#define PROF_ADD(slot)
+#endif
+
 // STREAM = false: the weight digits of one output block stay in shared
 // memory (C_in <= 64); D per tile, double buffered. STREAM = true: weight
 // stages stream past the resident A of a unit once per output block; D per
@@ -462,48 +471,68 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
       } else {
         const int nkc = p.kcores / p.kch;  // weight stages per tap
         const int pkc = p.kch / 2;          // MMAs per tile per stage
-        long long g = 0, st = 0;            // (unit, block) groups and weight stages consumed
+        long long g = 0;                    // (unit, block) groups issued
+        int s = 0;                          // weight stage slot
+        uint32_t sphase = 0;                // its mbarrier phase (flips at each ring wrap)
         for (int i = 0; i < nu && !failed; ++i) {
           int cob0, nt;
           long long t0;
           unit_of(u0 + i, cob0, t0, nt);
           const int a = i % p.nA;
-          if (!tc::mbar_wait_sleep(&bars->a_full[a], (uint32_t)((i / p.nA) & 1))) {
-            failed = true;
-            break;
+          {
+            PROF_T0();
+            if (!tc::mbar_wait_sleep(&bars->a_full[a], (uint32_t)((i / p.nA) & 1))) {
+              failed = true;
+              break;
+            }
+            PROF_ADD(0);
           }
           tc::fence_after();
           const uint32_t asa = smem_u32(abuf + (size_t)a * p.a_bytes);
           for (int cob = 0; cob < p.ncob && !failed; ++cob, ++g) {
             const int gb = (int)(g & 1);
-            if (g >= 2 && !tc::mbar_wait_sleep(&bars->d_empty[gb], (uint32_t)(((g >> 1) - 1) & 1))) {
-              failed = true;
-              break;
+            {
+              PROF_T0();
+              if (g >= 2 && !tc::mbar_wait_sleep(&bars->d_empty[gb], (uint32_t)(((g >> 1) - 1) & 1))) {
+                failed = true;
+                break;
+              }
+              PROF_ADD(1);
             }
             tc::fence_after();
             for (int tap = 0; tap < 9 && !failed; ++tap) {
               const int kh = tap / 3, kw = tap - kh * 3;
-              for (int kc = 0; kc < nkc; ++kc, ++st) {
-                const int s = (int)(st % p.nbs);
-                if (!tc::mbar_wait_sleep(&bars->s_full[s], (uint32_t)((st / p.nbs) & 1))) {
-                  failed = true;
-                  break;
+              for (int kc = 0; kc < nkc; ++kc) {
+                {
+                  PROF_T0();
+                  if (!tc::mbar_wait_sleep(&bars->s_full[s], sphase)) {
+                    failed = true;
+                    break;
+                  }
+                  PROF_ADD(2);
                 }
+                PROF_T0();
                 tc::fence_after();
                 const uint64_t bstage = tc::desc_interleave(bsa + (uint32_t)s * p.bstage_bytes, lbo_b, 128u);
+                const uint64_t a0 = tc::desc_interleave(asa + (uint32_t)(kh * p.Wp + kw) * 16u +
+                                                            (uint32_t)(kc * p.kch) * p.a_plane,
+                                                        p.a_plane, 128u);
+                const uint32_t first = (tap | kc) == 0 ? 0u : 1u;
                 for (int j = 0; j < nt; ++j) {
                   const uint32_t dt = tmem + (uint32_t)((gb * p.U + j) * p.N3);
-                  uint64_t ad = tc::desc_interleave(asa + (uint32_t)(j * kM + kh * p.Wp + kw) * 16u +
-                                                        (uint32_t)(kc * p.kch) * p.a_plane,
-                                                    p.a_plane, 128u);
-                  uint64_t bd = bstage;
-                  for (int kp = 0; kp < pkc; ++kp) {
-                    tc::mma_s8(dt, ad, bd, idesc, (tap | kc | kp) != 0 ? 1u : 0u);
-                    ad += astep;
-                    bd += bstep;
-                  }
+                  const uint64_t ad = a0 + (uint64_t)(j * kM);  // 128 rows of 16 bytes
+                  // At most 4 slice pairs per stage (kch <= 8): unrolled, one add per operand.
+                  tc::mma_s8(dt, ad, bstage, idesc, first);
+#pragma unroll
+                  for (int kp = 1; kp < 4; ++kp)
+                    if (kp < pkc) tc::mma_s8(dt, ad + kp * astep, bstage + kp * bstep, idesc, 1u);
                 }
                 tc::mma_commit(&bars->s_empty[s]);
+                PROF_ADD(3);
+                if (++s == p.nbs) {
+                  s = 0;
+                  sphase ^= 1u;
+                }
               }
             }
             if (failed) break;
@@ -583,13 +612,13 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
   } else if (STREAM && warp == kProducer) {
     if (lane == 0) {
       const int nkc = p.kcores / p.kch;
-      long long st = 0;
+      int s = 0;
+      uint32_t round = 0;  // passes over the ring
       for (int i = 0; i < nu && !failed; ++i) {
         for (int cob = 0; cob < p.ncob && !failed; ++cob) {
           for (int tap = 0; tap < 9 && !failed; ++tap) {
-            for (int kc = 0; kc < nkc; ++kc, ++st) {
-              const int s = (int)(st % p.nbs);
-              if (st >= p.nbs && !tc::mbar_wait_sleep(&bars->s_empty[s], (uint32_t)(((st / p.nbs) - 1) & 1))) {
+            for (int kc = 0; kc < nkc; ++kc) {
+              if (round > 0 && !tc::mbar_wait_sleep(&bars->s_empty[s], (round - 1) & 1u)) {
                 failed = true;
                 break;
               }
@@ -597,6 +626,10 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
               const unsigned char* src =
                   p.bimg + (((size_t)cob * 9 + tap) * p.kcores + (size_t)kc * p.kch) * p.N3 * 16;
               bulk_g2s(bsm + (size_t)s * p.bstage_bytes, src, p.bstage_bytes, &bars->s_full[s]);
+              if (++s == p.nbs) {
+                s = 0;
+                ++round;
+              }
             }
           }
         }
@@ -752,6 +785,14 @@ sf_status dispatch_w(int wdt, const Params& p, size_t smem, cudaStream_t st) {
 
 }  // namespace
 
+#ifdef SF_C3TC_PROF
+extern "C" int sf_dev_c3tc_prof(unsigned long long* out) {
+  cudaMemcpyFromSymbol(out, g_c3tc_prof, 8 * sizeof(unsigned long long));
+  unsigned long long z[8] = {0};
+  return (int)cudaMemcpyToSymbol(g_c3tc_prof, z, sizeof(z));
+}
+#endif
+
 bool tc3_packs(int Co, int C, int K) { return K == 3 && C >= 1 && C <= kTcMaxC && Co >= 1 && Co <= 4096; }
 
 size_t tc3_section_bytes(int Co, int C) {
@@ -840,11 +881,17 @@ sf_status run_conv3x3_tc(const void* x, const void* w_gather, int cpl, const voi
     // holds kch 16-channel slices of one tap of one 32-channel block. Prefer
     // two tiles per unit (each weight stage feeds both), then double-buffered
     // A, then more stages.
-    p.kch = std::min(g.kcores, 16);
+    // Stages of at most 8 slices (12 KB): more of them in flight cover the
+    // L2 latency of the weight stream.
+    p.kch = std::min(g.kcores, 8);
+    while (g.kcores % p.kch) p.kch -= 2;
     p.bstage_bytes = (uint32_t)(p.kch * g.N3 * 16);
     const int cand[4][2] = {{2, 2}, {2, 1}, {1, 2}, {1, 1}};
-    for (size_t budget : {(size_t)200 * 1024, limit}) {
-      for (int ci = 0; ci < 4 && U == 0; ++ci) {
+    // Two tiles per unit halve the weight bytes per MMA, which bound the
+    // large layers, so they win even at the full 227 KB (C512 14x14: 2.9 ms
+    // with one tile per unit at 180 KB).
+    for (int ci = 0; ci < 4 && U == 0; ++ci) {
+      for (size_t budget : {(size_t)200 * 1024, limit}) {
         for (int nbs = kMaxBStages; nbs >= 2 && U == 0; --nbs) {
           const int u = cand[ci][0], na = cand[ci][1];
           const uint32_t rows = rows_for(u);
@@ -852,7 +899,7 @@ sf_status run_conv3x3_tc(const void* x, const void* w_gather, int cpl, const voi
           const size_t b_off = (size_t)na * a_bytes;
           const size_t bar_off = (b_off + (size_t)nbs * p.bstage_bytes + 127) / 128 * 128;
           const size_t total = bar_off + sizeof(Bars);
-          if (total <= budget && (nbs >= 3 || budget == limit)) {
+          if (total <= budget && (nbs >= 4 || budget == limit)) {
             U = u;
             p.rows_a = rows;
             p.a_plane = rows * 16;
@@ -865,8 +912,8 @@ sf_status run_conv3x3_tc(const void* x, const void* w_gather, int cpl, const voi
             smem = total;
           }
         }
+        if (U) break;
       }
-      if (U) break;
     }
   }
   if (U == 0) return SF_ERR_UNSUPPORTED;
