@@ -168,4 +168,19 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 int num_sms_current_device();
 
+// Device-side choice between two kernel paths launched back to back: a
+// sampling kernel writes a nonzero count to *count, and each gated kernel
+// returns at entry unless the count selects it (side 1: count < thr; side 2:
+// count >= thr). side 0: not gated.
+struct Gate {
+  const uint32_t* count;
+  uint32_t thr;
+  int side;
+};
+__device__ __forceinline__ bool gate_open(const Gate& g) {
+  if (g.side == 0) return true;
+  const uint32_t c = *reinterpret_cast<const volatile uint32_t*>(g.count);
+  return g.side == 1 ? c < g.thr : c >= g.thr;
+}
+
 }  // namespace sf

@@ -98,6 +98,7 @@ struct Params {
   // 16-channel slices of one tap of one 32-channel output block.
   int nA, nbs, kch;
   uint32_t b_off, bstage_bytes;
+  Gate gate;  // runs only when the gate selects this path
 };
 
 struct Bars {
@@ -346,6 +347,7 @@ template <typename XT, typename WT, bool VEC, bool STREAM>
 __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p) {
   constexpr int kConv = STREAM ? kEpi0 - 1 : kEpi0;  // converter warps
   constexpr int kProducer = kEpi0 - 1;              // weight-stage copier (STREAM)
+  if (!gate_open(p.gate)) return;  // uniform across the grid: before any barrier or TMEM allocation
   extern __shared__ __align__(128) unsigned char smem[];
   unsigned char* bsm = smem + p.b_off;
   unsigned char* abuf = smem + p.a_off;
@@ -813,22 +815,12 @@ sf_status tc3_pack(const void* w, int src_dtype, int Co, int C, void* section, c
   return cudaGetLastError() == cudaSuccess ? SF_OK : SF_ERR_CUDA;
 }
 
-sf_status run_conv3x3_tc(const void* x, const void* w_gather, int cpl, const void* section, const float* bias,
-                         void* y, uint32_t* err, int N, int C, int H, int W, int Co, int xdt, int wdt,
-                         cudaStream_t st) {
-  if (!tc3_packs(Co, C, 3)) return SF_ERR_UNSUPPORTED;
-  if (wdt != SF_DTYPE_F32 && wdt != SF_DTYPE_BF16) return SF_ERR_UNSUPPORTED;
+namespace {
+// Launch plan (geometry, unit size, shared-memory layout, TMEM columns);
+// false for shapes the kernel does not take.
+bool plan_tc(Params& p, size_t& smem_out, int N, int C, int H, int W, int Co) {
+  if (!tc3_packs(Co, C, 3)) return false;
   const Geo g = geometry(Co, C);
-  Params p;
-  memset(&p, 0, sizeof(p));
-  p.x = x;
-  p.scales = static_cast<const float*>(section);
-  p.bimg = static_cast<const unsigned char*>(section) + g.scale_bytes;
-  p.bias = bias;
-  p.wg = w_gather;
-  p.cpl = cpl;
-  p.y = y;
-  p.err = err;
   p.N = N; p.C = C; p.H = H; p.W = W; p.Co = Co;
   p.Wp = W + 2;
   p.Hs = H + 1;
@@ -841,7 +833,7 @@ sf_status run_conv3x3_tc(const void* x, const void* w_gather, int cpl, const voi
   const long long positions = (long long)N * p.Hs * p.Wp;
   p.ntiles = (positions + kM - 1) / kM;
   // Positions (and the A rows past the last tile) are decoded in 32 bits.
-  if (p.ntiles * kM + 4ll * kM + 2ll * p.Wp >= (1ll << 31)) return SF_ERR_UNSUPPORTED;
+  if (p.ntiles * kM + 4ll * kM + 2ll * p.Wp >= (1ll << 31)) return false;
   p.b_bytes = (uint32_t)g.b_bytes;
   const size_t limit = 227 * 1024;
   size_t smem = 0;
@@ -916,7 +908,7 @@ sf_status run_conv3x3_tc(const void* x, const void* w_gather, int cpl, const voi
       }
     }
   }
-  if (U == 0) return SF_ERR_UNSUPPORTED;
+  if (U == 0) return false;
   smem = std::max<size_t>(smem, 120 * 1024);  // one CTA (and one TMEM allocation) per SM
   p.U = U;
   if (p.nbs > 0) {
@@ -931,9 +923,39 @@ sf_status run_conv3x3_tc(const void* x, const void* w_gather, int cpl, const voi
   while (cols < (uint32_t)(2 * U * p.N3) && p.nbs > 0) cols <<= 1;
   while (cols < (uint32_t)(2 * p.N3)) cols <<= 1;
   p.tmem_cols = cols;
-  if (cols > 512) return SF_ERR_UNSUPPORTED;
+  if (cols > 512) return false;
   const long long ctas = std::min<long long>(p.nunits, (long long)num_sms_current_device());
   p.units_per_cta = (p.nunits + ctas - 1) / ctas;
+  smem_out = smem;
+  return true;
+}
+}  // namespace
+
+bool tc3_supported(int N, int C, int H, int W, int Co) {
+  Params p;
+  memset(&p, 0, sizeof(p));
+  size_t smem = 0;
+  return plan_tc(p, smem, N, C, H, W, Co);
+}
+
+sf_status run_conv3x3_tc(const void* x, const void* w_gather, int cpl, const void* section, const float* bias,
+                         void* y, uint32_t* err, int N, int C, int H, int W, int Co, int xdt, int wdt,
+                         cudaStream_t st, const Gate& gate) {
+  if (wdt != SF_DTYPE_F32 && wdt != SF_DTYPE_BF16) return SF_ERR_UNSUPPORTED;
+  Params p;
+  memset(&p, 0, sizeof(p));
+  size_t smem = 0;
+  if (!plan_tc(p, smem, N, C, H, W, Co)) return SF_ERR_UNSUPPORTED;
+  const Geo g = geometry(Co, C);
+  p.x = x;
+  p.scales = static_cast<const float*>(section);
+  p.bimg = static_cast<const unsigned char*>(section) + g.scale_bytes;
+  p.bias = bias;
+  p.wg = w_gather;
+  p.cpl = cpl;
+  p.y = y;
+  p.err = err;
+  p.gate = gate;
   switch (xdt) {
     case SF_DTYPE_F32: return dispatch_w<float>(wdt, p, smem, st);
     case SF_DTYPE_F16: return dispatch_w<__half>(wdt, p, smem, st);

@@ -19,10 +19,13 @@ bool tc3_packs(int Co, int C, int K);
 size_t tc3_section_bytes(int Co, int C);
 // Writes the section from OIHW weights of any supported dtype.
 sf_status tc3_pack(const void* w_oihw, int src_dtype, int Co, int C, void* section, cudaStream_t st);
-// Runs the convolution; SF_ERR_UNSUPPORTED for shapes it does not take.
+// Whether the kernel can run this shape (shared memory, TMEM, 32-bit
+// position decode); run_conv3x3_tc returns SF_ERR_UNSUPPORTED otherwise.
+bool tc3_supported(int N, int C, int H, int W, int Co);
+// Runs the convolution (when `gate` selects it).
 sf_status run_conv3x3_tc(const void* x, const void* w_gather, int cpl, const void* section, const float* bias,
                          void* y, uint32_t* err, int N, int C, int H, int W, int Co, int xdt, int wdt,
-                         cudaStream_t st);
+                         cudaStream_t st, const Gate& gate);
 
 }  // namespace c3tc
 }  // namespace sf

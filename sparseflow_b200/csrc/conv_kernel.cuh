@@ -118,6 +118,7 @@ struct ConvParams {
   uint32_t w_cob_bytes;  // bytes of one output-channel block of packed weights (WSMEM kernels)
   int tma_store;         // 1: epilogue tiles leave through TMA tensor stores (y map)
   int w_off, stg_off, bar_off;  // byte offsets in dynamic smem
+  Gate gate;                    // runs only when the gate selects this path
 };
 
 struct Plan {
@@ -326,6 +327,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // the correctly rounded value of one real number) and the LIF epilogue
   // carries no division code.
   constexpr bool TAU_POW2 = MODE >= 3;
+  if (!gate_open(p.gate)) return;  // uniform across the grid: before any barrier
   extern __shared__ __align__(128) unsigned char smem[];
   constexpr int KK = K * K;
   constexpr int QN = (R - 1) * S + K;  // input columns a row segment reads

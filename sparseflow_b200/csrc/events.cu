@@ -31,7 +31,8 @@ template <typename XT, int VEC, bool FLAT>
 __global__ void __launch_bounds__(kEvThreads) spike_masks_kernel(const XT* __restrict__ x, int C, int HW, int nw,
                                                                  long long nimg,
                                                                  unsigned long long* __restrict__ masks,
-                                                                 uint32_t* __restrict__ flags) {
+                                                                 uint32_t* __restrict__ flags, const Gate gate) {
+  if (!gate_open(gate)) return;
   const int word = blockIdx.y;
   const int vpi = HW / VEC;  // vectors per image
   long long img;
@@ -97,7 +98,7 @@ __global__ void __launch_bounds__(kEvThreads) spike_masks_kernel(const XT* __res
 
 template <typename XT>
 sf_status launch(const void* x, int nimg, int C, int HW, unsigned long long* masks, uint32_t* flags,
-                 cudaStream_t st) {
+                 cudaStream_t st, const Gate& gate) {
   const int nw = (C + 63) / 64;
   constexpr int V = 16 / (int)sizeof(XT);
   const bool vec = aligned16(x) && HW % V == 0;
@@ -107,31 +108,76 @@ sf_status launch(const void* x, int nimg, int C, int HW, unsigned long long* mas
   if (vpi >= kEvThreads && nimg <= 65535) {
     const dim3 grid((vpi + kEvThreads - 1) / kEvThreads, nw, (unsigned)nimg);
     if (vec)
-      spike_masks_kernel<XT, V, false><<<grid, kEvThreads, 0, st>>>(xp, C, HW, nw, nimg, masks, flags);
+      spike_masks_kernel<XT, V, false><<<grid, kEvThreads, 0, st>>>(xp, C, HW, nw, nimg, masks, flags, gate);
     else
-      spike_masks_kernel<XT, 1, false><<<grid, kEvThreads, 0, st>>>(xp, C, HW, nw, nimg, masks, flags);
+      spike_masks_kernel<XT, 1, false><<<grid, kEvThreads, 0, st>>>(xp, C, HW, nw, nimg, masks, flags, gate);
   } else {
     const long long blocks = ((long long)nimg * vpi + kEvThreads - 1) / kEvThreads;
     if (blocks > 0x7fffffffll) return SF_ERR_UNSUPPORTED;
     const dim3 grid((unsigned)blocks, nw, 1);
     if (vec)
-      spike_masks_kernel<XT, V, true><<<grid, kEvThreads, 0, st>>>(xp, C, HW, nw, nimg, masks, flags);
+      spike_masks_kernel<XT, V, true><<<grid, kEvThreads, 0, st>>>(xp, C, HW, nw, nimg, masks, flags, gate);
     else
-      spike_masks_kernel<XT, 1, true><<<grid, kEvThreads, 0, st>>>(xp, C, HW, nw, nimg, masks, flags);
+      spike_masks_kernel<XT, 1, true><<<grid, kEvThreads, 0, st>>>(xp, C, HW, nw, nimg, masks, flags, gate);
   }
   return cudaGetLastError() == cudaSuccess ? SF_OK : SF_ERR_CUDA;
 }
 
 }  // namespace
 
-size_t event_workspace_bytes(long long nimg, int C, int HW) {
+static size_t event_core_bytes(long long nimg, int C, int HW) {
   const size_t nw = (size_t)(C + 63) / 64;
   const size_t mask_bytes = (size_t)nimg * HW * nw * 8;
   return ((mask_bytes + 255) / 256) * 256 + (((size_t)nimg * 4 + 255) / 256) * 256;
 }
 
+size_t event_workspace_bytes(long long nimg, int C, int HW) { return event_core_bytes(nimg, C, HW) + 256; }
+
+uint32_t* event_count_word(void* workspace, long long nimg, int C, int HW) {
+  return reinterpret_cast<uint32_t*>(static_cast<char*>(workspace) + event_core_bytes(nimg, C, HW));
+}
+
+namespace {
+template <typename XT>
+__global__ void __launch_bounds__(1024) sample_nonzeros_kernel(const XT* __restrict__ x, long long n, int samples,
+                                                                uint32_t* count) {
+  __shared__ uint32_t warp_cnt[32];
+  const long long stride = max(1ll, n / samples);
+  uint32_t c = 0;
+  for (int i = threadIdx.x; i < samples; i += 1024) {
+    const long long idx = (long long)i * stride;
+    if (idx < n) c += DT<XT>::nz_bit(x[idx]);
+  }
+  for (int o = 16; o; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+  if ((threadIdx.x & 31) == 0) warp_cnt[threadIdx.x >> 5] = c;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    c = warp_cnt[threadIdx.x];
+    for (int o = 16; o; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+    if (threadIdx.x == 0) *count = c;
+  }
+}
+}  // namespace
+
+sf_status sample_nonzeros(const void* x, int xdt, long long n, int samples, uint32_t* count, cudaStream_t st) {
+  switch (xdt) {
+    case SF_DTYPE_F32:
+      sample_nonzeros_kernel<float><<<1, 1024, 0, st>>>(static_cast<const float*>(x), n, samples, count);
+      break;
+    case SF_DTYPE_F16:
+      sample_nonzeros_kernel<__half><<<1, 1024, 0, st>>>(static_cast<const __half*>(x), n, samples, count);
+      break;
+    case SF_DTYPE_BF16:
+      sample_nonzeros_kernel<__nv_bfloat16><<<1, 1024, 0, st>>>(static_cast<const __nv_bfloat16*>(x), n, samples,
+                                                                  count);
+      break;
+    default: return SF_ERR_INVALID_ARG;
+  }
+  return cudaGetLastError() == cudaSuccess ? SF_OK : SF_ERR_CUDA;
+}
+
 sf_status extract_events(const void* x, int xdt, long long nimg, int C, int HW, void* workspace,
-                         size_t workspace_bytes, EventBuffers& out, cudaStream_t st) {
+                         size_t workspace_bytes, EventBuffers& out, cudaStream_t st, const Gate& gate) {
   if (workspace_bytes < event_workspace_bytes(nimg, C, HW)) return SF_ERR_WORKSPACE;
   if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return SF_ERR_ALIGNMENT;
   const size_t nw = (size_t)(C + 63) / 64;
@@ -141,9 +187,9 @@ sf_status extract_events(const void* x, int xdt, long long nimg, int C, int HW, 
   out.nw = (int)nw;
   if (cudaMemsetAsync(out.flags, 0, (size_t)nimg * 4, st) != cudaSuccess) return SF_ERR_CUDA;
   switch (xdt) {
-    case SF_DTYPE_F32: return launch<float>(x, (int)nimg, C, HW, out.masks, out.flags, st);
-    case SF_DTYPE_F16: return launch<__half>(x, (int)nimg, C, HW, out.masks, out.flags, st);
-    case SF_DTYPE_BF16: return launch<__nv_bfloat16>(x, (int)nimg, C, HW, out.masks, out.flags, st);
+    case SF_DTYPE_F32: return launch<float>(x, (int)nimg, C, HW, out.masks, out.flags, st, gate);
+    case SF_DTYPE_F16: return launch<__half>(x, (int)nimg, C, HW, out.masks, out.flags, st, gate);
+    case SF_DTYPE_BF16: return launch<__nv_bfloat16>(x, (int)nimg, C, HW, out.masks, out.flags, st, gate);
   }
   return SF_ERR_INVALID_ARG;
 }

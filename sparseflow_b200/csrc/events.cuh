@@ -10,11 +10,18 @@ struct EventBuffers {
   int nw;                     // 64-bit words per pixel
 };
 
-// Workspace bytes for nimg images of C channels and HW pixels.
+// Workspace bytes for nimg images of C channels and HW pixels: masks, flags,
+// and one 256-byte slot for the sampled nonzero count (event_count_word).
 size_t event_workspace_bytes(long long nimg, int C, int HW);
+uint32_t* event_count_word(void* workspace, long long nimg, int C, int HW);
 
-// Fills `out` (carved from `workspace`) for x (NCHW, nimg images) on `st`.
+// Fills `out` (carved from `workspace`) for x (NCHW, nimg images) on `st`;
+// the mask kernel runs only when `gate` selects it.
 sf_status extract_events(const void* x, int xdt, long long nimg, int C, int HW, void* workspace,
-                         size_t workspace_bytes, EventBuffers& out, cudaStream_t st);
+                         size_t workspace_bytes, EventBuffers& out, cudaStream_t st, const Gate& gate);
+
+// Writes to *count the number of nonzeros among `samples` elements of x
+// (n elements) taken at a fixed stride: one CTA, a few microseconds.
+sf_status sample_nonzeros(const void* x, int xdt, long long n, int samples, uint32_t* count, cudaStream_t st);
 
 }  // namespace sf

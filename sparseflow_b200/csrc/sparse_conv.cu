@@ -210,6 +210,17 @@ size_t tc_section_offset(int c_out, int c_in, int kernel, int wsz) {
   return (gather_bytes(c_out, c_in, kernel, wsz) + 255) & ~(size_t)255;
 }
 
+// Spike density below which the gather kernel beats the tensor-core kernel
+// for 3x3/s1 layers of C_in input channels (0: the tensor cores always win).
+// Crossovers measured on the C5 grid (1024 images of 14x14 / 28x28 / 56x56,
+// one B200): C_in 64 none (tensor cores 2.8-4.4x cuDNN at every density);
+// C_in 128 between 0.1 % and 1 %; C_in 256 and 512 between 1 % and 5 %.
+double tc3_min_density(int C) {
+  if (C <= c3tc::kTcResidentMaxC) return 0.0;
+  return C <= 160 ? 0.004 : 0.015;
+}
+constexpr int kDensitySamples = 32768;
+
 // Stage 1 + stage 2 for T*N images; the LIF variant when lif is set.
 // masks_in: events of x precomputed by a fused conv + LIF (binary spikes;
 // x itself is then not read). mask_out: LIF only, the output spikes' events.
@@ -230,16 +241,33 @@ sf_status run_conv(const void* x, const void* w_packed, const float* bias, void*
     if (s != SF_ERR_UNSUPPORTED) return s;
   }
   // 3x3 stride 1: integer tcgen05 implicit GEMM over x streamed once
-  // (conv3x3_tc.cu), unless the policy asks for the gather kernel.
-  if (!lif && !masks_in && K == 3 && S == 1 && P == 1 && policy(SF_POLICY_CONV3X3_PATH) != 1 &&
-      c3tc::tc3_packs(Co, C, K)) {
+  // (conv3x3_tc.cu), unless the policy asks for the gather kernel. Its cost
+  // does not depend on the spike density; the gather kernel's does. For
+  // C_in <= 64 the tensor-core kernel is faster at every density; above, the
+  // gather kernel wins on sparse enough inputs, so a sampled nonzero count
+  // picks one of the two paths on the device (both are launched; the other
+  // returns at entry).
+  const int pol3 = (int)policy(SF_POLICY_CONV3X3_PATH);
+  Gate gate{nullptr, 0u, 0};
+  bool tc_after = false;
+  if (!lif && !masks_in && K == 3 && S == 1 && P == 1 && pol3 != 1 && c3tc::tc3_packs(Co, C, K) &&
+      (wdt == SF_DTYPE_F32 || wdt == SF_DTYPE_BF16) && c3tc::tc3_supported(T * N, C, H, W, Co)) {
     uint32_t* err = nullptr;
     if (cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_conv_error) != cudaSuccess) return SF_ERR_CUDA;
-    const int wsz = (int)dtype_size(wdt);
-    const void* section = static_cast<const char*>(w_packed) + tc_section_offset(Co, C, K, wsz);
-    s = c3tc::run_conv3x3_tc(x, w_packed, weight_block_cpl(C, K, Co, wsz), section, bias, y, err, T * N, C, H, W,
-                             Co, xdt, wdt, st);
-    if (s != SF_ERR_UNSUPPORTED) return s;
+    const double rho = tc3_min_density(C);
+    if (pol3 == 2 || rho <= 0.0) {
+      const int wsz = (int)dtype_size(wdt);
+      const void* section = static_cast<const char*>(w_packed) + tc_section_offset(Co, C, K, wsz);
+      return c3tc::run_conv3x3_tc(x, w_packed, weight_block_cpl(C, K, Co, wsz), section, bias, y, err, T * N, C,
+                                  H, W, Co, xdt, wdt, st, gate);
+    }
+    const long long nimg = (long long)T * N;
+    if (ws_bytes < event_workspace_bytes(nimg, C, H * W)) return SF_ERR_WORKSPACE;
+    uint32_t* count = event_count_word(workspace, nimg, C, H * W);
+    s = sample_nonzeros(x, xdt, nimg * C * H * W, kDensitySamples, count, st);
+    if (s != SF_OK) return s;
+    gate = Gate{count, (uint32_t)std::ceil(rho * kDensitySamples), 1};
+    tc_after = true;
   }
   // 1x1 stride 2: one pass over x with masks built in shared memory
   // (pointwise.cu). For stride 1 that kernel measured slower than the two
@@ -263,7 +291,7 @@ sf_status run_conv(const void* x, const void* w_packed, const float* bias, void*
     ev.nw = nw;
     if (cudaGetSymbolAddress(reinterpret_cast<void**>(&ev.flags), g_zero_flags) != cudaSuccess) return SF_ERR_CUDA;
   } else {
-    s = extract_events(x, xdt, (long long)T * N, C, H * W, workspace, ws_bytes, ev, st);
+    s = extract_events(x, xdt, (long long)T * N, C, H * W, workspace, ws_bytes, ev, st, gate);
     if (s != SF_OK) return s;
   }
   if (mask_out && Co % 64 != 0) {
@@ -332,7 +360,15 @@ sf_status run_conv(const void* x, const void* w_packed, const float* bias, void*
     p.inv_tau = pow2 ? 1.f / p.tau : 0.f;
     mode = (mask_out ? 2 : 1) + (pow2 ? 2 : 0);
   }
-  return dispatch(mode, xdt, wdt, K, S, p, ym, grid_used, pl, st);
+  p.gate = gate;
+  s = dispatch(mode, xdt, wdt, K, S, p, ym, grid_used, pl, st);
+  if (s != SF_OK || !tc_after) return s;
+  uint32_t* err = nullptr;
+  if (cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_conv_error) != cudaSuccess) return SF_ERR_CUDA;
+  const int wsz = (int)dtype_size(wdt);
+  const void* section = static_cast<const char*>(w_packed) + tc_section_offset(Co, C, K, wsz);
+  return c3tc::run_conv3x3_tc(x, w_packed, weight_block_cpl(C, K, Co, wsz), section, bias, y, err, T * N, C, H, W,
+                              Co, xdt, wdt, st, Gate{gate.count, gate.thr, 2});
 }
 
 }  // namespace

@@ -123,3 +123,18 @@ def test_tc3x3_full_size_c5_cell_vs_cudnn_fp32():
     assert (y - ref).abs().max().item() <= RTOL * ref.abs().max().item()
     from sparseflow_b200 import _lib
     assert _lib.conv_status(x.device) == 0
+
+
+@pytest.mark.parametrize("c,density,expect", [(128, 0.0005, 1), (128, 0.05, 2), (256, 0.005, 1), (256, 0.1, 2)])
+def test_density_gate_picks_one_path(c, density, expect):
+    """For C_in > 64 a sampled nonzero count picks the gather kernel (sparse inputs) or the
+    tensor-core kernel on the device; the automatic result equals that path's bit for bit."""
+    g = torch.Generator().manual_seed(c + int(density * 1e4))
+    x = (torch.rand(8, c, 14, 14, generator=g) < density).float().cuda()
+    wt = (torch.randn(c, c, 3, 3, generator=g) * 0.05).cuda()
+    b = torch.randn(c, generator=g).cuda()
+    auto = _run(x, wt, b, 0)
+    forced = _run(x, wt, b, expect)
+    other = _run(x, wt, b, 3 - expect)
+    assert torch.equal(auto, forced)
+    _close(auto.cpu().numpy(), other.cpu().numpy())

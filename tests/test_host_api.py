@@ -166,7 +166,8 @@ def test_native_argument_checks_without_gpu():
     # C_in > 64: 32-channel output blocks (N = 96), digit image [4 blocks][9][8 slices][96][16]
     assert lib.sf_packed_weight_bytes(128, 128, 3, 0) == 128 * 9 * 128 * 4 + 3 * 128 * 4 + 4 * 9 * 8 * 96 * 16
     cd = _lib.ConvDesc(2, 64, 56, 56, 64, 56, 56, 3, 1, 1, 0, 0, 1)
-    assert lib.sf_sparse_conv2d_workspace_size(ctypes.byref(cd)) == 2 * 56 * 56 * 8 + 256
+    # masks (8 B per pixel), one flag per image (256-byte slot), one sampled-count slot
+    assert lib.sf_sparse_conv2d_workspace_size(ctypes.byref(cd)) == 2 * 56 * 56 * 8 + 256 + 256
 
 
 def test_optimize_turns_on_event_masks_for_sources_of_replaced_convs(monkeypatch):
