@@ -290,22 +290,20 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const XT* __restr
       tc::tmem_ld8(ta + (uint32_t)(2 * p.CB), r2);
       tc::tmem_wait_ld();
       if (valid) {
-        // |D| < 2^22, so adding 1.5 * 2^23 to the bits gives the float
-        // 1.5 * 2^23 + D exactly (no conversion instruction); the scaled
-        // digit sums are then exact, and only their sum rounds.
+        // D0 * 256 + D1 is exact in int32 (|D0| <= 64 * 9 * C_in, |D1| <=
+        // 128 * 9 * C_in) and converts with one rounding (none below 2^24,
+        // e.g. always for C_in <= 64); |D2| < 2^22, so adding 1.5 * 2^23 to
+        // its bits gives the float 1.5 * 2^23 + D2 exactly. Then the sum and
+        // the scaling round.
 #pragma unroll
         for (int e = 0; e < 8; e += 2) {
           if (c8 + e >= nco) break;
           const float4 sb = tb[(c8 + e) >> 1];
 #pragma unroll
           for (int f = 0; f < 2; ++f) {
-            const float a0 = __int_as_float((int)r0[e + f] + 0x4B400000);
-            const float a1 = __int_as_float((int)r1[e + f] + 0x4B400000);
-            const float a2 = __int_as_float((int)r2[e + f] + 0x4B400000);
-            const float x0 = fmaf(a0, 65536.f, -12582912.f * 65536.f);
-            const float x1 = fmaf(a1, 256.f, -12582912.f * 256.f);
-            const float x2 = a2 - 12582912.f;
-            const float v = fmaf(f ? sb.z : sb.x, (x0 + x1) + x2, f ? sb.w : sb.y);
+            const float x01 = __int2float_rn((int)r0[e + f] * 256 + (int)r1[e + f]);
+            const float x2 = __int_as_float((int)r2[e + f] + 0x4B400000) - 12582912.f;
+            const float v = fmaf(f ? sb.z : sb.x, fmaf(x01, 256.f, x2), f ? sb.w : sb.y);
             // Evict-first stores: y is not read again here (1.7 % faster on the C5 cell).
             if (c8 + e + f < nco) st_cs(yp + (uint32_t)(c8 + e + f) * (uint32_t)HW, DT<XT>::from_f(v));
           }
