@@ -223,6 +223,19 @@ def run_reference(args):
         pg.destroy_process_group()
 
 
+def masks_of(x4):
+    """Event masks of a binary NCHW tensor in the layout a spike producer writes:
+    [n][h][w][ceil(C/64)] 64-bit words, bit c % 64 of word c // 64 set iff channel c is nonzero."""
+    n, c, h, w = x4.shape
+    nw = (c + 63) // 64
+    pad = torch.zeros(n, nw * 64, h, w, dtype=torch.bool, device=x4.device)
+    pad[:, :c] = x4 != 0
+    out = torch.zeros(n, h, w, nw, dtype=torch.int64, device=x4.device)
+    for b in range(64):
+        out |= pad[:, b::64].permute(0, 2, 3, 1).to(torch.int64) << b
+    return out.contiguous()
+
+
 def extras(dev, hbm_peak, steps):
     """Side measurements: prescan GB/s, C2 1x1 bf16, C3 fused conv+BN+LIF, cuDNN comparisons."""
     from sparseflow_b200.Kernels._prescan_common import prescan2d
@@ -282,6 +295,23 @@ def extras(dev, hbm_peak, steps):
     out["c2_conv1x1_bf16w"] = {"GBps": round(b2 / ms / 1e6, 1), "frac_of_measured_hbm": round(b2 / ms / 1e6 / hbm_peak, 3),
                                "ms": round(ms, 4), "cudnn_ms": round(cud, 4), "speedup_vs_cudnn": round(cud / ms, 2),
                                "density": round(float((x2 != 0).float().mean()), 5)}
+    # The same layer as it runs inside a network: its input spikes come from a LIF node that hands
+    # over their event masks (LIFNode.emit_event_masks), so the tcgen05 kernel builds its A operand
+    # from the masks (32 bytes per pixel) instead of reading 1 KB of fp32 spikes. The masks are
+    # built here, outside the timed region, as that producer would have written them.
+    from sparseflow_b200 import _lib
+    m2 = masks_of(x2f)
+    y2 = torch.empty(n2, 64, 56, 56, device=dev)
+    wp2 = _lib.pack_weights(conv2.weight, torch.bfloat16)
+    msk = cuda_time(lambda: _lib.sparse_conv2d_from_masks(m2, tuple(x2f.shape), x2f.dtype, wp2, None, y2, 1, 1, 0),
+                    steps, 3) / steps
+    ref2 = torch.nn.functional.conv2d(x2f, wf)
+    bm = m2.numel() * 8 + n2 * 64 * 56 * 56 * 4 + 64 * 256 * 2
+    out["c2_conv1x1_bf16w_from_producer_masks"] = {
+        "ms": round(msk, 4), "cudnn_ms": round(cud, 4), "speedup_vs_cudnn": round(cud / msk, 2),
+        "GBps": round(bm / msk / 1e6, 1), "frac_of_measured_hbm": round(bm / msk / 1e6 / hbm_peak, 3),
+        "bytes": bm, "max_rel_err_vs_cudnn_fp32": float((y2 - ref2).abs().max() / ref2.abs().max())}
+    del m2, y2, ref2
     del x2, x2f
 
     # C3: fused conv3x3 + BN-fold + LIF, T16 N64 C128 28x28, Bernoulli(0.005).

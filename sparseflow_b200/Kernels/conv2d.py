@@ -63,17 +63,17 @@ def pack_weight(weight: torch.Tensor) -> torch.Tensor:
 def uses_event_masks(c_in: int, h_in: int, w_in: int, kernel_size: int, stride: int, padding: int) -> bool:
     """Whether a convolution handed its input's event masks runs from them.
 
-    1x1/s2 has no mask-driven kernel. The tensor-core kernels read the spikes
-    themselves faster than the gather kernel reads masks: 1x1/s1 on images of
-    at least one 128-pixel MMA tile, and 3x3/s1 with C_in <= 64 (measured on
-    the C64 56x56 cell: 0.38 ms from the spikes against 0.46 ms for the
-    gather kernel from masks; 0.027 against 0.06 ms on 8x8 maps)."""
+    1x1/s2 has no mask-driven kernel. 1x1/s1 always does: on images of at
+    least one 128-pixel MMA tile the tcgen05 kernel builds its A operand from
+    the masks (32 bytes per pixel for 256 channels instead of 1 KB of fp32
+    spikes; C2 cell 0.34 ms from the spikes), on smaller images the gather
+    kernel reads them. The 3x3/s1 tensor-core kernel with C_in <= 64 reads the
+    spikes faster than the gather kernel reads masks (C64 56x56: 0.37 ms
+    against 0.46 ms; 8x8 maps: 0.027 against 0.06 ms), so those layers ignore
+    them."""
     if (kernel_size, stride) == (1, 2):
         return False
     lib = _lib.load()
-    if kernel_size == 1 and stride == 1 and lib.sf_get_path_policy(_lib.SF_POLICY_CONV1X1_PATH) == 0 and \
-            h_in * w_in >= lib.sf_get_path_policy(_lib.SF_POLICY_CONV1X1_TC_MIN_HW):
-        return False
     if (kernel_size, stride, padding) == (3, 1, 1) and c_in <= TC3X3_MAX_CIN and \
             lib.sf_get_path_policy(_lib.SF_POLICY_CONV3X3_PATH) != 1:
         return False

@@ -39,6 +39,7 @@
 // before the CTA exits.
 #include <cudaTypedefs.h>
 #include <cstdlib>
+#include <cstring>
 #include "conv_kernel.cuh"
 #include "policy.cuh"
 
@@ -56,7 +57,9 @@ constexpr int kThreads = (kMmaWarp + 1) * 32;
 constexpr int kM = 128;       // pixels per tile = MMA M = TMEM lanes
 constexpr int kKC = 64;       // channels per chunk (one 128-byte swizzle row of bf16)
 constexpr int kMaxStages = 6; // staging ring (as many as shared memory allows)
-constexpr int kASlots = 4;    // bf16 A ring
+constexpr int kASlots = 4;    // bf16 A ring (16 KB chunks) when x is streamed
+constexpr int kASlotsMasks = 8;  // ... and when A comes from masks (cheap to build: the ring depth
+                                 // then decides how many chunk round trips overlap)
 constexpr int kMaxD = 4;      // TMEM accumulators (as many as 512 columns hold)
 
 struct TcParams {
@@ -72,6 +75,11 @@ struct TcParams {
   long long ntiles, tiles_per_cta;
   uint32_t stage_bytes, a_bytes, b_plane_bytes;
   uint32_t tmem_cols;
+  // Mask-fed mode: the spikes' nonzero-channel masks ([image][pixel][nw]
+  // 64-bit words, as a spike producer writes them) instead of x.
+  const unsigned long long* masks;
+  int nw;
+  int aslots;  // 16 KB A chunks in the ring: kASlots, or up to kASlotsMasks in mask-fed mode
 };
 
 __device__ __forceinline__ void tma_load_3d(void* dst_smem, const CUtensorMap* map, int c0, int c1, int c2,
@@ -88,6 +96,12 @@ __device__ __forceinline__ void tma_load_3d(void* dst_smem, const CUtensorMap* m
 // 8-row (1024 B) atom the 16-byte chunk c of row r sits at chunk c ^ (r % 8).
 __device__ __forceinline__ uint32_t sw128(int row, int k, int rows) {
   return (uint32_t)((k >> 6) * rows * 128 + row * 128 + ((((k & 63) >> 3) ^ (row & 7)) << 4) + (k & 7) * 2);
+}
+
+__device__ __forceinline__ void st_cs(float* p, float v) { __stcs(p, v); }
+__device__ __forceinline__ void st_cs(__half* p, __half v) { __stcs(reinterpret_cast<unsigned short*>(p), __half_as_ushort(v)); }
+__device__ __forceinline__ void st_cs(__nv_bfloat16* p, __nv_bfloat16 v) {
+  __stcs(reinterpret_cast<unsigned short*>(p), __bfloat16_as_ushort(v));
 }
 
 // tcgen05 shared-memory descriptor: K-major, 128-byte swizzle, 8-row atoms
@@ -149,20 +163,25 @@ __device__ __forceinline__ float packed_w(const TcParams& p, int co, int ci) {
 
 struct Bars {
   uint64_t s_full[kMaxStages], s_empty[kMaxStages];
-  uint64_t a_full[kASlots], a_empty[kASlots];
+  uint64_t a_full[kASlotsMasks], a_empty[kASlotsMasks];
   uint64_t d_full[kMaxD], d_empty[kMaxD];
   uint32_t tmem_base;
-  uint32_t a_nz[kASlots][kConvWarps];  // per converter warp: its part of the chunk has a nonzero
+  uint32_t a_nz[kASlotsMasks][kConvWarps];  // per converter warp: its part of the chunk has a nonzero
   uint32_t odd[kMaxD];                  // = i + 1 when tile i (in D[b]) holds a value that is not exactly a bf16
+  float bias_s[256];                    // bias (0 without one), read by the epilogue as a broadcast
 };
 
 // SUB: MMA sub-tiles of 128 pixels per tile. Two make each TMA row 1 KB
 // (256 pixels) instead of 512 B.
-template <typename XT, typename WT, int SUB>
+// MASKS: A comes from the masks (bit c of a pixel's word = channel c is a
+// spike, i.e. exactly 1.0): a stage holds one tile's words for all channels
+// (kTile pixels x nw x 8 bytes, one bulk copy) and serves every chunk.
+template <typename XT, typename WT, int SUB, bool MASKS>
 __global__ void __launch_bounds__(kThreads, 1)
     pointwise_tc_kernel(const TcParams p, const __grid_constant__ CUtensorMap xmap) {
   constexpr int kTile = kM * SUB;          // pixels per tile
-  constexpr int kSlots = kASlots / SUB;    // A ring (each slot SUB x 16 KB)
+  const int kSlots = p.aslots / SUB;  // A ring (each slot SUB x 16 KB); a power of two
+  const int kSlotShift = __ffs(kSlots) - 1;
   constexpr uint32_t kSubA = kM * kKC * 2; // bytes of one sub-tile's A chunk
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -194,6 +213,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     fence_mbar_init();
   }
+  for (int co = tid; co < 256; co += kThreads) bars->bias_s[co] = (p.bias != nullptr && co < p.Co) ? p.bias[co] : 0.f;
   if (warp == kMmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(&bars->tmem_base)),
@@ -238,16 +258,34 @@ __global__ void __launch_bounds__(kThreads, 1)
         const long long tile = t0 + i;
         const int img = (int)(tile / p.tiles_per_img);
         const int px0 = (int)(tile - (long long)img * p.tiles_per_img) * kTile;
-        for (int kc = 0; kc < KC; ++kc) {
+        if constexpr (MASKS) {
+          // One stage per tile: its pixels' words for all channels (a
+          // multiple of 16 bytes: H*W even, checked on the host).
           if (round > 0 && !mbar_wait_ns(&bars->s_empty[s], (round - 1) & 1u)) {
             failed = true;
             break;
           }
-          mbar_arrive_expect_tx(&bars->s_full[s], p.stage_bytes);
-          tma_load_3d(stage + (size_t)s * p.stage_bytes, &xmap, px0, kc * kKC, img, &bars->s_full[s]);
+          const int npx = min(kTile, p.HW - px0);
+          const uint32_t bytes = (uint32_t)npx * p.nw * 8u;
+          mbar_arrive_expect_tx(&bars->s_full[s], bytes);
+          bulk_g2s(stage + (size_t)s * p.stage_bytes, p.masks + ((size_t)img * p.HW + px0) * p.nw, bytes,
+                   &bars->s_full[s]);
           if (++s == p.nstages) {
             s = 0;
             ++round;
+          }
+        } else {
+          for (int kc = 0; kc < KC; ++kc) {
+            if (round > 0 && !mbar_wait_ns(&bars->s_empty[s], (round - 1) & 1u)) {
+              failed = true;
+              break;
+            }
+            mbar_arrive_expect_tx(&bars->s_full[s], p.stage_bytes);
+            tma_load_3d(stage + (size_t)s * p.stage_bytes, &xmap, px0, kc * kKC, img, &bars->s_full[s]);
+            if (++s == p.nstages) {
+              s = 0;
+              ++round;
+            }
           }
         }
       }
@@ -267,8 +305,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t d = tmem + (uint32_t)(b * SUB * p.Npad);
         uint32_t acc = 0u;
         for (int kc = 0; kc < KC; ++kc) {
-          const int g = i * KC + kc, a = g % kSlots;
-          if (!mbar_wait_ns(&bars->a_full[a], (uint32_t)((g / kSlots) & 1))) {
+          const int g = i * KC + kc, a = g & (kSlots - 1);
+          if (!mbar_wait_ns(&bars->a_full[a], (uint32_t)((g >> kSlotShift) & 1))) {
             failed = true;
             break;
           }
@@ -325,12 +363,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c0 = half * ncol; c0 < (half + 1) * ncol; c0 += 16) {
           float v[16];
           tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)((b * SUB + sb) * p.Npad + c0), v);
+          if (px < p.HW) {
+            // Row pointer advanced by adds; evict-first stores (y is not read again here).
+            XT* yq = yimg + (size_t)c0 * p.HW + px;
+            if (c0 + 16 <= p.Co) {
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const int co = c0 + e;
-            if (co < p.Co && px < p.HW) {
-              const float bv = p.bias ? __ldg(p.bias + co) : 0.f;
-              yimg[(size_t)co * p.HW + px] = DT<XT>::from_f(v[e] + bv);
+              for (int e = 0; e < 16; ++e, yq += p.HW) st_cs(yq, DT<XT>::from_f(v[e] + bars->bias_s[c0 + e]));
+            } else {
+#pragma unroll
+              for (int e = 0; e < 16; ++e, yq += p.HW)
+                if (c0 + e < p.Co) st_cs(yq, DT<XT>::from_f(v[e] + bars->bias_s[c0 + e]));
             }
           }
         }
@@ -361,59 +403,96 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t sround = 0;  // staging ring position, advanced incrementally
     for (int i = 0; i < nt; ++i) {
       const int b = i % p.nd;
+      const long long tile = t0 + i;
+      const int tile_px0 = (int)(tile - (tile / p.tiles_per_img) * p.tiles_per_img) * kTile;
       for (int kc = 0; kc < KC && !failed; ++kc) {
-        const int g = i * KC + kc, a = g % kSlots;
+        const int g = i * KC + kc, a = g & (kSlots - 1);
         if (!mbar_wait_ns(&bars->s_full[s], sround & 1u)) {
           failed = true;
           break;
         }
-        if (g >= kSlots && !mbar_wait_ns(&bars->a_empty[a], (uint32_t)(((g / kSlots) - 1) & 1))) {
+        if (g >= kSlots && !mbar_wait_ns(&bars->a_empty[a], (uint32_t)(((g >> kSlotShift) - 1) & 1))) {
           failed = true;
           break;
         }
-        const XT* st = reinterpret_cast<const XT*>(stage + (size_t)s * p.stage_bytes);  // [64][128]
-        unsigned char* ab = abuf + (size_t)a * p.a_bytes;
-        uint32_t nz = 0u, odd = 0u;
-        // Lane l takes pixels phalf*64 + l and + 32: conflict-free 4-byte reads,
-        // and each warp-wide 16-byte store covers all eight swizzle positions.
-        // The stage is released as soon as its values are in registers.
-        constexpr int kPP = kTile / 64;  // pixels per lane
-        float v[kPP][8];
+        if constexpr (MASKS) {
+          // Lane l takes pixels phalf*(kTile/2) + k*32 + l; warp octet o
+          // expands channels kc*64 + o*8 .. +7 of each: bit set -> bf16 1.0.
+          const unsigned long long* st = reinterpret_cast<const unsigned long long*>(stage + (size_t)s * p.stage_bytes);
+          unsigned char* ab = abuf + (size_t)a * p.a_bytes;
+          uint32_t orall = 0u;
+          constexpr int kPP = kTile / 64;
 #pragma unroll
-        for (int k = 0; k < kPP; ++k)
+          for (int k = 0; k < kPP; ++k) {
+            const int px = phalf * (kTile / 2) + k * 32 + lane;
+            const bool in = tile_px0 + px < p.HW;
+            const uint32_t byte = in ? (uint32_t)(st[(size_t)px * p.nw + kc] >> (o * 8)) & 0xffu : 0u;
+            orall |= byte;
+            uint4 qv;
+            uint32_t* qq = &qv.x;
 #pragma unroll
-          for (int e = 0; e < 8; ++e)
-            v[k][e] = DT<XT>::to_f(st[(o * 8 + e) * kTile + phalf * (kTile / 2) + k * 32 + lane]);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars->s_empty[s]);
-        if (++s == p.nstages) {
-          s = 0;
-          ++sround;
-        }
-        // The MMA is exact whenever every x is exactly a bf16 (then each
-        // product with a bf16 weight plane is exact in fp32): for the fp32
-        // bits u that means u & 0xffff == 0, tested on the OR of all values,
-        // which also gives "any nonzero". Such values convert by taking the
-        // high halves (a byte permute).
-        uint32_t orall = 0u;
-#pragma unroll
-        for (int k = 0; k < kPP; ++k) {
-          uint4 qv;
-          uint32_t* qq = &qv.x;
-#pragma unroll
-          for (int e = 0; e < 8; e += 2) {
-            const uint32_t u0 = __float_as_uint(v[k][e]), u1 = __float_as_uint(v[k][e + 1]);
-            orall |= u0 | u1;
-            qq[e / 2] = __byte_perm(u0, u1, 0x7632);
+            for (int e = 0; e < 4; ++e) {
+              const uint32_t b2 = (byte >> (2 * e)) & 3u;  // channels 2e, 2e+1 -> low, high bf16
+              qq[e] = (b2 & 1u) * 0x3f80u + (b2 >> 1) * 0x3f800000u;
+            }
+            *reinterpret_cast<uint4*>(ab + (px >> 7) * kSubA + sw128(px & (kM - 1), o * 8, kM)) = qv;
           }
-          const int px = phalf * (kTile / 2) + k * 32 + lane;  // pixel in the tile -> sub-tile, row
-          *reinterpret_cast<uint4*>(ab + (px >> 7) * kSubA + sw128(px & (kM - 1), o * 8, kM)) = qv;
-        }
-        nz = __any_sync(0xffffffffu, (orall & 0x7fffffffu) != 0u);
-        odd = __any_sync(0xffffffffu, (orall & 0xffffu) != 0u);
-        if (lane == 0) {
-          bars->a_nz[a][warp] = nz;
-          if (odd) bars->odd[b] = (uint32_t)(i + 1);  // tagged with the tile: no clearing needed
+          if (kc == KC - 1) {
+            // The stage served every chunk of this tile.
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->s_empty[s]);
+            if (++s == p.nstages) {
+              s = 0;
+              ++sround;
+            }
+          }
+          const uint32_t nz = __any_sync(0xffffffffu, orall != 0u);
+          if (lane == 0) bars->a_nz[a][warp] = nz;
+        } else {
+          const XT* st = reinterpret_cast<const XT*>(stage + (size_t)s * p.stage_bytes);  // [64][128]
+          unsigned char* ab = abuf + (size_t)a * p.a_bytes;
+          uint32_t nz = 0u, odd = 0u;
+          // Lane l takes pixels phalf*64 + l and + 32: conflict-free 4-byte reads,
+          // and each warp-wide 16-byte store covers all eight swizzle positions.
+          // The stage is released as soon as its values are in registers.
+          constexpr int kPP = kTile / 64;  // pixels per lane
+          float v[kPP][8];
+  #pragma unroll
+          for (int k = 0; k < kPP; ++k)
+  #pragma unroll
+            for (int e = 0; e < 8; ++e)
+              v[k][e] = DT<XT>::to_f(st[(o * 8 + e) * kTile + phalf * (kTile / 2) + k * 32 + lane]);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars->s_empty[s]);
+          if (++s == p.nstages) {
+            s = 0;
+            ++sround;
+          }
+          // The MMA is exact whenever every x is exactly a bf16 (then each
+          // product with a bf16 weight plane is exact in fp32): for the fp32
+          // bits u that means u & 0xffff == 0, tested on the OR of all values,
+          // which also gives "any nonzero". Such values convert by taking the
+          // high halves (a byte permute).
+          uint32_t orall = 0u;
+  #pragma unroll
+          for (int k = 0; k < kPP; ++k) {
+            uint4 qv;
+            uint32_t* qq = &qv.x;
+  #pragma unroll
+            for (int e = 0; e < 8; e += 2) {
+              const uint32_t u0 = __float_as_uint(v[k][e]), u1 = __float_as_uint(v[k][e + 1]);
+              orall |= u0 | u1;
+              qq[e / 2] = __byte_perm(u0, u1, 0x7632);
+            }
+            const int px = phalf * (kTile / 2) + k * 32 + lane;  // pixel in the tile -> sub-tile, row
+            *reinterpret_cast<uint4*>(ab + (px >> 7) * kSubA + sw128(px & (kM - 1), o * 8, kM)) = qv;
+          }
+          nz = __any_sync(0xffffffffu, (orall & 0x7fffffffu) != 0u);
+          odd = __any_sync(0xffffffffu, (orall & 0xffffu) != 0u);
+          if (lane == 0) {
+            bars->a_nz[a][warp] = nz;
+            if (odd) bars->odd[b] = (uint32_t)(i + 1);  // tagged with the tile: no clearing needed
+          }
         }
         fence_proxy_async_smem();
         __syncwarp();
@@ -447,7 +526,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encoder() {
 
 template <typename XT, typename WT>
 sf_status launch(TcParams p, const CUtensorMap& xmap, size_t smem, int sub, cudaStream_t st) {
-  auto kern = sub == 2 ? pointwise_tc_kernel<XT, WT, 2> : pointwise_tc_kernel<XT, WT, 1>;
+  auto kern = p.masks ? (sub == 2 ? pointwise_tc_kernel<XT, WT, 2, true> : pointwise_tc_kernel<XT, WT, 1, true>)
+                      : (sub == 2 ? pointwise_tc_kernel<XT, WT, 2, false> : pointwise_tc_kernel<XT, WT, 1, false>);
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return SF_ERR_CUDA;
   const long long ctas = std::min<long long>(p.ntiles, (long long)num_sms_current_device());
@@ -472,16 +552,26 @@ sf_status dispatch_w(int wdt, const TcParams& p, const CUtensorMap& xmap, size_t
 // every tile would be padding and the gather kernels measured faster), H*W
 // rows that TMA cannot address (H*W*element size not a multiple of 16, x not
 // 16-byte aligned), or operands beyond shared memory.
+// masks != nullptr: A comes from the spikes' event masks (x is not read;
+// H*W must be even so every tile's words are a 16-byte multiple).
 sf_status run_pointwise_tc(const void* x, const void* w_packed, const float* bias, void* y, uint32_t* err, int N,
-                           int C, int H, int W, int Co, int xdt, int wdt, cudaStream_t st) {
+                           int C, int H, int W, int Co, int xdt, int wdt, cudaStream_t st,
+                           const unsigned long long* masks) {
   if (Co > 256 || Co <= 0 || C <= 0 || C > 512) return SF_ERR_UNSUPPORTED;
   const int esz = (int)dtype_size(xdt);
   const long long HW = (long long)H * W;
   if (HW < policy(SF_POLICY_CONV1X1_TC_MIN_HW)) return SF_ERR_UNSUPPORTED;
-  if ((HW * esz) % 16 != 0 || (reinterpret_cast<uintptr_t>(x) & 15u) != 0) return SF_ERR_UNSUPPORTED;
+  if (masks) {
+    if (HW % 2 != 0 || (reinterpret_cast<uintptr_t>(masks) & 15u) != 0) return SF_ERR_UNSUPPORTED;
+  } else if ((HW * esz) % 16 != 0 || (reinterpret_cast<uintptr_t>(x) & 15u) != 0) {
+    return SF_ERR_UNSUPPORTED;
+  }
   auto enc = encoder();
-  if (!enc) return SF_ERR_UNSUPPORTED;
+  if (!enc && !masks) return SF_ERR_UNSUPPORTED;
   TcParams p;
+  memset(&p, 0, sizeof(p));
+  p.masks = masks;
+  p.nw = (C + 63) / 64;
   p.x = x;
   p.wp = w_packed;
   p.bias = bias;
@@ -502,8 +592,13 @@ sf_status run_pointwise_tc(const void* x, const void* w_packed, const float* bia
   auto plan = [&](int sub, size_t* smem_out) {
     const int nd = std::min(kMaxD, 512 / (sub * p.Npad));
     if (nd < 2) return false;
-    const size_t stage = (size_t)kKC * kM * sub * esz;
-    const size_t fixed = 1024 + (size_t)kASlots * kM * kKC * 2 + (size_t)p.nplanes * p.b_plane_bytes + sizeof(Bars);
+    const size_t stage = masks ? (size_t)kM * sub * p.nw * 8 : (size_t)kKC * kM * sub * esz;
+    size_t fixed = 0;
+    for (int aslots = masks ? kASlotsMasks : kASlots; aslots >= kASlots; aslots /= 2) {
+      fixed = 1024 + (size_t)aslots * kM * kKC * 2 + (size_t)p.nplanes * p.b_plane_bytes + sizeof(Bars);
+      p.aslots = aslots;
+      if (fixed + 2 * stage <= 232448) break;
+    }
     if (fixed + 2 * stage > 232448) return false;
     p.nd = nd;
     p.nstages = (int)std::min<size_t>(kMaxStages, (232448 - fixed) / stage);
@@ -527,6 +622,15 @@ sf_status run_pointwise_tc(const void* x, const void* w_packed, const float* bia
 
   // x as a 3-D tensor (pixels, channels, images); box = one chunk.
   CUtensorMap xmap;
+  memset(&xmap, 0, sizeof(xmap));
+  if (masks) {
+    switch (xdt) {
+      case SF_DTYPE_F32: return dispatch_w<float>(wdt, p, xmap, smem, sub, st);
+      case SF_DTYPE_F16: return dispatch_w<__half>(wdt, p, xmap, smem, sub, st);
+      case SF_DTYPE_BF16: return dispatch_w<__nv_bfloat16>(wdt, p, xmap, smem, sub, st);
+    }
+    return SF_ERR_INVALID_ARG;
+  }
   const CUtensorMapDataType dt = xdt == SF_DTYPE_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                  : xdt == SF_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                                        : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;

@@ -13,7 +13,8 @@
 namespace sf {
 namespace pwtc {
 sf_status run_pointwise_tc(const void* x, const void* w_packed, const float* bias, void* y, uint32_t* err, int N,
-                           int C, int H, int W, int Co, int xdt, int wdt, cudaStream_t st);
+                           int C, int H, int W, int Co, int xdt, int wdt, cudaStream_t st,
+                           const unsigned long long* masks = nullptr);
 }  // namespace pwtc
 namespace pw {
 sf_status run_pointwise(const void* x, const void* w_packed, const float* bias, void* y, int N, int C, int H,
@@ -234,10 +235,16 @@ sf_status run_conv(const void* x, const void* w_packed, const float* bias, void*
   if (!workspace && !masks_in) return SF_ERR_WORKSPACE;
   if (!aligned16(w_packed)) return SF_ERR_ALIGNMENT;
   // 1x1 stride 1: tcgen05 GEMM tiles over x streamed once (pointwise_tc.cu).
-  if (!lif && !masks_in && K == 1 && S == 1 && P == 0 && policy(SF_POLICY_CONV1X1_PATH) == 0) {
+  // With the spikes' event masks handed over (masks_in), the same kernel
+  // builds A from the masks and never reads x: with bf16 weights (one digit
+  // plane) that beats the gather kernel from the masks (C2 cell: 0.23-0.25 ms
+  // against 0.26-0.27 ms); with fp32 weights (three bf16 planes) it does not
+  // (0.33 against 0.26 ms), so those run the gather kernel.
+  if (!lif && K == 1 && S == 1 && P == 0 && policy(SF_POLICY_CONV1X1_PATH) == 0 &&
+      !(masks_in && wdt == SF_DTYPE_F32)) {
     uint32_t* err = nullptr;
     if (cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_conv_error) != cudaSuccess) return SF_ERR_CUDA;
-    s = pwtc::run_pointwise_tc(x, w_packed, bias, y, err, T * N, C, H, W, Co, xdt, wdt, st);
+    s = pwtc::run_pointwise_tc(x, w_packed, bias, y, err, T * N, C, H, W, Co, xdt, wdt, st, masks_in);
     if (s != SF_ERR_UNSUPPORTED) return s;
   }
   // 3x3 stride 1: integer tcgen05 implicit GEMM over x streamed once

@@ -66,23 +66,31 @@ def test_next_conv_runs_from_masks(c_mid, k2, hw):
         torch.testing.assert_close(y_tc, y_plain, rtol=1e-5, atol=1e-5)
 
 
-def test_1x1_on_large_images_ignores_masks():
-    """A 1x1/s1 layer on images of at least 128 pixels runs the tensor-core kernel from the spikes
-    themselves (faster there than the mask-driven gather kernel), with the attached masks unused."""
+def test_1x1_on_large_images_runs_from_masks_on_tensor_cores():
+    """A 1x1/s1 layer (bf16 weights) on images of at least 128 pixels given the producer's event
+    masks runs the tcgen05 kernel with its A operand built from the masks (x is not read): bit for
+    bit the result from the spikes, within 1e-5 of the float64 reference."""
     from sparseflow_b200.Ops.sparse_conv2d import SparseConv2d
-    g = torch.Generator().manual_seed(3)
-    x = (torch.rand(4, 2, 32, 12, 12, generator=g) < 0.1).float().cuda()
-    first = _fused(32, 72, 3, 9)
-    conv2 = nn.Conv2d(72, 48, 1, 1, 0)
-    conv2.weight.data = torch.randn(48, 72, 1, 1, generator=g) * 0.1
-    conv2 = conv2.cuda()
-    second = SparseConv2d.from_dense(conv2)
-    s = first(x)
-    assert getattr(s, "_sf_event_masks", None) is not None
-    y = second(s)
-    assert not second._last_used_event_masks
-    ref = torch.nn.functional.conv2d(s.reshape(8, 72, 12, 12).double(), conv2.weight.double(), conv2.bias.double())
-    torch.testing.assert_close(y.reshape(8, 48, 12, 12).double(), ref, rtol=1e-5, atol=1e-5)
+    for c_mid, hw in ((72, 12), (256, 16), (130, 14)):
+        g = torch.Generator().manual_seed(c_mid + hw)
+        x = (torch.rand(4, 2, 32, hw, hw, generator=g) < 0.1).float().cuda()
+        first = _fused(32, c_mid, 3, 9)
+        conv2 = nn.Conv2d(c_mid, 48, 1, 1, 0)
+        conv2.weight.data = (torch.randn(48, c_mid, 1, 1, generator=g) * 0.1).bfloat16().float()
+        conv2 = conv2.cuda().to(torch.bfloat16)  # bf16 weights: the tensor-core kernel runs from the masks
+        second = SparseConv2d.from_dense(conv2)
+        s = first(x)
+        assert getattr(s, "_sf_event_masks", None) is not None
+        y = second(s)
+        assert second._last_used_event_masks
+        y_plain = second(s.clone())
+        assert not second._last_used_event_masks
+        ref = torch.nn.functional.conv2d(s.reshape(8, c_mid, hw, hw).double(), conv2.weight.double(),
+                                         conv2.bias.double())
+        y = y.double()
+        y_plain = y_plain.double()
+        torch.testing.assert_close(y.reshape(8, 48, hw, hw), ref, rtol=1e-5, atol=1e-5)
+        torch.testing.assert_close(y, y_plain, rtol=0, atol=0)  # same kernel, same sums, same order
 
 
 def test_stale_masks_are_not_used():
