@@ -97,6 +97,7 @@ struct Params {
   // Streamed weights (C_in > 64): nA A buffers, nbs weight stages of kch
   // 16-channel slices of one tap of one 32-channel output block.
   int nA, nbs, kch;
+  int ngb;  // TMEM group buffers (2: the epilogue of a group overlaps the next one's MMAs)
   uint32_t b_off, bstage_bytes;
   Gate gate;  // runs only when the gate selects this path
 };
@@ -490,10 +491,11 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
           tc::fence_after();
           const uint32_t asa = smem_u32(abuf + (size_t)a * p.a_bytes);
           for (int cob = 0; cob < p.ncob && !failed; ++cob, ++g) {
-            const int gb = (int)(g & 1);
+            const int gb = p.ngb == 2 ? (int)(g & 1) : 0;
+            const long long gr = p.ngb == 2 ? (g >> 1) : g;  // uses of this buffer so far
             {
               PROF_T0();
-              if (g >= 2 && !tc::mbar_wait_sleep(&bars->d_empty[gb], (uint32_t)(((g >> 1) - 1) & 1))) {
+              if (g >= p.ngb && !tc::mbar_wait_sleep(&bars->d_empty[gb], (uint32_t)((gr - 1) & 1))) {
                 failed = true;
                 break;
               }
@@ -592,8 +594,9 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
         for (int cob = 0; cob < p.ncob && !failed; ++cob, ++g) {
           load_tab(cob);
           const int nco = min(cwq, p.Co - (cob * p.CB + cbeg));
-          const int gb = (int)(g & 1);
-          if (!tc::mbar_wait_sleep(&bars->d_full[gb], (uint32_t)((g >> 1) & 1))) {
+          const int gb = p.ngb == 2 ? (int)(g & 1) : 0;
+          const long long gr = p.ngb == 2 ? (g >> 1) : g;
+          if (!tc::mbar_wait_sleep(&bars->d_full[gb], (uint32_t)(gr & 1))) {
             failed = true;
             break;
           }
@@ -876,11 +879,14 @@ bool plan_tc(Params& p, size_t& smem_out, int N, int C, int H, int W, int Co) {
     p.kch = std::min(g.kcores, 8);
     while (g.kcores % p.kch) p.kch -= 2;
     p.bstage_bytes = (uint32_t)(p.kch * g.N3 * 16);
-    const int cand[4][2] = {{2, 2}, {2, 1}, {1, 2}, {1, 1}};
-    // Two tiles per unit halve the weight bytes per MMA, which bound the
-    // large layers, so they win even at the full 227 KB (C512 14x14: 2.9 ms
-    // with one tile per unit at 180 KB).
-    for (int ci = 0; ci < 4 && U == 0; ++ci) {
+    const int cand[6][2] = {{4, 2}, {4, 1}, {2, 2}, {2, 1}, {1, 2}, {1, 1}};
+    // More tiles per unit cut the weight bytes and the per-stage overhead per
+    // MMA, which bound these layers, so they win even at the full 227 KB
+    // (C512 14x14: 2.9 ms with one tile per unit at 180 KB, 2.2 ms with two).
+    // Four tiles of 96 columns leave TMEM room for one group only; that pays
+    // on maps of width >= 28 (C128 28x28: 0.547 against 0.588 ms) but not on
+    // 14x14 (C256: 0.67 against 0.58 ms).
+    for (int ci = (W >= 28 ? 0 : 2); ci < 6 && U == 0; ++ci) {
       for (size_t budget : {(size_t)200 * 1024, limit}) {
         for (int nbs = kMaxBStages; nbs >= 2 && U == 0; --nbs) {
           const int u = cand[ci][0], na = cand[ci][1];
@@ -917,8 +923,9 @@ bool plan_tc(Params& p, size_t& smem_out, int N, int C, int H, int W, int Co) {
     p.nunits = p.upcob * p.ncob;
   }
   p.fd_upcob = make_fastdiv((uint32_t)p.upcob);
+  p.ngb = (p.nbs > 0 && 2 * U * p.N3 > 512) ? 1 : 2;
   uint32_t cols = 32;
-  while (cols < (uint32_t)(2 * U * p.N3) && p.nbs > 0) cols <<= 1;
+  while (cols < (uint32_t)(p.ngb * U * p.N3) && p.nbs > 0) cols <<= 1;
   while (cols < (uint32_t)(2 * p.N3)) cols <<= 1;
   p.tmem_cols = cols;
   if (cols > 512) return false;
