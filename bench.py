@@ -60,9 +60,11 @@ def parse():
     ap.add_argument("--no-extra", action="store_true", help="skip the C2/C3/prescan side measurements")
     ap.add_argument("--only-timed", action="store_true",
                     help="run only the warm-up and timed steps (no cuDNN, e2e, extras or CPU baseline); for ncu")
-    ap.add_argument("--kernel", choices=["conv", "prescan", "c2", "c3", "lif", "lif_events", "c4"], default="conv",
+    ap.add_argument("--kernel", choices=["conv", "prescan", "c2", "c2masks", "c3", "lif", "lif_events", "c4"],
+                    default="conv",
                     help="with --only-timed: time the sparse conv (default), the prescan on the same input, "
-                         "the C2 1x1 cell (--images = T*N of C2, default 512), the C3 fused conv+LIF or the "
+                         "the C2 1x1 cell (--images = T*N of C2, default 512; c2masks: fed by the producer's "
+                         "event masks), the C3 fused conv+LIF or the "
                          "standalone LIF, without or with the event masks (--images = T*N, default 1024), or "
                          "the C4 Spiking-ResNet50 forward after optimize()")
     ap.add_argument("--sweep", action="store_true",
@@ -510,7 +512,7 @@ def main():
     mod.set_inference_mode(True)
     step_bytes = conv_bytes(n_img, C, H, W, C, H, W, 3)
 
-    if args.only_timed and args.kernel == "c2":
+    if args.only_timed and args.kernel in ("c2", "c2masks"):
         from sparseflow_b200.Ops.sparse_conv2d import SparseConv2d
         n2 = args.images if args.images != T_STEPS * N_BATCH else 512
         g2 = torch.Generator(device=dev).manual_seed(17 + rank)
@@ -523,10 +525,20 @@ def main():
         m2 = SparseConv2d.from_dense(conv2.to(dev).to(torch.bfloat16), block_size=16)
         m2.set_inference_mode(True)
         with torch.no_grad():
-            ms = cuda_time(lambda: m2(x2), args.steps, args.warmup, dist) / args.steps
+            if args.kernel == "c2masks":
+                from sparseflow_b200 import _lib
+                m2m = masks_of(x2)
+                y2 = torch.empty(n2, 64, 56, 56, device=dev)
+                wp2 = _lib.pack_weights(conv2.weight, torch.bfloat16)
+                ms = cuda_time(lambda: _lib.sparse_conv2d_from_masks(m2m, tuple(x2.shape), x2.dtype, wp2, None, y2,
+                                                                     1, 1, 0), args.steps, args.warmup, dist) / args.steps
+            else:
+                ms = cuda_time(lambda: m2(x2), args.steps, args.warmup, dist) / args.steps
         b2 = conv_bytes(n2, 256, 56, 56, 64, 56, 56, 1, wsz=2, bias=False)
+        if args.kernel == "c2masks":
+            b2 = m2m.numel() * 8 + n2 * 64 * 56 * 56 * 4 + 64 * 256 * 2
         if rank == 0:
-            print(json.dumps({"kernel": "c2", "ms_per_step": round(ms, 4), "GBps": round(b2 / ms / 1e6, 1),
+            print(json.dumps({"kernel": args.kernel, "ms_per_step": round(ms, 4), "GBps": round(b2 / ms / 1e6, 1),
                               "frac_of_measured_hbm": round(b2 / ms / 1e6 / hbm_peak, 3), "images": n2}))
         if dist is not None:
             dist.destroy_process_group()
