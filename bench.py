@@ -367,8 +367,51 @@ def extras(dev, hbm_peak, steps):
     chain["speedup"] = round(chain["plain_ms"] / chain["emit_ms"], 3)
     out["lif_events_to_conv"] = chain
     del xl
+    out["c1_conv3x3_small"] = c1_small(dev, hbm_peak, steps)
     out["c4_spiking_resnet50"] = c4_resnet(dev)
     return out
+
+
+def c1_small(dev, hbm_peak, steps, sets=8):
+    """C1: SparseConv2d 3x3/s1/p1 64->64 with bias on [T=4, N=8, 64, 32, 32]
+    Bernoulli(0.02) fp32 spikes, kaiming weights, block 16. One call is 16.9 MB, so `sets` input /
+    output pairs (135 MB, larger than L2) rotate between calls; cuDNN on the same rotation; the
+    reference CPU path (F.conv2d, all host threads) on the full C1 step."""
+    from oracle import oracle
+    from sparseflow_b200.Ops.sparse_conv2d import SparseConv2d
+    g = torch.Generator(device=dev).manual_seed(41)
+    conv = make_conv(64, 64, 3, 1, 1, True, 41, device=dev)
+    mod = SparseConv2d.from_dense(conv, block_size=16)
+    mod.set_inference_mode(True)
+    xs = [(torch.rand(4, 8, 64, 32, 32, device=dev, generator=g) < 0.02).float() for _ in range(sets)]
+    k = [0]
+
+    def step():
+        k[0] = (k[0] + 1) % sets
+        return mod(xs[k[0]])
+    n = max(steps, 50)
+    ms = cuda_time(step, n, 5) / n
+    x4 = [x.reshape(32, 64, 32, 32) for x in xs]
+
+    def cudnn_step():
+        k[0] = (k[0] + 1) % sets
+        return torch.nn.functional.conv2d(x4[k[0]], conv.weight, conv.bias, 1, 1)
+    cud = cuda_time(cudnn_step, n, 5) / n
+    nbytes = conv_bytes(32, 64, 32, 32, 64, 32, 32, 3)
+    conv_cpu = make_conv(64, 64, 3, 1, 1, True, 41, device="cpu")
+    xc = xs[0].reshape(32, 64, 32, 32).cpu()
+    torch.set_num_threads(os.cpu_count() or 1)
+    with torch.no_grad():
+        oracle.reference_cpu_conv2d(xc, conv_cpu.weight, conv_cpu.bias, 1, 1)
+        t0 = time.perf_counter()
+        for _ in range(20):
+            oracle.reference_cpu_conv2d(xc, conv_cpu.weight, conv_cpu.bias, 1, 1)
+        cpu_ms = (time.perf_counter() - t0) / 20 * 1e3
+    return {"ms": round(ms, 4), "GBps": round(nbytes / ms / 1e6, 1),
+            "frac_of_measured_hbm": round(nbytes / ms / 1e6 / hbm_peak, 3), "cudnn_ms": round(cud, 4),
+            "speedup_vs_cudnn": round(cud / ms, 2), "cpu_reference_ms": round(cpu_ms, 3),
+            "speedup_vs_cpu_reference": round(cpu_ms / ms, 1), "bytes": nbytes,
+            "note": f"{sets} rotating input/output sets (135 MB > L2); launch-bound at this size"}
 
 
 def c4_resnet(dev, iters=3):
@@ -746,6 +789,7 @@ def main():
                     "h2d_copy_GBps_per_rank": round(h2d_agg / world, 1)},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
+                         "frac_of_nominal_8TBps": round(achieved / 8000.0, 4),
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                          else "fallback 6650 GB/s",
                          "kernel": "one sf_sparse_conv2d call = conv3x3_tc_kernel<float,float,true> "
