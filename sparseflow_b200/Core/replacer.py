@@ -5,7 +5,8 @@ by dotted module name, for ``SparseConv2d.from_dense(conv, block_size, ...)``
 and attaches the reference's ``sf_*`` observability attributes
 (:122-154). Layers listed in ``static_zero_layers`` become
 ``StaticZeroConv2d`` (bias-only output, reference Ops/static_zero_conv2d.py).
-Targets of other families (linear, conv1d/3d, depthwise, attention, pools)
+Linear targets become ``SparseLinear`` (reference Core/replacer.py linear branch).
+Targets of other families (conv1d/3d, depthwise, attention, pools)
 have no kernel on the B200 path and are kept dense and counted as such.
 Returns ``(replaced, sparse_count, static_zero_count, dense_keep_count)``.
 """
@@ -17,9 +18,11 @@ import torch
 import torch.nn as nn
 
 from ..Ops.sparse_conv2d import SparseConv2d
+from ..Ops.sparse_linear import SparseLinear
 from .analyzer import ReplacementTarget, display_block_info
 
 _CONV2D_OPS = ("conv2d_3x3", "conv2d_1x1", "conv2d_3x3_s2")
+_LINEAR_OPS = ("linear",)
 _STATIC_ZERO_OPS = ("conv2d_3x3", "conv2d_1x1", "conv2d_3x3_s2")
 
 
@@ -109,7 +112,7 @@ class ModuleReplacer:
                 if self.verbose:
                     print(f"  [STATIC ] {t.conv_name} ({t.op_type}) -> StaticZeroConv2d")
                 continue
-            if only_static_zero or t.op_type not in _CONV2D_OPS:
+            if only_static_zero or t.op_type not in _CONV2D_OPS + _LINEAR_OPS:
                 dense_keep += 1
                 if self.verbose:
                     why = "DenseKeep" if only_static_zero else "DenseKeep (no B200 kernel for this op)"
@@ -128,6 +131,10 @@ class ModuleReplacer:
     def _create_sparse_module(self, target: ReplacementTarget, block: Optional[int],
                               sparse_kwargs: Dict[str, Any]) -> nn.Module:
         mod = target.conv_module
+        if target.op_type in _LINEAR_OPS:
+            lin = SparseLinear.from_dense(mod, threshold=float(sparse_kwargs.get("threshold", 1e-6)),
+                                          return_ms=bool(sparse_kwargs.get("return_ms", False)))
+            return lin.to(mod.weight.device)
         sparse = SparseConv2d.from_dense(mod, block_size=block,
                                          threshold=float(sparse_kwargs.get("threshold", 1e-6)),
                                          return_ms=bool(sparse_kwargs.get("return_ms", False)))

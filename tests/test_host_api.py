@@ -66,8 +66,10 @@ def test_analyzer_finds_spike_consumers_and_replacer_swaps(capsys):
     assert model[6].sf_operator_type == "conv2d_3x3_s2"
     assert model[9].sf_operator_type == "conv2d_1x1"
     assert model[3].sf_backend_mode == "sparse" and model[3].block_size == 8
+    # the classifier after the (transparent) average pool of the last spikes becomes SparseLinear
+    assert type(model[13]).__name__ == "SparseLinear" and model[13].sf_operator_type == "linear"
     out = capsys.readouterr().out
-    assert "Replacement summary: total=3, sparse=3" in out
+    assert "Replacement summary: total=4, sparse=4" in out
     assert kinds.count("SparseConv2d") == 3
 
 
@@ -96,7 +98,7 @@ def test_replacer_static_zero_and_block_override():
     x = (torch.rand(2, 2, 3, 16, 16) < 0.3).float()
     targets = NetworkAnalyzer(SpikeOpRegistry.default()).analyze(model, x)
     res = ModuleReplacer(verbose=False).replace(model, targets, block_sizes={"3": 16}, static_zero_layers={"9"})
-    assert res == (3, 2, 1, 1)  # the final Linear is a target kept dense
+    assert res == (4, 3, 1, 0)  # the final Linear becomes SparseLinear
     assert model[3].block_size == 16
     assert isinstance(model[9], StaticZeroConv2d)
     y = model[9](torch.zeros(2, 2, 64, 8, 8))
