@@ -168,6 +168,10 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 int num_sms_current_device();
 
+// Opts a kernel in to the full 227 KB of dynamic shared memory once per
+// (kernel, device) instead of on every launch (a driver call each time).
+bool allow_max_smem(const void* kernel);
+
 // Device-side choice between two kernel paths launched back to back: a
 // sampling kernel writes a nonzero count to *count, and each gated kernel
 // returns at entry unless the count selects it (side 1: count < thr; side 2:

@@ -772,8 +772,7 @@ sf_status launch(Params p, size_t smem, cudaStream_t st) {
   const bool stream = p.nbs > 0;
   auto kern = stream ? (vec ? conv3x3_tc_kernel<XT, WT, true, true> : conv3x3_tc_kernel<XT, WT, false, true>)
                      : (vec ? conv3x3_tc_kernel<XT, WT, true, false> : conv3x3_tc_kernel<XT, WT, false, false>);
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-    return SF_ERR_CUDA;
+  if (!allow_max_smem(reinterpret_cast<const void*>(kern))) return SF_ERR_CUDA;
   const long long grid = (p.nunits + p.units_per_cta - 1) / p.units_per_cta;
   kern<<<(unsigned)grid, kThreads, smem, st>>>(p);
   return cudaGetLastError() == cudaSuccess ? SF_OK : SF_ERR_CUDA;
@@ -913,6 +912,14 @@ bool plan_tc(Params& p, size_t& smem_out, int N, int C, int H, int W, int Co) {
     }
   }
   if (U == 0) return false;
+  // Small problems: fewer tiles per unit until every SM has a unit (C1, 32
+  // images of 32x32: 281 tiles, 71 four-tile units for 148 SMs).
+  const int sms = num_sms_current_device();
+  while (U > 1 && (p.ntiles + U - 1) / U * (p.nbs > 0 ? 1 : p.ncob) < sms) {
+    --U;
+    p.rows_a = rows_for(U);
+    p.a_plane = p.rows_a * 16;
+  }
   smem = std::max<size_t>(smem, 120 * 1024);  // one CTA (and one TMEM allocation) per SM
   p.U = U;
   if (p.nbs > 0) {

@@ -761,8 +761,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <int K, int S, int CPL, int R, int B, typename XT, typename WT, int MODE, bool WSMEM>
 sf_status launch_conv(const ConvParams& p, const CUtensorMap& ymap, int grid, int smem, cudaStream_t st) {
   auto kern = sparse_conv_kernel<K, S, CPL, R, B, XT, WT, MODE, WSMEM>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-    return SF_ERR_CUDA;
+  if (!allow_max_smem(reinterpret_cast<const void*>(kern))) return SF_ERR_CUDA;
   kern<<<grid, kThreads, smem, st>>>(p, ymap);
   return cudaGetLastError() == cudaSuccess ? SF_OK : SF_ERR_CUDA;
 }

@@ -528,8 +528,7 @@ template <typename XT, typename WT>
 sf_status launch(TcParams p, const CUtensorMap& xmap, size_t smem, int sub, cudaStream_t st) {
   auto kern = p.masks ? (sub == 2 ? pointwise_tc_kernel<XT, WT, 2, true> : pointwise_tc_kernel<XT, WT, 1, true>)
                       : (sub == 2 ? pointwise_tc_kernel<XT, WT, 2, false> : pointwise_tc_kernel<XT, WT, 1, false>);
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-    return SF_ERR_CUDA;
+  if (!allow_max_smem(reinterpret_cast<const void*>(kern))) return SF_ERR_CUDA;
   const long long ctas = std::min<long long>(p.ntiles, (long long)num_sms_current_device());
   p.tiles_per_cta = (p.ntiles + ctas - 1) / ctas;
   const long long grid = (p.ntiles + p.tiles_per_cta - 1) / p.tiles_per_cta;

@@ -4,6 +4,9 @@
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
+#include <set>
+#include <utility>
 #include <cudaTypedefs.h>
 #include "conv_kernel.cuh"
 #include "policy.cuh"
@@ -135,6 +138,19 @@ int g_num_sms[64] = {0};
 }  // namespace
 }  // namespace conv
 
+bool allow_max_smem(const void* kernel) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count({kernel, dev})) return true;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess)
+    return false;
+  done.insert({kernel, dev});
+  return true;
+}
+
 int num_sms_current_device() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 148;
@@ -211,6 +227,22 @@ size_t tc_section_offset(int c_out, int c_in, int kernel, int wsz) {
   return (gather_bytes(c_out, c_in, kernel, wsz) + 255) & ~(size_t)255;
 }
 
+// Device address of g_conv_error for the current device, looked up once per
+// device (the host-side symbol is not a device address).
+uint32_t* conv_error_word() {
+  static uint32_t* cache[64] = {nullptr};
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache[dev] == nullptr) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_conv_error) != cudaSuccess) return nullptr;
+    cache[dev] = static_cast<uint32_t*>(ptr);
+  }
+  return cache[dev];
+}
+
 // Spike density below which the gather kernel beats the tensor-core kernel
 // for 3x3/s1 layers of C_in input channels (0: the tensor cores always win).
 // Crossovers measured on the C5 grid (1024 images of 14x14 / 28x28 / 56x56,
@@ -243,7 +275,7 @@ sf_status run_conv(const void* x, const void* w_packed, const float* bias, void*
   if (!lif && K == 1 && S == 1 && P == 0 && policy(SF_POLICY_CONV1X1_PATH) == 0 &&
       !(masks_in && wdt == SF_DTYPE_F32)) {
     uint32_t* err = nullptr;
-    if (cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_conv_error) != cudaSuccess) return SF_ERR_CUDA;
+    if ((err = conv_error_word()) == nullptr) return SF_ERR_CUDA;
     s = pwtc::run_pointwise_tc(x, w_packed, bias, y, err, T * N, C, H, W, Co, xdt, wdt, st, masks_in);
     if (s != SF_ERR_UNSUPPORTED) return s;
   }
@@ -260,7 +292,7 @@ sf_status run_conv(const void* x, const void* w_packed, const float* bias, void*
   if (!lif && !masks_in && K == 3 && S == 1 && P == 1 && pol3 != 1 && c3tc::tc3_packs(Co, C, K) &&
       (wdt == SF_DTYPE_F32 || wdt == SF_DTYPE_BF16) && c3tc::tc3_supported(T * N, C, H, W, Co)) {
     uint32_t* err = nullptr;
-    if (cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_conv_error) != cudaSuccess) return SF_ERR_CUDA;
+    if ((err = conv_error_word()) == nullptr) return SF_ERR_CUDA;
     const double rho = tc3_min_density(C);
     if (pol3 == 2 || rho <= 0.0) {
       const int wsz = (int)dtype_size(wdt);
@@ -314,7 +346,7 @@ sf_status run_conv(const void* x, const void* w_packed, const float* bias, void*
   p.bias = bias;
   p.y = y;
   p.v = v;
-  if (cudaGetSymbolAddress(reinterpret_cast<void**>(&p.err), g_conv_error) != cudaSuccess) return SF_ERR_CUDA;
+  if ((p.err = conv_error_word()) == nullptr) return SF_ERR_CUDA;
   p.masks = ev.masks;
   p.flags = ev.flags;
   p.mask_out = mask_out;
@@ -371,7 +403,7 @@ sf_status run_conv(const void* x, const void* w_packed, const float* bias, void*
   s = dispatch(mode, xdt, wdt, K, S, p, ym, grid_used, pl, st);
   if (s != SF_OK || !tc_after) return s;
   uint32_t* err = nullptr;
-  if (cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_conv_error) != cudaSuccess) return SF_ERR_CUDA;
+  if ((err = conv_error_word()) == nullptr) return SF_ERR_CUDA;
   const int wsz = (int)dtype_size(wdt);
   const void* section = static_cast<const char*>(w_packed) + tc_section_offset(Co, C, K, wsz);
   return c3tc::run_conv3x3_tc(x, w_packed, weight_block_cpl(C, K, Co, wsz), section, bias, y, err, T * N, C, H, W,
