@@ -308,6 +308,10 @@ sf_status run_conv(const void* x, const void* w_packed, const float* bias, void*
     gate = Gate{count, (uint32_t)std::ceil(rho * kDensitySamples), 1};
     tc_after = true;
   }
+  // The gather path (mask pass + gather kernel), or the one-pass 1x1/s2
+  // kernel; gated by `gate` when the tensor-core kernel follows.
+  auto gather_path = [&]() -> sf_status {
+  sf_status s = SF_OK;
   // 1x1 stride 2: one pass over x with masks built in shared memory
   // (pointwise.cu). For stride 1 that kernel measured slower than the two
   // stages (0.74 vs 0.54 ms on the C2 cell; both issue-bound), so it runs
@@ -400,14 +404,17 @@ sf_status run_conv(const void* x, const void* w_packed, const float* bias, void*
     mode = (mask_out ? 2 : 1) + (pow2 ? 2 : 0);
   }
   p.gate = gate;
-  s = dispatch(mode, xdt, wdt, K, S, p, ym, grid_used, pl, st);
-  if (s != SF_OK || !tc_after) return s;
-  uint32_t* err = nullptr;
-  if ((err = conv_error_word()) == nullptr) return SF_ERR_CUDA;
+  return dispatch(mode, xdt, wdt, K, S, p, ym, grid_used, pl, st);
+  };
+  s = gather_path();
+  if (!tc_after) return s;
+  // The tensor-core kernel always follows a gated gather path: gated too when
+  // that path launched, ungated (it alone computes y) when it could not.
   const int wsz = (int)dtype_size(wdt);
   const void* section = static_cast<const char*>(w_packed) + tc_section_offset(Co, C, K, wsz);
-  return c3tc::run_conv3x3_tc(x, w_packed, weight_block_cpl(C, K, Co, wsz), section, bias, y, err, T * N, C, H, W,
-                              Co, xdt, wdt, st, Gate{gate.count, gate.thr, 2});
+  return c3tc::run_conv3x3_tc(x, w_packed, weight_block_cpl(C, K, Co, wsz), section, bias, y, conv_error_word(),
+                              T * N, C, H, W, Co, xdt, wdt, st,
+                              s == SF_OK ? Gate{gate.count, gate.thr, 2} : Gate{nullptr, 0u, 0});
 }
 
 }  // namespace

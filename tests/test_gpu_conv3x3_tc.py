@@ -138,3 +138,32 @@ def test_density_gate_picks_one_path(c, density, expect):
     other = _run(x, wt, b, 3 - expect)
     assert torch.equal(auto, forced)
     _close(auto.cpu().numpy(), other.cpu().numpy())
+
+
+def test_tc3x3_streamed_weights_non_binary_and_16bit():
+    """C_in > 64 (weights streamed): units holding values other than 0/1 take the fp32 path for
+    every output block; bf16 and fp16 inputs convert through the scalar converter."""
+    g = torch.Generator().manual_seed(12)
+    x = (torch.rand(5, 96, 12, 20, generator=g) < 0.1).float()
+    x[3] *= torch.randn(96, 12, 20, generator=g)
+    wt = torch.randn(80, 96, 3, 3, generator=g) * 0.05
+    b = torch.randn(80, generator=g)
+    ref = oracle.conv2d(x.numpy(), wt.numpy(), b.numpy(), 1, 1)
+    _close(_run(x.cuda(), wt.cuda(), b.cuda(), 2).cpu().numpy(), ref)
+    xs = (torch.rand(3, 160, 9, 13, generator=g) < 0.2).float()
+    for dt in (torch.bfloat16, torch.float16):
+        y = _run(xs.to(dt).cuda(), wt[:, :1].repeat(1, 160, 1, 1).cuda() * 0.5, None, 2)
+        ref = oracle.conv2d(xs.numpy(), (wt[:, :1].repeat(1, 160, 1, 1) * 0.5).numpy(), None, 1, 1)
+        _close(y.float().cpu().numpy(), ref, rtol=1e-2)
+
+
+def test_tc3x3_unaligned_input_takes_scalar_converter():
+    """x not 16-byte aligned (a view at an odd element offset): the scalar converter path."""
+    g = torch.Generator().manual_seed(13)
+    base = (torch.rand(2 * 64 * 20 * 20 + 1, generator=g) < 0.05).float()
+    x = base[1:].reshape(2, 64, 20, 20)
+    wt = torch.randn(64, 64, 3, 3, generator=g) * 0.05
+    xd = base.cuda()[1:].reshape(2, 64, 20, 20)
+    assert xd.data_ptr() % 16 != 0
+    ref = oracle.conv2d(x.numpy(), wt.numpy(), None, 1, 1)
+    _close(_run(xd, wt.cuda(), None, 2).cpu().numpy(), ref)
