@@ -60,6 +60,7 @@ constexpr int kEpiWarps = 16;
 constexpr int kMmaWarp = kEpi0 + kEpiWarps;
 constexpr int kThreads = (kMmaWarp + 1) * 32;
 constexpr int kMaxBStages = 8;
+constexpr int kMaxKch = 16;  // 16-channel slices per weight stage
 constexpr int kM = 128;
 constexpr int kTags = 4;
 
@@ -342,6 +343,34 @@ __device__ unsigned long long g_c3tc_prof[8];
 // memory (C_in <= 64); D per tile, double buffered. STREAM = true: weight
 // stages stream past the resident A of a unit once per output block; D per
 // (unit, block) group of U tiles, double buffered.
+// MMAs of one weight stage (PK slice pairs) for the nt tiles of a unit; tile j
+// accumulates at TMEM column dt0 + j*n3 and reads A 128 rows further on.
+// Unrolled per PK: the MMA warp's issue loop bounds the streamed layers.
+template <int PK>
+__device__ __forceinline__ void issue_stage(uint32_t dt0, uint32_t n3, int nt, uint64_t a0, uint64_t bstage,
+                                            uint64_t astep, uint64_t bstep, uint32_t idesc, uint32_t first) {
+  for (int j = 0; j < nt; ++j) {
+    const uint32_t dt = dt0 + (uint32_t)j * n3;
+    const uint64_t ad = a0 + (uint64_t)(j * kM);  // 128 rows of 16 bytes
+    tc::mma_s8(dt, ad, bstage, idesc, first);
+#pragma unroll
+    for (int kp = 1; kp < PK; ++kp) tc::mma_s8(dt, ad + kp * astep, bstage + kp * bstep, idesc, 1u);
+  }
+}
+
+// Any other pair count (C_in of 96, 160, 192, ...): a plain loop.
+__device__ __forceinline__ void issue_stage_n(int pk, uint32_t dt0, uint32_t n3, int nt, uint64_t a0,
+                                              uint64_t bstage, uint64_t astep, uint64_t bstep, uint32_t idesc,
+                                              uint32_t first) {
+  for (int j = 0; j < nt; ++j) {
+    const uint32_t dt = dt0 + (uint32_t)j * n3;
+    const uint64_t ad = a0 + (uint64_t)(j * kM);
+    tc::mma_s8(dt, ad, bstage, idesc, first);
+#pragma unroll 1
+    for (int kp = 1; kp < pk; ++kp) tc::mma_s8(dt, ad + kp * astep, bstage + kp * bstep, idesc, 1u);
+  }
+}
+
 template <typename XT, typename WT, bool VEC, bool STREAM>
 __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p) {
   constexpr int kConv = STREAM ? kEpi0 - 1 : kEpi0;  // converter warps
@@ -449,19 +478,19 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
             tc::fence_after();
             const uint32_t dt = tmem + (uint32_t)(d * p.N3);
             const uint64_t abase = tc::desc_interleave(asa + (uint32_t)(j * kM) * 16u, p.a_plane, 128u);
-            uint64_t bd = bbase;
-            uint32_t acc = 0u;
-            for (int kh = 0; kh < 3; ++kh) {
+            // Nine taps of one or two slice pairs, fully unrolled per case.
+            if (pk == 2) {
 #pragma unroll
-              for (int kw = 0; kw < 3; ++kw) {
-                uint64_t ad = abase + (uint64_t)(kh * p.Wp + kw);
-                tc::mma_s8(dt, ad, bd, idesc, acc);
-                acc = 1u;
-                bd += bstep;
-                if (pk == 2) {
-                  tc::mma_s8(dt, ad + astep, bd, idesc, 1u);
-                  bd += bstep;
-                }
+              for (int t = 0; t < 9; ++t) {
+                const uint64_t ad = abase + (uint64_t)((t / 3) * p.Wp + t % 3);
+                tc::mma_s8(dt, ad, bbase + (uint64_t)(2 * t) * bstep, idesc, t == 0 ? 0u : 1u);
+                tc::mma_s8(dt, ad + astep, bbase + (uint64_t)(2 * t + 1) * bstep, idesc, 1u);
+              }
+            } else {
+#pragma unroll
+              for (int t = 0; t < 9; ++t) {
+                const uint64_t ad = abase + (uint64_t)((t / 3) * p.Wp + t % 3);
+                tc::mma_s8(dt, ad, bbase + (uint64_t)t * bstep, idesc, t == 0 ? 0u : 1u);
               }
             }
             tc::mma_commit(&bars->d_full[d]);
@@ -520,15 +549,14 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
                                                             (uint32_t)(kc * p.kch) * p.a_plane,
                                                         p.a_plane, 128u);
                 const uint32_t first = (tap | kc) == 0 ? 0u : 1u;
-                for (int j = 0; j < nt; ++j) {
-                  const uint32_t dt = tmem + (uint32_t)((gb * p.U + j) * p.N3);
-                  const uint64_t ad = a0 + (uint64_t)(j * kM);  // 128 rows of 16 bytes
-                  // At most 4 slice pairs per stage (kch <= 8): unrolled, one add per operand.
-                  tc::mma_s8(dt, ad, bstage, idesc, first);
-#pragma unroll
-                  for (int kp = 1; kp < 4; ++kp)
-                    if (kp < pkc) tc::mma_s8(dt, ad + kp * astep, bstage + kp * bstep, idesc, 1u);
-                }
+                // One stage: kch/2 slice pairs for each tile of the unit.
+                const uint32_t dt0 = tmem + (uint32_t)(gb * p.U * p.N3);
+                if (pkc == 8)
+                  issue_stage<8>(dt0, p.N3, nt, a0, bstage, astep, bstep, idesc, first);
+                else if (pkc == 4)
+                  issue_stage<4>(dt0, p.N3, nt, a0, bstage, astep, bstep, idesc, first);
+                else
+                  issue_stage_n(pkc, dt0, p.N3, nt, a0, bstage, astep, bstep, idesc, first);
                 tc::mma_commit(&bars->s_empty[s]);
                 PROF_ADD(3);
                 if (++s == p.nbs) {
@@ -873,9 +901,10 @@ bool plan_tc(Params& p, size_t& smem_out, int N, int C, int H, int W, int Co) {
     // holds kch 16-channel slices of one tap of one 32-channel block. Prefer
     // two tiles per unit (each weight stage feeds both), then double-buffered
     // A, then more stages.
-    // Stages of at most 8 slices (12 KB): more of them in flight cover the
-    // L2 latency of the weight stream.
-    p.kch = std::min(g.kcores, 8);
+    // Stages of up to 16 slices (24 KB): each stage costs the MMA warp a
+    // wait, fences and a commit, which bound these layers at 8 slices
+    // (C256 14x14: 0.61 ms with 8-slice stages, 0.45 ms with 16).
+    p.kch = std::min(g.kcores, kMaxKch);
     while (g.kcores % p.kch) p.kch -= 2;
     p.bstage_bytes = (uint32_t)(p.kch * g.N3 * 16);
     const int cand[6][2] = {{4, 2}, {4, 1}, {2, 2}, {2, 1}, {1, 2}, {1, 1}};

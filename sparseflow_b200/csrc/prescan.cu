@@ -360,7 +360,7 @@ constexpr int kPoolThreads = 256;
 __global__ void __launch_bounds__(kPoolThreads) pool_tiles_kernel(PrescanParams p, int rows_per_cta) {
   extern __shared__ __align__(16) uint32_t smem[];
   __shared__ int s_cnt[64];
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tid = threadIdx.x;
   const int chunks = (p.GH + rows_per_cta - 1) / rows_per_cta;
   const int n = blockIdx.x / chunks;
   const int gh0 = (blockIdx.x - n * chunks) * rows_per_cta;

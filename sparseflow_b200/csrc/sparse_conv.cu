@@ -245,12 +245,14 @@ uint32_t* conv_error_word() {
 
 // Spike density below which the gather kernel beats the tensor-core kernel
 // for 3x3/s1 layers of C_in input channels (0: the tensor cores always win).
-// Crossovers measured on the C5 grid (1024 images of 14x14 / 28x28 / 56x56,
-// one B200): C_in 64 none (tensor cores 2.8-4.4x cuDNN at every density);
-// C_in 128 between 0.1 % and 1 %; C_in 256 and 512 between 1 % and 5 %.
+// Crossovers measured with both paths forced (1024 images of 14x14, 28x28
+// and 56x56, one B200): C_in 64 none (tensor cores 2.8-4.5x cuDNN at every
+// density); C_in 128 near 0.4 % (0.3 % at 28x28, 0.7 % at 14x14); C_in 256
+// near 0.8 %; C_in 512 near 1 %.
 double tc3_min_density(int C) {
   if (C <= c3tc::kTcResidentMaxC) return 0.0;
-  return C <= 160 ? 0.004 : 0.015;
+  if (C <= 160) return 0.004;
+  return C <= 320 ? 0.008 : 0.01;
 }
 constexpr int kDensitySamples = 32768;
 

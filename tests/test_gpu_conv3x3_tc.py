@@ -48,6 +48,10 @@ GEOM = [
     (1, 512, 14, 14, 512, 0.01),
     (1, 512, 56, 56, 32, 0.01),
     (3, 256, 7, 7, 64, 0.3),
+    # weight stages of 5 and 6 slice pairs (C_in 160 and 192; 384 takes two 6-pair stages a tap)
+    (1, 160, 12, 12, 64, 0.1),
+    (2, 192, 10, 11, 96, 0.15),
+    (1, 384, 9, 9, 64, 0.05),
 ]
 
 
@@ -125,7 +129,8 @@ def test_tc3x3_full_size_c5_cell_vs_cudnn_fp32():
     assert _lib.conv_status(x.device) == 0
 
 
-@pytest.mark.parametrize("c,density,expect", [(128, 0.0005, 1), (128, 0.05, 2), (256, 0.005, 1), (256, 0.1, 2)])
+@pytest.mark.parametrize("c,density,expect", [(128, 0.0005, 1), (128, 0.05, 2), (256, 0.005, 1), (256, 0.1, 2),
+                                               (512, 0.003, 1), (512, 0.05, 2)])
 def test_density_gate_picks_one_path(c, density, expect):
     """For C_in > 64 a sampled nonzero count picks the gather kernel (sparse inputs) or the
     tensor-core kernel on the device; the automatic result equals that path's bit for bit."""
