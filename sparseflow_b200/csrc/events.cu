@@ -139,37 +139,40 @@ uint32_t* event_count_word(void* workspace, long long nimg, int C, int HW) {
 
 namespace {
 template <typename XT>
-__global__ void __launch_bounds__(1024) sample_nonzeros_kernel(const XT* __restrict__ x, long long n, int samples,
-                                                                uint32_t* count) {
-  __shared__ uint32_t warp_cnt[32];
+__global__ void __launch_bounds__(256) sample_nonzeros_kernel(const XT* __restrict__ x, long long n, int samples,
+                                                               uint32_t* count) {
+  __shared__ uint32_t warp_cnt[8];
   const long long stride = max(1ll, n / samples);
-  uint32_t c = 0;
-  for (int i = threadIdx.x; i < samples; i += 1024) {
-    const long long idx = (long long)i * stride;
-    if (idx < n) c += DT<XT>::nz_bit(x[idx]);
-  }
+  const int i = blockIdx.x * 256 + threadIdx.x;
+  const long long idx = (long long)i * stride;
+  uint32_t c = (i < samples && idx < n) ? DT<XT>::nz_bit(x[idx]) : 0u;
   for (int o = 16; o; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
   if ((threadIdx.x & 31) == 0) warp_cnt[threadIdx.x >> 5] = c;
   __syncthreads();
-  if (threadIdx.x < 32) {
-    c = warp_cnt[threadIdx.x];
-    for (int o = 16; o; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
-    if (threadIdx.x == 0) *count = c;
+  if (threadIdx.x == 0) {
+    uint32_t t = 0;
+    for (int w = 0; w < 8; ++w) t += warp_cnt[w];
+    if (t) atomicAdd(count, t);
   }
 }
 }  // namespace
 
+// The samples are scattered over x (one 32-byte sector each), so they are
+// spread over many CTAs: one SM issuing all 32768 took 20-28 us.
 sf_status sample_nonzeros(const void* x, int xdt, long long n, int samples, uint32_t* count, cudaStream_t st) {
+  if (samples <= 0 || samples > kMaxDensitySamples) return SF_ERR_INVALID_ARG;
+  if (cudaMemsetAsync(count, 0, 4, st) != cudaSuccess) return SF_ERR_CUDA;
+  const unsigned blocks = (unsigned)((samples + 255) / 256);
   switch (xdt) {
     case SF_DTYPE_F32:
-      sample_nonzeros_kernel<float><<<1, 1024, 0, st>>>(static_cast<const float*>(x), n, samples, count);
+      sample_nonzeros_kernel<float><<<blocks, 256, 0, st>>>(static_cast<const float*>(x), n, samples, count);
       break;
     case SF_DTYPE_F16:
-      sample_nonzeros_kernel<__half><<<1, 1024, 0, st>>>(static_cast<const __half*>(x), n, samples, count);
+      sample_nonzeros_kernel<__half><<<blocks, 256, 0, st>>>(static_cast<const __half*>(x), n, samples, count);
       break;
     case SF_DTYPE_BF16:
-      sample_nonzeros_kernel<__nv_bfloat16><<<1, 1024, 0, st>>>(static_cast<const __nv_bfloat16*>(x), n, samples,
-                                                                  count);
+      sample_nonzeros_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), n,
+                                                                     samples, count);
       break;
     default: return SF_ERR_INVALID_ARG;
   }

@@ -20,8 +20,10 @@ uint32_t* event_count_word(void* workspace, long long nimg, int C, int HW);
 sf_status extract_events(const void* x, int xdt, long long nimg, int C, int HW, void* workspace,
                          size_t workspace_bytes, EventBuffers& out, cudaStream_t st, const Gate& gate);
 
-// Writes to *count the number of nonzeros among `samples` elements of x
-// (n elements) taken at a fixed stride: one CTA, a few microseconds.
+// Writes to *count the number of nonzeros among `samples` (at most
+// kMaxDensitySamples) elements of x (n elements) taken at a fixed stride: a
+// memset of the count and one load per thread over samples/256 CTAs.
+constexpr int kMaxDensitySamples = 32768;
 sf_status sample_nonzeros(const void* x, int xdt, long long n, int samples, uint32_t* count, cudaStream_t st);
 
 }  // namespace sf

@@ -14,6 +14,7 @@
 #include <cmath>
 #include <cstdlib>
 #include "common.cuh"
+#include "lif.cuh"
 #include "policy.cuh"
 
 namespace sf {
@@ -71,7 +72,8 @@ constexpr int kLifPrefetch = 8;
 template <typename XT, typename ST, int VEC>
 __global__ void __launch_bounds__(256) lif_multistep_kernel(const XT* __restrict__ x, float* __restrict__ v,
                                                             ST* __restrict__ s, long long numel, int T,
-                                                            LifParams q) {
+                                                            LifParams q, Gate gate) {
+  if (!gate_open(gate)) return;
   const long long nvec = numel / VEC;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < nvec;
        i += (long long)gridDim.x * blockDim.x) {
@@ -96,7 +98,8 @@ __global__ void __launch_bounds__(256) lif_multistep_kernel(const XT* __restrict
 }
 
 template <typename XT, typename ST>
-sf_status launch(const void* x, float* v, void* s, long long numel, int T, const LifParams& q, cudaStream_t st) {
+sf_status launch(const void* x, float* v, void* s, long long numel, int T, const LifParams& q, cudaStream_t st,
+                 const Gate& gate) {
   const bool vec = numel % 4 == 0 && aligned16(v) && (reinterpret_cast<uintptr_t>(x) % (4 * sizeof(XT))) == 0 &&
                    (reinterpret_cast<uintptr_t>(s) % (4 * sizeof(ST))) == 0;
   const int V = vec ? 4 : 1;
@@ -106,20 +109,21 @@ sf_status launch(const void* x, float* v, void* s, long long numel, int T, const
   if (blocks <= 0) return SF_OK;
   if (vec)
     lif_multistep_kernel<XT, ST, 4><<<(unsigned)blocks, 256, 0, st>>>(static_cast<const XT*>(x), v,
-                                                                     static_cast<ST*>(s), numel, T, q);
+                                                                     static_cast<ST*>(s), numel, T, q, gate);
   else
     lif_multistep_kernel<XT, ST, 1><<<(unsigned)blocks, 256, 0, st>>>(static_cast<const XT*>(x), v,
-                                                                     static_cast<ST*>(s), numel, T, q);
+                                                                     static_cast<ST*>(s), numel, T, q, gate);
   return cudaGetLastError() == cudaSuccess ? SF_OK : SF_ERR_CUDA;
 }
 
 template <typename XT>
 sf_status dispatch_s(int sdt, const void* x, float* v, void* s, long long numel, int T, const LifParams& q,
                      cudaStream_t st) {
+  const Gate open{nullptr, 0u, 0};
   switch (sdt) {
-    case SF_DTYPE_F32: return launch<XT, float>(x, v, s, numel, T, q, st);
-    case SF_DTYPE_F16: return launch<XT, __half>(x, v, s, numel, T, q, st);
-    case SF_DTYPE_BF16: return launch<XT, __nv_bfloat16>(x, v, s, numel, T, q, st);
+    case SF_DTYPE_F32: return launch<XT, float>(x, v, s, numel, T, q, st, open);
+    case SF_DTYPE_F16: return launch<XT, __half>(x, v, s, numel, T, q, st, open);
+    case SF_DTYPE_BF16: return launch<XT, __nv_bfloat16>(x, v, s, numel, T, q, st, open);
   }
   return SF_ERR_INVALID_ARG;
 }
@@ -165,7 +169,8 @@ template <typename XT, typename ST, bool POW2>
 __global__ void __launch_bounds__(256, SF_LIF_EV_MINB) lif_events_kernel(const XT* __restrict__ x, float* __restrict__ v,
                                                          ST* __restrict__ s, uint32_t* __restrict__ masks, int T,
                                                          int N, int C, int HW, int ncb, int npb, int nw2,
-                                                         LifParams q, float inv_tau) {
+                                                         LifParams q, float inv_tau, Gate gate) {
+  if (!gate_open(gate)) return;
   // Membranes of the warp's 32 channels x 32 pixels, [channel][warp][lane]:
   // conflict-free, and no per-channel register file to unroll.
   __shared__ float vs[kEvCh][8][32];
@@ -246,7 +251,7 @@ inline float pow2_reciprocal(float tau) {
 
 template <typename XT, typename ST>
 sf_status launch_events(const void* x, float* v, void* s, void* masks, int T, int N, int C, int HW,
-                        const LifParams& q, cudaStream_t st) {
+                        const LifParams& q, cudaStream_t st, const Gate& gate) {
   const int ncb = (C + kEvCh - 1) / kEvCh, npb = (HW + 31) / 32, nw2 = 2 * ((C + 63) / 64);
   const long long warps = (long long)N * ncb * npb;
   const long long blocks = (warps + 7) / 8;
@@ -255,11 +260,11 @@ sf_status launch_events(const void* x, float* v, void* s, void* masks, int T, in
   if (inv != 0.f)
     lif_events_kernel<XT, ST, true><<<(unsigned)blocks, 256, 0, st>>>(
         static_cast<const XT*>(x), v, static_cast<ST*>(s), static_cast<uint32_t*>(masks), T, N, C, HW, ncb, npb,
-        nw2, q, inv);
+        nw2, q, inv, gate);
   else
     lif_events_kernel<XT, ST, false><<<(unsigned)blocks, 256, 0, st>>>(
         static_cast<const XT*>(x), v, static_cast<ST*>(s), static_cast<uint32_t*>(masks), T, N, C, HW, ncb, npb,
-        nw2, q, 0.f);
+        nw2, q, 0.f, gate);
   return cudaGetLastError() == cudaSuccess ? SF_OK : SF_ERR_CUDA;
 }
 
@@ -290,7 +295,8 @@ __global__ void __launch_bounds__(256, 4) lif_bitmap_kernel(const XT* __restrict
                                                          ST* __restrict__ s, uint32_t* __restrict__ masks,
                                                          long long numel, int T, long long img_elems,
                                                          long long region_words, int n_per_step, LifParams q,
-                                                         float inv_tau) {
+                                                         float inv_tau, Gate gate) {
+  if (!gate_open(gate)) return;
   constexpr int VEC = 4;
   const long long nvec = numel / VEC;
   const int lane = threadIdx.x & 31;
@@ -359,7 +365,8 @@ __device__ __forceinline__ uint32_t warp_transpose32(uint32_t x, int lane) {
 // 32 channels: lane = channel reads its 32-pixel window of the bitmap, the
 // warp transposes, lane = pixel writes that 32-channel half word.
 __global__ void __launch_bounds__(512) bitmap_to_masks_kernel(uint32_t* __restrict__ masks, int C, int HW,
-                                                              long long region_words, int nw) {
+                                                              long long region_words, int nw, Gate gate) {
+  if (!gate_open(gate)) return;
   extern __shared__ uint32_t bm[];
   uint32_t* reg = masks + (size_t)blockIdx.x * region_words;
   const int nbits_words = (int)(((long long)C * HW) >> 5);
@@ -386,7 +393,7 @@ __global__ void __launch_bounds__(512) bitmap_to_masks_kernel(uint32_t* __restri
 
 template <typename XT, typename ST>
 bool launch_events_bitmap(const void* x, float* v, void* s, void* masks, int T, int N, int C, int HW,
-                          const LifParams& q, cudaStream_t st, sf_status* status) {
+                          const LifParams& q, cudaStream_t st, const Gate& gate, sf_status* status) {
   const long long img_elems = (long long)C * HW;
   const long long bitmap_bytes = img_elems / 8;
   if (img_elems % 128 != 0 || bitmap_bytes > kBitmapMaxBytes) return false;
@@ -402,11 +409,11 @@ bool launch_events_bitmap(const void* x, float* v, void* s, void* masks, int T, 
   if (inv != 0.f)
     lif_bitmap_kernel<XT, ST, true><<<(unsigned)blocks, 256, 0, st>>>(
         static_cast<const XT*>(x), v, static_cast<ST*>(s), static_cast<uint32_t*>(masks), numel, T, img_elems,
-        region_words, N, q, inv);
+        region_words, N, q, inv, gate);
   else
     lif_bitmap_kernel<XT, ST, false><<<(unsigned)blocks, 256, 0, st>>>(
         static_cast<const XT*>(x), v, static_cast<ST*>(s), static_cast<uint32_t*>(masks), numel, T, img_elems,
-        region_words, N, q, 0.f);
+        region_words, N, q, 0.f, gate);
   if (cudaGetLastError() != cudaSuccess) {
     *status = SF_ERR_CUDA;
     return true;
@@ -423,19 +430,19 @@ bool launch_events_bitmap(const void* x, float* v, void* s, void* masks, int T, 
     return true;
   }
   bitmap_to_masks_kernel<<<(unsigned)images, 512, smem, st>>>(static_cast<uint32_t*>(masks), C, HW, region_words,
-                                                              nw);
+                                                              nw, gate);
   *status = cudaGetLastError() == cudaSuccess ? SF_OK : SF_ERR_CUDA;
   return true;
 }
 
 template <typename XT, typename ST>
 sf_status launch_events_any(const void* x, float* v, void* s, void* m, int T, int N, int C, int HW,
-                            const LifParams& q, cudaStream_t st) {
+                            const LifParams& q, cudaStream_t st, const Gate& gate = Gate{nullptr, 0u, 0}) {
   sf_status status = SF_OK;
   if (policy(SF_POLICY_LIF_EVENTS_GENERAL) == 0 &&
-      launch_events_bitmap<XT, ST>(x, v, s, m, T, N, C, HW, q, st, &status))
+      launch_events_bitmap<XT, ST>(x, v, s, m, T, N, C, HW, q, st, gate, &status))
     return status;
-  return launch_events<XT, ST>(x, v, s, m, T, N, C, HW, q, st);
+  return launch_events<XT, ST>(x, v, s, m, T, N, C, HW, q, st, gate);
 }
 
 template <typename XT>
@@ -449,6 +456,20 @@ sf_status dispatch_events_s(int sdt, const void* x, float* v, void* s, void* m, 
   return SF_ERR_INVALID_ARG;
 }
 }  // namespace
+
+sf_status lif_after_conv(const float* y, float* v, float* spikes, void* masks, int T, int N, int C, int HW,
+                         float tau, float v_threshold, float v_reset, int hard_reset, int decay_input,
+                         const Gate& gate, cudaStream_t st) {
+  LifParams q;
+  q.tau = tau;
+  q.vth = v_threshold;
+  q.vr = hard_reset ? v_reset : 0.f;
+  q.hard = hard_reset;
+  q.decay_input = decay_input;
+  if (masks) return launch_events_any<float, float>(y, v, spikes, masks, T, N, C, HW, q, st, gate);
+  return launch<float, float>(y, v, spikes, (long long)N * C * HW, T, q, st, gate);
+}
+
 }  // namespace sf
 
 using namespace sf;

@@ -11,6 +11,7 @@
 #include "conv_kernel.cuh"
 #include "policy.cuh"
 #include "events.cuh"
+#include "lif.cuh"
 #include "conv3x3_tc.cuh"
 
 namespace sf {
@@ -254,7 +255,22 @@ double tc3_min_density(int C) {
   if (C <= 160) return 0.004;
   return C <= 320 ? 0.008 : 0.01;
 }
-constexpr int kDensitySamples = 32768;
+// The same for the fused conv + LIF: the tensor-core route writes the
+// preactivations and runs the LIF over them in place, 8 bytes per output
+// element more than the fused gather kernel; emitting the next layer's event
+// masks costs the gather kernel more than the LIF kernel. Crossovers (T16
+// N64, one B200, both routes forced, ms gather / tensor cores):
+//   C_in 64 56x56:  masks 0.735 / 0.735 at 0.1 %, 0.809 / 0.734 at 0.3 %;
+//                   none  0.646 / 0.666 at 0.1 %, 0.705 / 0.664 at 0.3 %
+//   C_in 128 28x28: masks 0.649 / 0.668 at 0.3 %, 0.688 / 0.667 at 0.4 %;
+//                   none  0.616 / 0.632 at 0.5 %, 0.682 / 0.632 at 0.7 %
+//   C_in 256 14x14: masks 0.553 / 0.550 at 0.6 %; none 0.548 / 0.528 at 0.6 %
+double tc3_lif_min_density(int C, bool masks) {
+  if (C <= c3tc::kTcResidentMaxC) return masks ? 0.0 : 0.002;
+  if (C <= 160) return masks ? 0.0035 : 0.0055;
+  return C <= 320 ? 0.0055 : 0.01;
+}
+constexpr int kDensitySamples = kMaxDensitySamples;
 
 // Stage 1 + stage 2 for T*N images; the LIF variant when lif is set.
 // masks_in: events of x precomputed by a fused conv + LIF (binary spikes;
@@ -287,21 +303,32 @@ sf_status run_conv(const void* x, const void* w_packed, const float* bias, void*
   // C_in <= 64 the tensor-core kernel is faster at every density; above, the
   // gather kernel wins on sparse enough inputs, so a sampled nonzero count
   // picks one of the two paths on the device (both are launched; the other
-  // returns at entry).
+  // returns at entry). The fused conv + LIF makes the same choice at its own
+  // densities.
   const int pol3 = (int)policy(SF_POLICY_CONV3X3_PATH);
   Gate gate{nullptr, 0u, 0};
   bool tc_after = false;
-  if (!lif && !masks_in && K == 3 && S == 1 && P == 1 && pol3 != 1 && c3tc::tc3_packs(Co, C, K) &&
-      (wdt == SF_DTYPE_F32 || wdt == SF_DTYPE_BF16) && c3tc::tc3_supported(T * N, C, H, W, Co)) {
-    uint32_t* err = nullptr;
-    if ((err = conv_error_word()) == nullptr) return SF_ERR_CUDA;
-    const double rho = tc3_min_density(C);
-    if (pol3 == 2 || rho <= 0.0) {
-      const int wsz = (int)dtype_size(wdt);
-      const void* section = static_cast<const char*>(w_packed) + tc_section_offset(Co, C, K, wsz);
-      return c3tc::run_conv3x3_tc(x, w_packed, weight_block_cpl(C, K, Co, wsz), section, bias, y, err, T * N, C,
-                                  H, W, Co, xdt, wdt, st, gate);
-    }
+  const bool tc_shape = !masks_in && K == 3 && S == 1 && P == 1 && pol3 != 1 && c3tc::tc3_packs(Co, C, K) &&
+                        (wdt == SF_DTYPE_F32 || wdt == SF_DTYPE_BF16) &&
+                        c3tc::tc3_supported(T * N, C, H, W, Co);
+  // Fused conv + LIF: the tensor-core kernel writes the fp32 preactivations
+  // into the spike buffer and the multi-step LIF runs over them in place (v,
+  // spikes and event masks as the fused gather kernel writes them). fp32
+  // spikes only: a 16-bit buffer would round the preactivations.
+  const bool lif_tc = lif && tc_shape && xdt == SF_DTYPE_F32;
+  auto tc_then_lif = [&](const Gate& g) -> sf_status {
+    const int wsz = (int)dtype_size(wdt);
+    const void* section = static_cast<const char*>(w_packed) + tc_section_offset(Co, C, K, wsz);
+    sf_status r = c3tc::run_conv3x3_tc(x, w_packed, weight_block_cpl(C, K, Co, wsz), section, bias, y,
+                                       conv_error_word(), T * N, C, H, W, Co, xdt, wdt, st, g);
+    if (r != SF_OK || !lif) return r;
+    return lif_after_conv(static_cast<const float*>(y), v, static_cast<float*>(y), mask_out, T, N, Co, Ho * Wo,
+                          lifd->tau, lifd->v_threshold, lifd->v_reset, lifd->hard_reset, lifd->decay_input, g, st);
+  };
+  if ((!lif && tc_shape) || lif_tc) {
+    if (conv_error_word() == nullptr) return SF_ERR_CUDA;
+    const double rho = lif ? tc3_lif_min_density(C, mask_out != nullptr) : tc3_min_density(C);
+    if (pol3 == 2 || rho <= 0.0) return tc_then_lif(Gate{nullptr, 0u, 0});
     const long long nimg = (long long)T * N;
     if (ws_bytes < event_workspace_bytes(nimg, C, H * W)) return SF_ERR_WORKSPACE;
     uint32_t* count = event_count_word(workspace, nimg, C, H * W);
@@ -410,13 +437,9 @@ sf_status run_conv(const void* x, const void* w_packed, const float* bias, void*
   };
   s = gather_path();
   if (!tc_after) return s;
-  // The tensor-core kernel always follows a gated gather path: gated too when
-  // that path launched, ungated (it alone computes y) when it could not.
-  const int wsz = (int)dtype_size(wdt);
-  const void* section = static_cast<const char*>(w_packed) + tc_section_offset(Co, C, K, wsz);
-  return c3tc::run_conv3x3_tc(x, w_packed, weight_block_cpl(C, K, Co, wsz), section, bias, y, conv_error_word(),
-                              T * N, C, H, W, Co, xdt, wdt, st,
-                              s == SF_OK ? Gate{gate.count, gate.thr, 2} : Gate{nullptr, 0u, 0});
+  // The tensor-core kernel (and LIF) always follow a gated gather path: gated
+  // too when that path launched, ungated (they alone compute y) when it could not.
+  return tc_then_lif(s == SF_OK ? Gate{gate.count, gate.thr, 2} : Gate{nullptr, 0u, 0});
 }
 
 }  // namespace
