@@ -244,6 +244,30 @@ uint32_t* conv_error_word() {
   return cache[dev];
 }
 
+// A second stream of the calling thread on the current device, with a fork
+// and a join event: the two gated routes of a 3x3 call run side by side, so
+// the kernels of the route the gate closes overlap the open route's instead
+// of queueing behind them. Created once per thread and device.
+struct SideStream {
+  cudaStream_t stream = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+};
+const SideStream* side_stream() {
+  thread_local SideStream cache[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  SideStream& ss = cache[dev];
+  if (ss.stream == nullptr) {
+    SideStream n;
+    if (cudaStreamCreateWithFlags(&n.stream, cudaStreamNonBlocking) != cudaSuccess) return nullptr;
+    if (cudaEventCreateWithFlags(&n.fork, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&n.join, cudaEventDisableTiming) != cudaSuccess)
+      return nullptr;
+    ss = n;
+  }
+  return &ss;
+}
+
 // Spike density below which the gather kernel beats the tensor-core kernel
 // for 3x3/s1 layers of C_in input channels (0: the tensor cores always win).
 // Crossovers measured with both paths forced (1024 images of 14x14, 28x28
@@ -316,19 +340,19 @@ sf_status run_conv(const void* x, const void* w_packed, const float* bias, void*
   // spikes and event masks as the fused gather kernel writes them). fp32
   // spikes only: a 16-bit buffer would round the preactivations.
   const bool lif_tc = lif && tc_shape && xdt == SF_DTYPE_F32;
-  auto tc_then_lif = [&](const Gate& g) -> sf_status {
+  auto tc_then_lif = [&](const Gate& g, cudaStream_t sx) -> sf_status {
     const int wsz = (int)dtype_size(wdt);
     const void* section = static_cast<const char*>(w_packed) + tc_section_offset(Co, C, K, wsz);
     sf_status r = c3tc::run_conv3x3_tc(x, w_packed, weight_block_cpl(C, K, Co, wsz), section, bias, y,
-                                       conv_error_word(), T * N, C, H, W, Co, xdt, wdt, st, g);
+                                       conv_error_word(), T * N, C, H, W, Co, xdt, wdt, sx, g);
     if (r != SF_OK || !lif) return r;
     return lif_after_conv(static_cast<const float*>(y), v, static_cast<float*>(y), mask_out, T, N, Co, Ho * Wo,
-                          lifd->tau, lifd->v_threshold, lifd->v_reset, lifd->hard_reset, lifd->decay_input, g, st);
+                          lifd->tau, lifd->v_threshold, lifd->v_reset, lifd->hard_reset, lifd->decay_input, g, sx);
   };
   if ((!lif && tc_shape) || lif_tc) {
     if (conv_error_word() == nullptr) return SF_ERR_CUDA;
     const double rho = lif ? tc3_lif_min_density(C, mask_out != nullptr) : tc3_min_density(C);
-    if (pol3 == 2 || rho <= 0.0) return tc_then_lif(Gate{nullptr, 0u, 0});
+    if (pol3 == 2 || rho <= 0.0) return tc_then_lif(Gate{nullptr, 0u, 0}, st);
     const long long nimg = (long long)T * N;
     if (ws_bytes < event_workspace_bytes(nimg, C, H * W)) return SF_ERR_WORKSPACE;
     uint32_t* count = event_count_word(workspace, nimg, C, H * W);
@@ -435,11 +459,22 @@ sf_status run_conv(const void* x, const void* w_packed, const float* bias, void*
   p.gate = gate;
   return dispatch(mode, xdt, wdt, K, S, p, ym, grid_used, pl, st);
   };
+  if (!tc_after) return gather_path();
+  // Both routes, each gated: the gather route on the caller's stream, the
+  // tensor-core route (and LIF) on the side stream between a fork after the
+  // sampler and a join before whatever the caller queues next.
+  const SideStream* side = side_stream();
+  if (side == nullptr) return SF_ERR_CUDA;
+  if (cudaEventRecord(side->fork, st) != cudaSuccess || cudaStreamWaitEvent(side->stream, side->fork, 0) != cudaSuccess)
+    return SF_ERR_CUDA;
   s = gather_path();
-  if (!tc_after) return s;
-  // The tensor-core kernel (and LIF) always follow a gated gather path: gated
-  // too when that path launched, ungated (they alone compute y) when it could not.
-  return tc_then_lif(s == SF_OK ? Gate{gate.count, gate.thr, 2} : Gate{nullptr, 0u, 0});
+  // Gated too when the gather route launched; ungated (it alone computes y)
+  // when that route could not.
+  const sf_status r =
+      tc_then_lif(s == SF_OK ? Gate{gate.count, gate.thr, 2} : Gate{nullptr, 0u, 0}, side->stream);
+  if (cudaEventRecord(side->join, side->stream) != cudaSuccess || cudaStreamWaitEvent(st, side->join, 0) != cudaSuccess)
+    return SF_ERR_CUDA;
+  return r;
 }
 
 }  // namespace
