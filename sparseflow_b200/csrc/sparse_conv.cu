@@ -252,12 +252,16 @@ struct SideStream {
   cudaStream_t stream = nullptr;
   cudaEvent_t fork = nullptr, join = nullptr;
 };
-const SideStream* side_stream() {
+// Null when there is none yet and `may_create` is false (a stream being
+// captured into a CUDA graph: creating streams there is not allowed in every
+// capture mode).
+const SideStream* side_stream(bool may_create) {
   thread_local SideStream cache[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
   SideStream& ss = cache[dev];
   if (ss.stream == nullptr) {
+    if (!may_create) return nullptr;
     SideStream n;
     if (cudaStreamCreateWithFlags(&n.stream, cudaStreamNonBlocking) != cudaSuccess) return nullptr;
     if (cudaEventCreateWithFlags(&n.fork, cudaEventDisableTiming) != cudaSuccess ||
@@ -463,8 +467,14 @@ sf_status run_conv(const void* x, const void* w_packed, const float* bias, void*
   // Both routes, each gated: the gather route on the caller's stream, the
   // tensor-core route (and LIF) on the side stream between a fork after the
   // sampler and a join before whatever the caller queues next.
-  const SideStream* side = side_stream();
-  if (side == nullptr) return SF_ERR_CUDA;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cap) != cudaSuccess) return SF_ERR_CUDA;
+  const SideStream* side = side_stream(cap == cudaStreamCaptureStatusNone);
+  if (side == nullptr) {
+    // No side stream: both routes in order on the caller's stream.
+    s = gather_path();
+    return tc_then_lif(s == SF_OK ? Gate{gate.count, gate.thr, 2} : Gate{nullptr, 0u, 0}, st);
+  }
   if (cudaEventRecord(side->fork, st) != cudaSuccess || cudaStreamWaitEvent(side->stream, side->fork, 0) != cudaSuccess)
     return SF_ERR_CUDA;
   s = gather_path();

@@ -172,3 +172,40 @@ def test_tc3x3_unaligned_input_takes_scalar_converter():
     assert xd.data_ptr() % 16 != 0
     ref = oracle.conv2d(x.numpy(), wt.numpy(), None, 1, 1)
     _close(_run(xd, wt.cuda(), None, 2).cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("fresh_thread", [False, True])
+def test_gated_routes_under_cuda_graph_capture(fresh_thread):
+    """A gated 3x3 call (C_in > 64, both routes launched) captured into a CUDA graph replays to the
+    eager result bit for bit: with a side stream already made (fork and join captured) and from a
+    thread that has none yet (both routes in order on the captured stream)."""
+    import threading
+    g = torch.Generator().manual_seed(41)
+    res = {}
+    for density in (0.001, 0.05):
+        x = (torch.rand(8, 128, 14, 14, generator=g) < density).float().cuda()
+        wt = (torch.randn(128, 128, 3, 3, generator=g) * 0.05).cuda()
+        eager = _run(x, wt, None, 0)
+
+        def capture():
+            from sparseflow_b200.Kernels.conv2d import sparse_conv2d_forward, pack_weight
+            wp = pack_weight(wt)
+            s = torch.cuda.Stream()
+            with torch.cuda.stream(s):
+                if not fresh_thread:
+                    sparse_conv2d_forward(x, wt, None, kernel_size=3, stride=1, padding=1, w_cl=wp)
+                torch.cuda.synchronize()
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=s):
+                    y, _ = sparse_conv2d_forward(x, wt, None, kernel_size=3, stride=1, padding=1, w_cl=wp)
+                graph.replay()
+            torch.cuda.synchronize()
+            res[density] = y.clone()
+
+        if fresh_thread:
+            th = threading.Thread(target=capture)
+            th.start()
+            th.join()
+        else:
+            capture()
+        assert torch.equal(res[density], eager)
