@@ -345,6 +345,14 @@ def extras(dev, hbm_peak, steps):
     out["c3_fused_conv_bn_lif"] = {"GBps": round(b3 / ms / 1e6, 1), "frac_of_measured_hbm": round(b3 / ms / 1e6 / hbm_peak, 3),
                                    "ms": round(ms, 4), "cudnn_conv_bn_torch_lif_ms": round(ms_ref, 4),
                                    "speedup_vs_cudnn_path": round(ms_ref / ms, 2)}
+    # The same layer at higher firing rates, where the density gate sends it to the tensor-core
+    # route (conv into the spike buffer, LIF in place); the cuDNN path does not depend on density.
+    by_density = {}
+    for dd in (0.02, 0.1):
+        x3 = (torch.rand(16, 64, 128, 28, 28, device=dev, generator=g) < dd).float()
+        by_density[str(dd)] = {"ms": round(cuda_time(c3_step, steps, 3) / steps, 4)}
+        by_density[str(dd)]["speedup_vs_cudnn_path"] = round(ms_ref / by_density[str(dd)]["ms"], 2)
+    out["c3_fused_conv_bn_lif"]["by_density"] = by_density
     del x3
     # LIF -> SparseConv2d on the headline layer shape (T16 N64 C64 56x56, ~1 % spikes): the LIF
     # writing the next convolution's event masks (LIFNode.emit_event_masks) against the plain
@@ -365,6 +373,8 @@ def extras(dev, hbm_peak, steps):
     lifl.reset()
     chain["spike_density"] = round(float(lifl(xl).float().mean()), 4)
     chain["speedup"] = round(chain["plain_ms"] / chain["emit_ms"], 3)
+    chain["note"] = ("the C64 3x3 convolution runs on the tensor cores from the spikes and ignores the masks, "
+                     "so optimize() leaves emission off for such layers; this times the emission cost alone")
     out["lif_events_to_conv"] = chain
     del xl
     out["c1_conv3x3_small"] = c1_small(dev, hbm_peak, steps)

@@ -207,6 +207,19 @@ sf_status sf_sparse_conv2d_from_masks(const void* event_masks, const void* w_pac
                                       const float* bias, void* y, const sf_conv_desc* d,
                                       void* stream);
 
+/* sf_sparse_conv2d of binary spikes x given both x and its event masks: a
+ * sampled density of x picks on the device the gather kernel from the masks
+ * (sparse spikes) or, for 3x3/s1/p1 layers the tcgen05 kernel takes, the
+ * tensor cores reading x; every other shape runs as
+ * sf_sparse_conv2d_from_masks. workspace: at least
+ * sf_sparse_conv2d_masks_or_x_workspace_size() bytes, 4-byte aligned (the
+ * sampled count; ignored where no choice is made). Same reference interface
+ * as sf_sparse_conv2d_from_masks. */
+size_t sf_sparse_conv2d_masks_or_x_workspace_size(void);
+sf_status sf_sparse_conv2d_masks_or_x(const void* x, const void* event_masks, const void* w_packed,
+                                      const float* bias, void* y, const sf_conv_desc* d,
+                                      void* workspace, size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Multi-step LIF neuron (the separate LIFNode after a BN, not fused into a  */
 /* convolution): the update of Ops/sparse_fused_conv_lif.py:271-293 applied  */

@@ -70,7 +70,8 @@ def uses_event_masks(c_in: int, h_in: int, w_in: int, kernel_size: int, stride: 
     kernel reads them. The 3x3/s1 tensor-core kernel with C_in <= 64 reads the
     spikes faster than the gather kernel reads masks (C64 56x56: 0.37 ms
     against 0.46 ms; 8x8 maps: 0.027 against 0.06 ms), so those layers ignore
-    them."""
+    them. Wider 3x3/s1 layers run from the masks when the spikes are sparse and
+    from x on the tensor cores otherwise, chosen on the device."""
     if (kernel_size, stride) == (1, 2):
         return False
     lib = _lib.load()
@@ -189,7 +190,10 @@ def sparse_conv2d_forward(
         se, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         se.record()
     used_masks = event_masks is not None and uses_event_masks(c_in, h_in, w_in, kernel_size, stride, padding)
-    if used_masks:
+    if used_masks and (kernel_size, stride, padding) == (3, 1, 1):
+        # Dense enough spikes run on the tensor cores from x; the choice is made on the device.
+        _lib.sparse_conv2d_masks_or_x(x, event_masks, w_packed, b, y, kernel_size, stride, padding)
+    elif used_masks:
         _lib.sparse_conv2d_from_masks(event_masks, tuple(x.shape), x.dtype, w_packed, b, y, kernel_size, stride,
                                       padding)
     else:

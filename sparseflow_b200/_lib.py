@@ -115,6 +115,9 @@ _SIGNATURES = {
     "sf_set_path_policy": (ctypes.c_int32, [ctypes.c_int32, ctypes.c_int64]),
     "sf_get_path_policy": (ctypes.c_int64, [ctypes.c_int32]),
     "sf_sparse_conv2d_from_masks": (ctypes.c_int32, [_VP, _VP, _VP, _VP, ctypes.POINTER(ConvDesc), _VP]),
+    "sf_sparse_conv2d_masks_or_x_workspace_size": (ctypes.c_size_t, []),
+    "sf_sparse_conv2d_masks_or_x": (ctypes.c_int32, [_VP, _VP, _VP, _VP, _VP, ctypes.POINTER(ConvDesc), _VP,
+                                                     ctypes.c_size_t, _VP]),
 }
 
 _lib = None
@@ -280,6 +283,23 @@ def sparse_conv2d_from_masks(masks: torch.Tensor, x_shape, x_dtype: torch.dtype,
     st = load().sf_sparse_conv2d_from_masks(_ptr(masks), _ptr(w_packed), _ptr(bias), _ptr(y), ctypes.byref(desc),
                                             _stream(y.device))
     _check("sf_sparse_conv2d_from_masks", st)
+
+
+def sparse_conv2d_masks_or_x(x: torch.Tensor, masks: torch.Tensor, w_packed: torch.Tensor,
+                             bias: Optional[torch.Tensor], y: torch.Tensor, kernel: int, stride: int,
+                             padding: int) -> None:
+    """Convolution of binary spikes x given x and its event masks: a sampled density picks the
+    gather kernel from the masks or the tensor cores from x on the device."""
+    _require_cuda(x, masks, w_packed, bias, y)
+    n, c, h, w = x.shape
+    _, co, ho, wo = y.shape
+    desc = ConvDesc(n, c, h, w, co, ho, wo, kernel, stride, padding, sf_dtype(x.dtype), sf_dtype(w_packed.dtype),
+                    int(bias is not None))
+    lib = load()
+    ws = torch.empty(int(lib.sf_sparse_conv2d_masks_or_x_workspace_size()), dtype=torch.uint8, device=x.device)
+    st = lib.sf_sparse_conv2d_masks_or_x(_ptr(x), _ptr(masks), _ptr(w_packed), _ptr(bias), _ptr(y),
+                                         ctypes.byref(desc), _ptr(ws), ws.numel(), _stream(y.device))
+    _check("sf_sparse_conv2d_masks_or_x", st)
 
 
 def fused_conv_lif(x5: torch.Tensor, w_packed: torch.Tensor, bias: Optional[torch.Tensor], v: torch.Tensor,

@@ -299,10 +299,12 @@ double tc3_lif_min_density(int C, bool masks) {
   return C <= 320 ? 0.0055 : 0.01;
 }
 constexpr int kDensitySamples = kMaxDensitySamples;
+constexpr size_t kMasksOrXWorkspace = 256;  // the sampled count of sf_sparse_conv2d_masks_or_x
 
 // Stage 1 + stage 2 for T*N images; the LIF variant when lif is set.
 // masks_in: events of x precomputed by a fused conv + LIF (binary spikes;
-// x itself is then not read). mask_out: LIF only, the output spikes' events.
+// x itself is then not read, or may be null, except by the tensor-core 3x3
+// route when x is given too). mask_out: LIF only, the output spikes' events.
 sf_status run_conv(const void* x, const void* w_packed, const float* bias, void* y, float* v, int T, int N, int C,
                    int H, int W, int Co, int Ho, int Wo, int K, int S, int P, int xdt, int wdt, bool lif,
                    const sf_lif_desc* lifd, void* workspace, size_t ws_bytes, cudaStream_t st,
@@ -336,7 +338,9 @@ sf_status run_conv(const void* x, const void* w_packed, const float* bias, void*
   const int pol3 = (int)policy(SF_POLICY_CONV3X3_PATH);
   Gate gate{nullptr, 0u, 0};
   bool tc_after = false;
-  const bool tc_shape = !masks_in && K == 3 && S == 1 && P == 1 && pol3 != 1 && c3tc::tc3_packs(Co, C, K) &&
+  // With masks handed over and x too (sf_sparse_conv2d_masks_or_x), the gate
+  // picks the gather kernel from the masks or the tensor cores from x.
+  const bool tc_shape = (!masks_in || x) && K == 3 && S == 1 && P == 1 && pol3 != 1 && c3tc::tc3_packs(Co, C, K) &&
                         (wdt == SF_DTYPE_F32 || wdt == SF_DTYPE_BF16) &&
                         c3tc::tc3_supported(T * N, C, H, W, Co);
   // Fused conv + LIF: the tensor-core kernel writes the fp32 preactivations
@@ -358,8 +362,14 @@ sf_status run_conv(const void* x, const void* w_packed, const float* bias, void*
     const double rho = lif ? tc3_lif_min_density(C, mask_out != nullptr) : tc3_min_density(C);
     if (pol3 == 2 || rho <= 0.0) return tc_then_lif(Gate{nullptr, 0u, 0}, st);
     const long long nimg = (long long)T * N;
-    if (ws_bytes < event_workspace_bytes(nimg, C, H * W)) return SF_ERR_WORKSPACE;
-    uint32_t* count = event_count_word(workspace, nimg, C, H * W);
+    uint32_t* count = nullptr;
+    if (masks_in) {
+      if (!workspace || ws_bytes < kMasksOrXWorkspace) return SF_ERR_WORKSPACE;
+      count = static_cast<uint32_t*>(workspace);
+    } else {
+      if (ws_bytes < event_workspace_bytes(nimg, C, H * W)) return SF_ERR_WORKSPACE;
+      count = event_count_word(workspace, nimg, C, H * W);
+    }
     s = sample_nonzeros(x, xdt, nimg * C * H * W, kDensitySamples, count, st);
     if (s != SF_OK) return s;
     gate = Gate{count, (uint32_t)std::ceil(rho * kDensitySamples), 1};
@@ -575,6 +585,21 @@ extern "C" sf_status sf_sparse_conv2d_from_masks(const void* event_masks, const 
   return run_conv(nullptr, w_packed, d->has_bias ? bias : nullptr, y, nullptr, 1, d->n, d->c_in, d->h, d->w,
                   d->c_out, d->h_out, d->w_out, d->kernel, d->stride, d->padding, d->x_dtype, d->w_dtype, false,
                   nullptr, nullptr, 0, static_cast<cudaStream_t>(stream),
+                  static_cast<const unsigned long long*>(event_masks));
+}
+
+extern "C" size_t sf_sparse_conv2d_masks_or_x_workspace_size(void) { return kMasksOrXWorkspace; }
+
+extern "C" sf_status sf_sparse_conv2d_masks_or_x(const void* x, const void* event_masks, const void* w_packed,
+                                                 const float* bias, void* y, const sf_conv_desc* d, void* workspace,
+                                                 size_t workspace_bytes, void* stream) {
+  if (!d || !event_masks || !x) return SF_ERR_INVALID_ARG;
+  if (d->has_bias && !bias) return SF_ERR_INVALID_ARG;
+  if ((reinterpret_cast<uintptr_t>(event_masks) & 15u) != 0) return SF_ERR_ALIGNMENT;
+  if (workspace && (reinterpret_cast<uintptr_t>(workspace) & 3u) != 0) return SF_ERR_ALIGNMENT;
+  return run_conv(x, w_packed, d->has_bias ? bias : nullptr, y, nullptr, 1, d->n, d->c_in, d->h, d->w, d->c_out,
+                  d->h_out, d->w_out, d->kernel, d->stride, d->padding, d->x_dtype, d->w_dtype, false, nullptr,
+                  workspace, workspace_bytes, static_cast<cudaStream_t>(stream),
                   static_cast<const unsigned long long*>(event_masks));
 }
 

@@ -200,3 +200,49 @@ def test_lif_events_bitmap_path_params(tau, v_reset):
     assert torch.equal(s_ev, s_plain) and torch.equal(ev.v, plain.v)
     want = _masks_from_spikes(s_ev.reshape(8, 64, 8, 8))
     assert torch.equal(s_ev._sf_event_masks[0].reshape(want.shape), want)
+
+
+@pytest.mark.parametrize("density,expect", [(0.001, 1), (0.05, 2)])
+def test_wide_3x3_masks_or_x_picks_a_route(density, expect):
+    """C_in 128 3x3/s1 given x and its event masks: sparse spikes run the gather kernel from the
+    masks, dense ones the tensor cores from x; the result equals that route's bit for bit and the
+    oracle within fp32 rounding."""
+    from sparseflow_b200 import _lib
+    from sparseflow_b200.Kernels.conv2d import pack_weight
+    from oracle import oracle
+    g = torch.Generator().manual_seed(int(density * 1e4))
+    x = (torch.rand(8, 128, 14, 14, generator=g) < density).float()
+    wt = torch.randn(96, 128, 3, 3, generator=g) * 0.05
+    b = torch.randn(96, generator=g) * 0.1
+    xs, wp, bs = x.cuda(), pack_weight(wt.cuda()), b.cuda()
+    masks = _masks_from_spikes(xs).contiguous()
+    y = torch.empty(8, 96, 14, 14, device="cuda")
+    _lib.sparse_conv2d_masks_or_x(xs, masks, wp, bs, y, 3, 1, 1)
+    ref = torch.empty_like(y)
+    with _lib.path_policy(_lib.SF_POLICY_CONV3X3_PATH, expect):
+        if expect == 1:
+            _lib.sparse_conv2d_from_masks(masks, tuple(xs.shape), xs.dtype, wp, bs, ref, 3, 1, 1)
+        else:
+            _lib.sparse_conv2d(xs, wp, bs, ref, 96, 3, 1, 1)
+    torch.cuda.synchronize()
+    assert torch.equal(y, ref)
+    o = oracle.conv2d(x.numpy(), wt.numpy(), b.numpy(), 1, 1)
+    assert float((y.cpu() - torch.from_numpy(o)).abs().max()) <= 2e-5 * float(abs(o).max())
+    assert _lib.conv_status(y.device) == 0
+
+
+def test_fused_lif_to_wide_3x3_through_modules():
+    """FusedSparseConvLIF (emitting masks) -> SparseConv2d C_in 128 at a firing rate above the
+    gate: the convolution runs from x on the tensor cores and equals the plain call on the spikes."""
+    from sparseflow_b200.Ops.sparse_conv2d import SparseConv2d
+    m = _fused(64, 128, 3, 11)
+    g = torch.Generator().manual_seed(3)
+    x = (torch.rand(3, 2, 64, 12, 12, generator=g) < 0.2).float().cuda()
+    s = m(x)
+    assert s._sf_event_masks is not None and float(s.mean()) > 0.01
+    conv = nn.Conv2d(128, 96, 3, 1, 1, bias=True).cuda()
+    sc = SparseConv2d.from_dense(conv, block_size=8)
+    y = sc(s)
+    plain = sc(s.clone())
+    torch.cuda.synchronize()
+    assert torch.equal(y, plain)
