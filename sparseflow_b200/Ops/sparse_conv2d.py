@@ -98,8 +98,7 @@ class SparseConv2d(nn.Module):
         # Caches (plain attributes, not buffers: state_dict matches nn.Conv2d).
         self._w_packed = None
         self._w_packed_key = None
-        self._fast_key = None  # plain-call cache (_fast_forward)
-        self._fast = None
+        self._fast = None  # plain-call cache (_plain_call)
         self._bias_key = None
         self._bias32 = None
         self._ag_mask_buf = None
@@ -163,7 +162,7 @@ class SparseConv2d(nn.Module):
         return self._pattern() in SUPPORTED_PATTERNS
 
     def _get_w_packed(self):
-        key = (self.weight._version, self.weight.data_ptr(), self.weight.dtype, self.weight.device)
+        key = (self.weight._version, self.weight.data_ptr())  # .to() gives the parameter new storage
         if self._w_packed is None or self._w_packed_key != key:
             self._w_packed = pack_weight(self.weight.data)
             self._w_packed_key = key
@@ -189,6 +188,9 @@ class SparseConv2d(nn.Module):
 
     # -- forward --------------------------------------------------------------
     def forward(self, x: torch.Tensor):
+        y = self._plain_call(x)
+        if y is not None:
+            return y
         self.fallback_reason = ""
         if self.profile_runtime:
             self._profile.calls += 1
@@ -237,44 +239,68 @@ class SparseConv2d(nn.Module):
                 setattr(self, name, torch.empty(n_tiles, dtype=torch.int32, device=x4.device))
         return n_tiles
 
-    def _fast_forward(self, x4):
-        """The plain call (no stats, timing or handed-over masks): descriptor, output shape and
-        workspace size cached per input shape, then one library call. Host time per call matters
-        for small layers (C1: ~10 us of device time)."""
-        key = (tuple(x4.shape), x4.dtype, x4.device, self.weight.dtype, self.bias is not None)
-        if self._fast_key != key:
-            n, c, h, w = x4.shape
-            ho, wo = self._output_hw(h, w)
-            wp = self._get_w_packed()
-            desc = _lib.ConvDesc(n, c, h, w, self.out_channels, ho, wo, self.kernel_size[0], self.stride[0],
-                                 self.padding[0], _lib.sf_dtype(x4.dtype), _lib.sf_dtype(wp.dtype),
-                                 int(self.bias is not None))
-            nbytes = int(_lib.load().sf_sparse_conv2d_workspace_size(ctypes.byref(desc)))
-            self._fast = (desc, nbytes, (n, self.out_channels, ho, wo))
-            self._fast_key = key
-        desc, nbytes, out_shape = self._fast
-        wp = self._get_w_packed()
-        bkey = None if self.bias is None else (self.bias._version, self.bias.data_ptr())
-        if self._bias_key != bkey:
-            self._bias32 = None if self.bias is None else self.bias.detach().to(torch.float32).contiguous()
-            self._bias_key = bkey
-        y = torch.empty(out_shape, dtype=x4.dtype, device=x4.device)
-        ws = _lib.workspace(x4.device, nbytes)
-        st = _lib.load().sf_sparse_conv2d(x4.data_ptr(), wp.data_ptr(),
-                                          None if self._bias32 is None else self._bias32.data_ptr(), y.data_ptr(),
-                                          ctypes.byref(desc), ws.data_ptr(), ws.numel(),
-                                          torch.cuda.current_stream(x4.device).cuda_stream)
-        _lib._check("sf_sparse_conv2d", st)
+    def _plain_call(self, x):
+        """The plain call, on 4-D or 5-D input: no statistics, timing, handed-over event masks or
+        dense dispatch. Descriptor, output shape and workspace size are cached per input shape,
+        the packed weights and fp32 bias per parameter version; then one library call on the
+        current stream. Host time per call matters for small layers (C1: ~10 us of device time).
+        None when the call is not a plain one."""
+        if (self.profile_runtime or self.return_ms or (self.collect_diag and not self._inference_mode)
+                or self.dispatch_backend != "sparse" or getattr(x, "_sf_event_masks", None) is not None):
+            return None
+        key = (x.shape, x.dtype, x.get_device(), self.allow_sparse_1x1)
+        c = self._fast
+        if c is None or c[0] != key:
+            c = self._plain_setup(x, key)
+            self._fast = c
+        if c[1] is None or not x.is_contiguous():
+            return None
+        _, fn, _desc, dref, nbytes, out_shape, idx = c
+        w = self.weight
+        if self._w_packed is None or self._w_packed_key != (w._version, w.data_ptr()):
+            self._get_w_packed()
+        b = self.bias
+        bp = None
+        if b is not None:
+            bkey = (b._version, b.data_ptr())
+            if self._bias_key != bkey:
+                self._bias32 = b.detach().to(torch.float32).contiguous()
+                self._bias_key = bkey
+            bp = self._bias32.data_ptr()
+        st = _lib.raw_stream(idx)
+        ws = _lib.workspace_on(idx, st, nbytes)
+        y = torch.empty(out_shape, dtype=x.dtype, device=x.device)
+        status = fn(x.data_ptr(), self._w_packed.data_ptr(), bp, y.data_ptr(), dref, ws.data_ptr(), ws.numel(), st)
+        if status != 0:
+            _lib._check("sf_sparse_conv2d", status)
+        self.fallback_reason = ""
         self._last_used_event_masks = False
         self._last_sparse_ms = 0.0
         self._last_dense_ms = 0.0
-        return y, "sparse_b200"
+        return y
+
+    def _plain_setup(self, x, key):
+        none = (key, None, None, None, None, None, None)
+        if not x.is_cuda or x.dim() not in (4, 5) or x.dtype not in (torch.float32, torch.float16, torch.bfloat16) \
+                or not self._supports_sparse():
+            return none
+        if x.dim() == 5:
+            t, bsz, c, h, w = x.shape
+            n = t * bsz
+        else:
+            n, c, h, w = x.shape
+        ho, wo = self._output_hw(h, w)
+        wp = self._get_w_packed()
+        desc = _lib.ConvDesc(n, c, h, w, self.out_channels, ho, wo, self.kernel_size[0], self.stride[0],
+                             self.padding[0], _lib.sf_dtype(x.dtype), _lib.sf_dtype(wp.dtype),
+                             int(self.bias is not None))
+        lib = _lib.load()
+        nbytes = int(lib.sf_sparse_conv2d_workspace_size(ctypes.byref(desc)))
+        out_shape = (t, bsz, self.out_channels, ho, wo) if x.dim() == 5 else (n, self.out_channels, ho, wo)
+        return (key, lib.sf_sparse_conv2d, desc, ctypes.byref(desc), nbytes, out_shape, x.get_device())
 
     def _sparse_forward(self, x4, event_masks=None):
         diag = self.collect_diag and not self._inference_mode
-        if not diag and not self.return_ms and event_masks is None and x4.is_contiguous() and \
-                x4.dtype in (torch.float32, torch.float16, torch.bfloat16):
-            return self._fast_forward(x4)
         kw = {}
         if event_masks is not None and not diag:
             kw["event_masks"] = event_masks

@@ -243,13 +243,27 @@ def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
     gets its own.
     """
     idx = device.index if device.index is not None else torch.cuda.current_device()
-    key = (idx, torch.cuda.current_stream(device).cuda_stream)
+    return workspace_on(idx, torch.cuda.current_stream(device).cuda_stream, nbytes)
+
+
+def workspace_on(idx: int, stream: int, nbytes: int) -> torch.Tensor:
+    """workspace() for a device index and a raw stream handle the caller already has."""
+    key = (idx, stream)
+    buf = _workspaces.get(key)
+    if buf is not None and buf.numel() >= nbytes:
+        return buf
     with _ws_lock:
         buf = _workspaces.get(key)
         if buf is None or buf.numel() < nbytes:
-            buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+            buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=torch.device("cuda", idx))
             _workspaces[key] = buf
     return buf
+
+
+def raw_stream(idx: int) -> int:
+    """Handle of the current stream of device idx (what torch.cuda.current_stream(idx).cuda_stream
+    returns, without building the Stream object)."""
+    return torch._C._cuda_getCurrentRawStream(idx)
 
 
 def sparse_conv2d(x: torch.Tensor, w_packed: torch.Tensor, bias: Optional[torch.Tensor], y: torch.Tensor,
