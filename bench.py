@@ -71,6 +71,9 @@ def parse():
                     help="C5 grid: C x H x density, sparse conv3x3 vs cuDNN and the HBM roofline (one JSON line per cell)")
     ap.add_argument("--sweep-images", type=int, default=T_STEPS * N_BATCH,
                     help="T*N images per sweep cell (BASELINE: T16 N64 = 1024)")
+    ap.add_argument("--cell", default=None,
+                    help="with --only-timed --kernel conv: 'C,H,density' times that C5 grid cell (C->C 3x3/s1/p1, "
+                         "HxH maps, Bernoulli spikes) instead of the headline cell; an ncu-sized case with --images")
     ap.add_argument("--images", type=int, default=T_STEPS * N_BATCH,
                     help="T*N images per step (multiple of 16); smaller values make an ncu-sized case")
     return ap.parse_args()
@@ -582,11 +585,16 @@ def main():
     n_img = args.images
     n_batch = n_img // T_STEPS
     g = torch.Generator(device=dev).manual_seed(1000 + rank)
-    x = (torch.rand(T_STEPS, n_batch, C, H, W, device=dev, generator=g) < DENSITY).float()
-    conv = make_conv(C, C, 3, 1, 1, True, 1, device=dev)
+    cc, hh, dd = C, H, DENSITY
+    if args.cell:
+        if not (args.only_timed and args.kernel == "conv"):
+            raise SystemExit("--cell needs --only-timed --kernel conv")
+        cc, hh, dd = int(args.cell.split(",")[0]), int(args.cell.split(",")[1]), float(args.cell.split(",")[2])
+    x = (torch.rand(T_STEPS, n_batch, cc, hh, hh, device=dev, generator=g) < dd).float()
+    conv = make_conv(cc, cc, 3, 1, 1, True, 1, device=dev)
     mod = SparseConv2d.from_dense(conv, block_size=16)
     mod.set_inference_mode(True)
-    step_bytes = conv_bytes(n_img, C, H, W, C, H, W, 3)
+    step_bytes = conv_bytes(n_img, cc, hh, hh, cc, hh, hh, 3)
 
     if args.only_timed and args.kernel in ("c2", "c2masks"):
         from sparseflow_b200.Ops.sparse_conv2d import SparseConv2d
