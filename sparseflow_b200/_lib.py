@@ -161,7 +161,8 @@ def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
 
 
 def _stream(device: torch.device) -> int:
-    return torch.cuda.current_stream(device).cuda_stream
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    return raw_stream(idx)
 
 
 def sf_dtype(dt: torch.dtype) -> int:
@@ -340,7 +341,7 @@ def lif_multistep(x: torch.Tensor, v: torch.Tensor, spikes: torch.Tensor, tau: f
     if v.dtype != torch.float32 or not (x.is_contiguous() and v.is_contiguous() and spikes.is_contiguous()):
         raise ValueError("lif_multistep needs contiguous tensors and an fp32 membrane")
     t = x.shape[0]
-    numel = x[0].numel() if t > 0 else v.numel()
+    numel = x.numel() // t if t > 0 else v.numel()
     if v.numel() != numel or spikes.shape != x.shape:
         raise ValueError("shape mismatch between x, v and spikes")
     desc = LifMsDesc(numel, t, float(tau), float(v_threshold), 0.0 if v_reset is None else float(v_reset),
