@@ -42,6 +42,7 @@
 // Every mbarrier wait gives up after one second (error word set, CTA
 // drains); TMEM is freed before the CTA exits. No TMA multicast.
 #include <algorithm>
+#include <cmath>
 #include <cstring>
 #include "conv_kernel.cuh"
 #include "tc_common.cuh"
@@ -55,10 +56,18 @@ using conv::mbar_arrive;
 
 // Warp roles (1024 threads): converters 0..14 (0..13 when the weights are
 // streamed, warp 14 then copies weight stages), epilogue 15..30, MMA 31.
-constexpr int kEpi0 = 15;
+// With the LIF epilogue (LM > 0) the CTA has 24 warps: converters 0..6
+// (0..5 and the weight-stage copier 6 when streamed), epilogue 7..22, MMA
+// 23. The converters have slack at one step's plane, and 768 threads leave
+// the epilogue 80 registers for the membranes of two tiles in flight.
 constexpr int kEpiWarps = 16;
-constexpr int kMmaWarp = kEpi0 + kEpiWarps;
-constexpr int kThreads = (kMmaWarp + 1) * 32;
+constexpr int kLifU = 3;  // most tiles per unit with the LIF epilogue
+template <int LM>
+constexpr int epi0() { return LM ? 7 : 15; }
+template <int LM>
+constexpr int mma_warp() { return epi0<LM>() + kEpiWarps; }
+template <int LM>
+constexpr int cta_threads() { return (mma_warp<LM>() + 1) * 32; }
 constexpr int kMaxBStages = 8;
 constexpr int kMaxKch = 16;  // 16-channel slices per weight stage
 constexpr int kM = 128;
@@ -101,6 +110,15 @@ struct Params {
   int ngb;  // TMEM group buffers (2: the epilogue of a group overlaps the next one's MMAs)
   uint32_t b_off, bstage_bytes;
   Gate gate;  // runs only when the gate selects this path
+  // Multi-step LIF epilogue (LM > 0): the plane holds the N images of one
+  // step, every unit runs t = 0..T-1 in turn (x, y of image t * N + n), and
+  // the epilogue turns the preactivation into a spike with membrane v
+  // [N, Co, H, W] (fp32, read and written by the same thread at every step).
+  int T;
+  float* v;
+  uint32_t vs_off;  // shared-memory staging of the membranes (streamed weights), or 0
+  float tau, vth, vr, inv_tau;
+  int hard, decay_input;
 };
 
 struct Bars {
@@ -129,6 +147,28 @@ __device__ __forceinline__ void st_cs(float* p, float v) { __stcs(p, v); }
 __device__ __forceinline__ void st_cs(__half* p, __half v) { __stcs(reinterpret_cast<unsigned short*>(p), __half_as_ushort(v)); }
 __device__ __forceinline__ void st_cs(__nv_bfloat16* p, __nv_bfloat16 v) {
   __stcs(reinterpret_cast<unsigned short*>(p), __bfloat16_as_ushort(v));
+}
+
+// Writes one output element: the preactivation a itself (LM = 0), or the
+// multi-step LIF update of membrane *vm with input a and its spike (LM = 1:
+// IEEE division by tau; LM = 2: multiplication by the exact reciprocal of a
+// power-of-two tau). Operation order as sf_lif_multistep's, so spikes equal
+// those of the convolution followed by that kernel bit for bit.
+template <int LM, typename XT>
+__device__ __forceinline__ void emit(XT* y, float* vm, float vold, float a, const Params& p) {
+  if constexpr (LM == 0) {
+    st_cs(y, DT<XT>::from_f(a));
+  } else {
+    float h;
+    if (p.decay_input)
+      h = LM == 2 ? vold + __fmul_rn(a - (vold - p.vr), p.inv_tau) : vold + __fdiv_rn(a - (vold - p.vr), p.tau);
+    else
+      h = LM == 2 ? __fadd_rn(vold - __fmul_rn(vold - p.vr, p.inv_tau), a)
+                  : __fadd_rn(vold - __fdiv_rn(vold - p.vr, p.tau), a);
+    const bool s = h >= p.vth;
+    *vm = p.hard ? (s ? p.vr : h) : (h - (s ? p.vth : 0.f));
+    st_cs(y, DT<XT>::from_f(s ? 1.f : 0.f));
+  }
 }
 
 template <typename WT>
@@ -185,6 +225,21 @@ __device__ __forceinline__ void convert_unit_scalar(const Params& p, const XT* _
 // positions x 8 channels), tests x*x == x (true exactly for 0 and 1; -0
 // counts as 0, NaN fails) and writes the 8-byte halves of four A rows. The
 // two padding columns of each row are written as zeros by a separate loop.
+// 16-byte load that does not allocate in L1 (NA) or the default __ldg.
+template <bool NA>
+__device__ __forceinline__ float4 ld_x4(const float4* p) {
+  if constexpr (NA) {
+    float4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p));
+    return v;
+  } else {
+    return __ldg(p);
+  }
+}
+
+template <bool NA>
 __device__ __forceinline__ void convert_unit_vec4(const Params& p, const float* __restrict__ x, unsigned char* ab,
                                                   long long q0, int warp, int lane, int nconv, uint32_t& nb) {
   const uint32_t HW = (uint32_t)(p.H * p.W);
@@ -217,10 +272,10 @@ __device__ __forceinline__ void convert_unit_vec4(const Params& p, const float* 
       const int ne = min(8, p.C - c0);
       if (ne == 8) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) v[e] = __ldg(src + e * step);
+        for (int e = 0; e < 8; ++e) v[e] = ld_x4<NA>(src + e * step);
       } else {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) v[e] = e < ne ? __ldg(src + e * step) : make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int e = 0; e < 8; ++e) v[e] = e < ne ? ld_x4<NA>(src + e * step) : make_float4(0.f, 0.f, 0.f, 0.f);
       }
     } else {
 #pragma unroll
@@ -268,11 +323,12 @@ __device__ __forceinline__ void convert_unit_vec4(const Params& p, const float* 
 
 // One tile's epilogue for the warp's channels [cbeg, cbeg + cwq) of output
 // block cob: D (three digit planes at TMEM column dcol) -> y, or, for a unit
-// holding values other than 0 / 1, fp32 FMAs from x and the weights.
-template <typename XT, typename WT>
-__device__ __forceinline__ void epilogue_tile(const Params& p, const XT* __restrict__ x, uint32_t tmem, uint32_t dcol,
-                                              long long tile, int cob, int qd, int lane, int cbeg, int cwq, int nco,
-                                              const float2* tab, bool odd) {
+// holding values other than 0 / 1, fp32 FMAs from x and the weights. x and
+// ybase are those of the unit's step; vbase is the LIF membrane (LM > 0).
+template <typename XT, typename WT, int LM>
+__device__ __forceinline__ void epilogue_tile(const Params& p, const XT* __restrict__ x, XT* ybase, float* vbase,
+                                              uint32_t tmem, uint32_t dcol, long long tile, int cob, int qd,
+                                              int lane, int cbeg, int cwq, int nco, const float2* tab, bool odd) {
   const size_t HW = (size_t)p.H * p.W;
   const uint32_t o = (uint32_t)(tile * kM) + qd * 32 + lane;
   const uint32_t Ro = fdiv(o, p.fd_wp);
@@ -281,7 +337,9 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const XT* __restr
   const int h = (int)(Ro - img * p.Hs);
   const bool valid = c < p.W && h < p.H && img < (uint32_t)p.N;
   const int cbase = cob * p.CB + cbeg;
-  XT* yp = static_cast<XT*>(p.y) + ((size_t)img * p.Co + cbase) * HW + (size_t)h * p.W + c;
+  const size_t off = ((size_t)img * p.Co + cbase) * HW + (size_t)h * p.W + c;
+  XT* yp = ybase + off;
+  float* vp = LM ? vbase + off : nullptr;
   if (!odd && nco == cwq) {
     // Every channel of the warp's quarter exists (cwq is 8 or 16): no
     // per-element bounds checks. The arithmetic is the one below.
@@ -295,14 +353,16 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const XT* __restr
       tc::tmem_wait_ld();
       if (valid) {
         XT* yc = yp + (size_t)c8 * HW;
+        float* vc = LM ? vp + (size_t)c8 * HW : nullptr;
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           const float4 sb = tb[(c8 + e) >> 1];
           const float x01 = __int2float_rn((int)r0[e] * 256 + (int)r1[e]);
           const float x2 = __int_as_float((int)r2[e] + 0x4B400000) - 12582912.f;
           const float v = fmaf((e & 1) ? sb.z : sb.x, fmaf(x01, 256.f, x2), (e & 1) ? sb.w : sb.y);
-          st_cs(yc, DT<XT>::from_f(v));
+          emit<LM>(yc, vc, LM ? *vc : 0.f, v, p);
           yc += HW;
+          if (LM) vc += HW;
         }
       }
     }
@@ -331,7 +391,10 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const XT* __restr
             const float x2 = __int_as_float((int)r2[e + f] + 0x4B400000) - 12582912.f;
             const float v = fmaf(f ? sb.z : sb.x, fmaf(x01, 256.f, x2), f ? sb.w : sb.y);
             // Evict-first stores: y is not read again here (1.7 % faster on the C5 cell).
-            if (c8 + e + f < nco) st_cs(yp + (uint32_t)(c8 + e + f) * (uint32_t)HW, DT<XT>::from_f(v));
+            if (c8 + e + f < nco) {
+              const uint32_t o2 = (uint32_t)(c8 + e + f) * (uint32_t)HW;
+              emit<LM>(yp + o2, LM ? vp + o2 : nullptr, LM ? vp[o2] : 0.f, v, p);
+            }
           }
         }
       }
@@ -349,8 +412,74 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const XT* __restr
           if (xv != 0.f) acc = fmaf(xv, gather_w<WT>(p, co, ci, tap), acc);
         }
       }
-      yp[(size_t)cc * HW] = DT<XT>::from_f(acc + (p.bias ? __ldg(p.bias + co) : 0.f));
+      const float a = acc + (p.bias ? __ldg(p.bias + co) : 0.f);
+      if constexpr (LM == 0)
+        yp[(size_t)cc * HW] = DT<XT>::from_f(a);
+      else
+        emit<LM>(yp + (size_t)cc * HW, vp + (size_t)cc * HW, vp[(size_t)cc * HW], a, p);
     }
+  }
+}
+
+// LIF epilogue over 8 full channels (streamed weights: cwq = 8), in two
+// halves so the membrane loads of the next tile overlap this one: lif_v_load
+// fetches a tile's 8 membranes of this thread; lif_tile8 combines the digit
+// planes and updates them (the arithmetic of epilogue_tile).
+struct TilePos {
+  uint32_t off;  // within one step (N * Co * H * W < 2^32, checked on the host)
+  bool valid;
+};
+__device__ __forceinline__ TilePos tile_pos(const Params& p, long long tile, int cob, int qd, int lane, int cbeg) {
+  const size_t HW = (size_t)p.H * p.W;
+  const uint32_t o = (uint32_t)(tile * kM) + qd * 32 + lane;
+  const uint32_t Ro = fdiv(o, p.fd_wp);
+  const int c = (int)(o - Ro * p.Wp);
+  const uint32_t img = fdiv(Ro, p.fd_hs);
+  const int h = (int)(Ro - img * p.Hs);
+  TilePos t;
+  t.valid = c < p.W && h < p.H && img < (uint32_t)p.N;
+  t.off = ((uint32_t)img * (uint32_t)p.Co + (uint32_t)(cob * p.CB + cbeg)) * (uint32_t)HW + (uint32_t)(h * p.W + c);
+  return t;
+}
+// Copies a tile's 8 membranes of this thread into its shared-memory slab
+// (8 floats 32 apart) with asynchronous 4-byte copies: no registers wait on
+// them. Each thread reads back only what it copied itself.
+__device__ __forceinline__ void lif_v_stage(const Params& p, const TilePos& tp, float* slab) {
+  if (!tp.valid) return;
+  const uint32_t HW = (uint32_t)(p.H * p.W);
+  const float* vp = p.v + tp.off;
+#pragma unroll
+  for (int e = 0; e < 8; ++e)
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(slab + e * 32)), "l"(vp + e * HW)
+                 : "memory");
+}
+template <typename XT, int LM>
+__device__ __forceinline__ void lif_tile8(const Params& p, XT* ybase, const TilePos& tp, uint32_t ta,
+                                          const float* vo, const float2* tab) {
+  const size_t HW = (size_t)p.H * p.W;
+  // Two TMEM round trips (D0, D1 then D2) keep 16 registers in flight
+  // rather than 24, so the next tile's membranes stay in registers.
+  uint32_t r0[8], r1[8];
+  tc::tmem_ld8(ta, r0);
+  tc::tmem_ld8(ta + (uint32_t)p.CB, r1);
+  tc::tmem_wait_ld();
+  float x01[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) x01[e] = __int2float_rn((int)r0[e] * 256 + (int)r1[e]);
+  tc::tmem_ld8(ta + (uint32_t)(2 * p.CB), r0);
+  tc::tmem_wait_ld();
+  if (!tp.valid) return;
+  const float4* tb = reinterpret_cast<const float4*>(tab);
+  XT* yc = ybase + tp.off;
+  float* vc = p.v + tp.off;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const float4 sb = tb[e >> 1];
+    const float x2 = __int_as_float((int)r0[e] + 0x4B400000) - 12582912.f;
+    const float a = fmaf((e & 1) ? sb.z : sb.x, fmaf(x01[e], 256.f, x2), (e & 1) ? sb.w : sb.y);
+    emit<LM>(yc, vc, vo[e * 32], a, p);
+    yc += HW;
+    vc += HW;
   }
 }
 
@@ -395,8 +524,10 @@ __device__ __forceinline__ void issue_stage_n(int pk, uint32_t dt0, uint32_t n3,
   }
 }
 
-template <typename XT, typename WT, bool VEC, bool STREAM>
-__global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p) {
+template <typename XT, typename WT, bool VEC, bool STREAM, int LM>
+__global__ void __launch_bounds__(cta_threads<LM>(), 1) conv3x3_tc_kernel(const Params p) {
+  constexpr int kEpi0 = epi0<LM>();
+  constexpr int kMmaWarp = mma_warp<LM>();
   constexpr int kConv = STREAM ? kEpi0 - 1 : kEpi0;  // converter warps
   constexpr int kProducer = kEpi0 - 1;              // weight-stage copier (STREAM)
   if (!gate_open(p.gate)) return;  // uniform across the grid: before any barrier or TMEM allocation
@@ -407,14 +538,25 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const long long u0 = (long long)blockIdx.x * p.units_per_cta;
   const long long u1 = min(p.nunits, u0 + p.units_per_cta);
-  const int nu = (int)max(0ll, u1 - u0);
+  // Every role walks the CTA's units in order, each T times (t = 0..T-1)
+  // with the LIF epilogue, once otherwise: nu steps, step i = unit
+  // u0 + i / TT at t = i % TT.
+  const int TT = LM ? p.T : 1;
+  const int nu = (int)max(0ll, u1 - u0) * TT;
   const XT* __restrict__ x = static_cast<const XT*>(p.x);
+  const size_t step_elems = (size_t)p.N * p.H * p.W;  // per channel, one step
   // Unit u: tiles [t0, t0 + nt) of output block cob (resident weights), or of
   // every block in turn (streamed weights: then cob of the unit is 0).
   auto unit_of = [&](long long u, int& cob, long long& t0, int& nt) {
     cob = STREAM ? 0 : (int)fdiv((uint32_t)u, p.fd_upcob);
     t0 = (u - (long long)cob * p.upcob) * p.U;
     nt = (int)min((long long)p.U, p.ntiles - t0);
+  };
+  // Step i: its unit, its t, and the tag key (unique per step of the grid).
+  auto step_of = [&](int i, long long& u, int& t) {
+    const int iu = LM ? i / TT : i;
+    t = i - iu * TT;
+    u = u0 + iu;
   };
 
   if (tid == 0) {
@@ -463,9 +605,10 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
         int cur_cob = -1, bloads = 0;
         long long g = 0;  // tiles issued by this CTA
         for (int i = 0; i < nu && !failed; ++i) {
-          int cob, nt;
-          long long t0;
-          unit_of(u0 + i, cob, t0, nt);
+          int cob, nt, ts;
+          long long t0, uu;
+          step_of(i, uu, ts);
+          unit_of(uu, cob, t0, nt);
           if (cob != cur_cob) {
             if (cur_cob >= 0) {
               // Every MMA reading the old weights must finish before they are replaced.
@@ -529,9 +672,10 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
         int s = 0;                          // weight stage slot
         uint32_t sphase = 0;                // its mbarrier phase (flips at each ring wrap)
         for (int i = 0; i < nu && !failed; ++i) {
-          int cob0, nt;
-          long long t0;
-          unit_of(u0 + i, cob0, t0, nt);
+          int cob0, nt, ts;
+          long long t0, uu;
+          step_of(i, uu, ts);
+          unit_of(uu, cob0, t0, nt);
           const int a = i % p.nA;
           {
             PROF_T0();
@@ -622,10 +766,15 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
       tab_cob = cob;
     };
     for (int i = 0; i < nu && !failed; ++i) {
-      const long long u = u0 + i;
+      long long u;
+      int ts;
+      step_of(i, u, ts);
+      const long long key = u * TT + ts;
       int cob0, nt;
       long long t0;
       unit_of(u, cob0, t0, nt);
+      const XT* xs = x + (size_t)ts * p.C * step_elems;
+      XT* ys = static_cast<XT*>(p.y) + (size_t)ts * p.Co * step_elems;
       if constexpr (!STREAM) {
         load_tab(cob0);
         const int nco = min(cwq, p.Co - (cob0 * p.CB + cbeg));  // valid channels of this warp (may be <= 0)
@@ -636,8 +785,9 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
             break;
           }
           tc::fence_after();
-          const bool odd = *reinterpret_cast<volatile uint32_t*>(&bars->tag[u % kTags]) == (uint32_t)(u + 1);
-          epilogue_tile<XT, WT>(p, x, tmem, (uint32_t)(d * p.N3), t0 + j, cob0, qd, lane, cbeg, cwq, nco, tab, odd);
+          const bool odd = *reinterpret_cast<volatile uint32_t*>(&bars->tag[key % kTags]) == (uint32_t)(key + 1);
+          epilogue_tile<XT, WT, LM>(p, xs, ys, p.v, tmem, (uint32_t)(d * p.N3), t0 + j, cob0, qd, lane, cbeg, cwq,
+                                    nco, tab, odd);
           tc::fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&bars->d_empty[d]);
@@ -648,15 +798,54 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
           const int nco = min(cwq, p.Co - (cob * p.CB + cbeg));
           const int gb = p.ngb == 2 ? (int)(g & 1) : 0;
           const long long gr = p.ngb == 2 ? (g >> 1) : g;
+          auto dcol = [&](int j) { return (uint32_t)((gb * p.U + j) * p.N3); };  // TMEM column of tile j
+          // LIF over full 8-channel groups: the membranes of all the group's
+          // tiles (at most kLifU) load before the wait for D, so their L2
+          // latency hides behind the MMAs.
+          const bool lif8 = LM != 0 && p.vs_off != 0 && cwq == 8 && nco == 8 && nt <= kLifU;
+          float* slab = reinterpret_cast<float*>(smem + p.vs_off) + ew * (kLifU * 8 * 32) + lane;
+          TilePos tp[kLifU];
+          if (lif8) {
+#pragma unroll
+            for (int j = 0; j < kLifU; ++j) {
+              if (j < nt) {
+                tp[j] = tile_pos(p, t0 + j, cob, qd, lane, cbeg);
+                lif_v_stage(p, tp[j], slab + j * 256);
+              }
+            }
+            asm volatile("cp.async.commit_group;" ::: "memory");
+          }
+#ifdef SF_C3TC_PROF
+          const long long pw0 = clock64();
+#endif
           if (!tc::mbar_wait_sleep(&bars->d_full[gb], (uint32_t)(gr & 1))) {
             failed = true;
             break;
           }
+#ifdef SF_C3TC_PROF
+          const long long pw1 = clock64();
+          if (lane == 0) atomicAdd(&g_c3tc_prof[5], (unsigned long long)(pw1 - pw0));
+#endif
           tc::fence_after();
-          const bool odd = *reinterpret_cast<volatile uint32_t*>(&bars->tag[u % kTags]) == (uint32_t)(u + 1);
-          for (int j = 0; j < nt; ++j)
-            epilogue_tile<XT, WT>(p, x, tmem, (uint32_t)((gb * p.U + j) * p.N3), t0 + j, cob, qd, lane, cbeg, cwq,
-                                  nco, tab, odd);
+          const bool odd = *reinterpret_cast<volatile uint32_t*>(&bars->tag[key % kTags]) == (uint32_t)(key + 1);
+          if (lif8) asm volatile("cp.async.wait_group 0;" ::: "memory");
+          if (lif8 && !odd) {
+#pragma unroll
+            for (int j = 0; j < kLifU; ++j) {
+              if (j < nt) {
+                lif_tile8<XT, LM>(p, ys, tp[j], tmem + ((uint32_t)(qd * 32) << 16) + dcol(j) + cbeg, slab + j * 256,
+                                  tab);
+              }
+            }
+          } else {
+            for (int j = 0; j < nt; ++j) {
+              epilogue_tile<XT, WT, LM>(p, xs, ys, p.v, tmem, dcol(j), t0 + j, cob, qd, lane, cbeg, cwq, nco, tab,
+                                        odd);
+            }
+          }
+#ifdef SF_C3TC_PROF
+          if (lane == 0) atomicAdd(&g_c3tc_prof[4], (unsigned long long)(clock64() - pw1));
+#endif
           tc::fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&bars->d_empty[gb]);
@@ -694,10 +883,14 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
     __syncwarp();
   } else {
     for (int i = 0; i < nu && !failed; ++i) {
-      const long long u = u0 + i;
+      long long u;
+      int ts;
+      step_of(i, u, ts);
+      const long long key = u * TT + ts;
       int cob, nt;
       long long t0;
       unit_of(u, cob, t0, nt);
+      const XT* xs = x + (size_t)ts * p.C * step_elems;
       const int na = STREAM ? p.nA : 2;
       const int a = i % na;
       if (i >= na && !tc::mbar_wait_sleep(&bars->a_empty[a], (uint32_t)(((i / na) - 1) & 1))) {
@@ -707,11 +900,13 @@ __global__ void __launch_bounds__(kThreads, 1) conv3x3_tc_kernel(const Params p)
       unsigned char* ab = abuf + (size_t)a * p.a_bytes;
       uint32_t nb = 0u;
       if constexpr (VEC)
-        convert_unit_vec4(p, reinterpret_cast<const float*>(x), ab, t0 * kM, warp, lane, kConv, nb);
+        // The LIF kernels keep x out of L1, which then holds the
+        // epilogue's spilled membranes.
+        convert_unit_vec4<LM != 0>(p, reinterpret_cast<const float*>(xs), ab, t0 * kM, warp, lane, kConv, nb);
       else
-        convert_unit_scalar<XT>(p, x, ab, t0 * kM, warp, lane, kConv, nb);
+        convert_unit_scalar<XT>(p, xs, ab, t0 * kM, warp, lane, kConv, nb);
       if (__any_sync(0xffffffffu, nb != 0u) && lane == 0)
-        *reinterpret_cast<volatile uint32_t*>(&bars->tag[u % kTags]) = (uint32_t)(u + 1);
+        *reinterpret_cast<volatile uint32_t*>(&bars->tag[key % kTags]) = (uint32_t)(key + 1);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->a_full[a]);
@@ -816,18 +1011,30 @@ Geo geometry(int Co, int C) {
   return g;
 }
 
-template <typename XT, typename WT>
-sf_status launch(Params p, size_t smem, cudaStream_t st) {
+template <typename XT, typename WT, int LM>
+sf_status launch_lm(const Params& p, size_t smem, cudaStream_t st) {
   // 16-byte row loads: fp32 rows of a multiple of 4 values, 16-byte aligned x.
   const bool vec = std::is_same<XT, float>::value && p.W % 4 == 0 &&
                    (reinterpret_cast<uintptr_t>(p.x) & 15u) == 0;
   const bool stream = p.nbs > 0;
-  auto kern = stream ? (vec ? conv3x3_tc_kernel<XT, WT, true, true> : conv3x3_tc_kernel<XT, WT, false, true>)
-                     : (vec ? conv3x3_tc_kernel<XT, WT, true, false> : conv3x3_tc_kernel<XT, WT, false, false>);
+  auto kern = stream ? (vec ? conv3x3_tc_kernel<XT, WT, true, true, LM> : conv3x3_tc_kernel<XT, WT, false, true, LM>)
+                     : (vec ? conv3x3_tc_kernel<XT, WT, true, false, LM> : conv3x3_tc_kernel<XT, WT, false, false, LM>);
   if (!allow_max_smem(reinterpret_cast<const void*>(kern))) return SF_ERR_CUDA;
   const long long grid = (p.nunits + p.units_per_cta - 1) / p.units_per_cta;
-  kern<<<(unsigned)grid, kThreads, smem, st>>>(p);
+  kern<<<(unsigned)grid, cta_threads<LM>(), smem, st>>>(p);
   return cudaGetLastError() == cudaSuccess ? SF_OK : SF_ERR_CUDA;
+}
+
+// LM from the parameters: 0 without a membrane, 2 for a power-of-two tau
+// (p.inv_tau set), 1 otherwise.
+template <typename XT, typename WT>
+sf_status launch(const Params& p, size_t smem, cudaStream_t st) {
+  if (p.v == nullptr) return launch_lm<XT, WT, 0>(p, smem, st);
+  if constexpr (std::is_same<XT, float>::value) {  // fp32 spike buffers only
+    if (p.inv_tau != 0.f) return launch_lm<XT, WT, 2>(p, smem, st);
+    return launch_lm<XT, WT, 1>(p, smem, st);
+  }
+  return SF_ERR_UNSUPPORTED;
 }
 
 template <typename XT>
@@ -870,7 +1077,7 @@ sf_status tc3_pack(const void* w, int src_dtype, int Co, int C, void* section, c
 namespace {
 // Launch plan (geometry, unit size, shared-memory layout, TMEM columns);
 // false for shapes the kernel does not take.
-bool plan_tc(Params& p, size_t& smem_out, int N, int C, int H, int W, int Co) {
+bool plan_tc(Params& p, size_t& smem_out, int N, int C, int H, int W, int Co, bool lif = false) {
   if (!tc3_packs(Co, C, 3)) return false;
   const Geo g = geometry(Co, C);
   p.N = N; p.C = C; p.H = H; p.W = W; p.Co = Co;
@@ -968,10 +1175,57 @@ bool plan_tc(Params& p, size_t& smem_out, int N, int C, int H, int W, int Co) {
   // Small problems: fewer tiles per unit until every SM has a unit (C1, 32
   // images of 32x32: 281 tiles, 71 four-tile units for 148 SMs).
   const int sms = num_sms_current_device();
+  const int u_max = lif ? std::min(U, kLifU) : U;
   while (U > 1 && (p.ntiles + U - 1) / U * (p.nbs > 0 ? 1 : p.ncob) < sms) {
     --U;
     p.rows_a = rows_for(U);
     p.a_plane = p.rows_a * 16;
+  }
+  if (lif) {
+    // With the LIF epilogue each CTA runs its units T times over one step's
+    // plane, which is small (C3: 435 tiles for 148 SMs): fewer tiles per unit
+    // where that lowers the most tiles any CTA gets (C3: 3-tile units, 3 per
+    // CTA, against 2 x 2 with 2-tile units).
+    auto most = [&](int u) {
+      const long long units = (p.ntiles + u - 1) / u * (p.nbs > 0 ? 1 : p.ncob);
+      const long long ctas = std::min<long long>(units, sms);
+      return (units + ctas - 1) / ctas * u;
+    };
+    int best = u_max;
+    for (int u = u_max - 1; u >= 1; --u)
+      if (most(u) < most(best)) best = u;
+    U = best;
+#ifdef SF_DEV_KNOBS
+    if (const char* e = getenv("SF_C3TC_LIF_U")) U = std::max(1, std::min(u_max, atoi(e)));
+#endif
+    p.rows_a = rows_for(U);
+    p.a_plane = p.rows_a * 16;
+    if (p.nbs > 0) {
+      // Streamed weights: [A buffers][membrane slabs][weight stages][barriers],
+      // the most weight stages (2..8) that fit, two A buffers if possible.
+      const size_t a_bytes = (size_t)p.rows_a * 16 * g.kcores;
+      const size_t vs_bytes = (size_t)kEpiWarps * kLifU * 8 * 32 * 4;
+      bool ok = false;
+      for (int na = 2; na >= 1 && !ok; --na) {
+        for (int nbs = kMaxBStages; nbs >= 2 && !ok; --nbs) {
+          const size_t vs_off = (size_t)na * a_bytes;
+          const size_t b_off = vs_off + vs_bytes;
+          const size_t bar_off = (b_off + (size_t)nbs * p.bstage_bytes + 127) / 128 * 128;
+          const size_t total = bar_off + sizeof(Bars);
+          if (total <= limit) {
+            ok = true;
+            p.a_bytes = (uint32_t)a_bytes;
+            p.nA = na;
+            p.nbs = nbs;
+            p.vs_off = (uint32_t)vs_off;
+            p.b_off = (uint32_t)b_off;
+            p.bar_off = (uint32_t)bar_off;
+            smem = total;
+          }
+        }
+      }
+      if (!ok) p.vs_off = 0;  // direct membrane loads (the general epilogue)
+    }
   }
   smem = std::max<size_t>(smem, 120 * 1024);  // one CTA (and one TMEM allocation) per SM
   p.U = U;
@@ -1003,14 +1257,38 @@ bool tc3_supported(int N, int C, int H, int W, int Co) {
   return plan_tc(p, smem, N, C, H, W, Co);
 }
 
+namespace {
+// 1 / tau when tau is a power of two with a normal reciprocal, else 0.
+float pow2_reciprocal(float tau) {
+  int e = 0;
+  const float m = std::frexp(std::fabs(tau), &e);
+  if (m != 0.5f || e < -124 || e > 126) return 0.f;
+  return 1.f / tau;
+}
+}  // namespace
+
 sf_status run_conv3x3_tc(const void* x, const void* w_gather, int cpl, const void* section, const float* bias,
                          void* y, uint32_t* err, int N, int C, int H, int W, int Co, int xdt, int wdt,
-                         cudaStream_t st, const Gate& gate) {
+                         cudaStream_t st, const Gate& gate, const TcLif* lif) {
   if (wdt != SF_DTYPE_F32 && wdt != SF_DTYPE_BF16) return SF_ERR_UNSUPPORTED;
   Params p;
   memset(&p, 0, sizeof(p));
   size_t smem = 0;
-  if (!plan_tc(p, smem, N, C, H, W, Co)) return SF_ERR_UNSUPPORTED;
+  if (lif) {
+    if (lif->T < 1 || !lif->v || N % lif->T != 0 || !(lif->tau != 0.f)) return SF_ERR_INVALID_ARG;
+    // The plane holds one step's images; units repeat over the T steps.
+    if (!plan_tc(p, smem, N / lif->T, C, H, W, Co, true)) return SF_ERR_UNSUPPORTED;
+    p.T = lif->T;
+    p.v = lif->v;
+    p.tau = lif->tau;
+    p.inv_tau = pow2_reciprocal(lif->tau);
+    p.vth = lif->v_threshold;
+    p.hard = lif->hard_reset;
+    p.vr = lif->hard_reset ? lif->v_reset : 0.f;
+    p.decay_input = lif->decay_input;
+  } else if (!plan_tc(p, smem, N, C, H, W, Co)) {
+    return SF_ERR_UNSUPPORTED;
+  }
   const Geo g = geometry(Co, C);
   p.x = x;
   p.scales = static_cast<const float*>(section);

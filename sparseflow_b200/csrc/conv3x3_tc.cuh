@@ -22,10 +22,20 @@ sf_status tc3_pack(const void* w_oihw, int src_dtype, int Co, int C, void* secti
 // Whether the kernel can run this shape (shared memory, TMEM, 32-bit
 // position decode); run_conv3x3_tc returns SF_ERR_UNSUPPORTED otherwise.
 bool tc3_supported(int N, int C, int H, int W, int Co);
-// Runs the convolution (when `gate` selects it).
+// Multi-step LIF applied in the epilogue: the N images are T steps of N / T
+// images each (image t * N / T + n), v is the fp32 membrane [N / T, Co, H, W]
+// (state in and out) and y receives the spikes instead of the convolution.
+struct TcLif {
+  int T;
+  float* v;
+  float tau, v_threshold, v_reset;
+  int hard_reset, decay_input;
+};
+// Runs the convolution (when `gate` selects it); with `lif`, the fused
+// convolution + multi-step LIF.
 sf_status run_conv3x3_tc(const void* x, const void* w_gather, int cpl, const void* section, const float* bias,
                          void* y, uint32_t* err, int N, int C, int H, int W, int Co, int xdt, int wdt,
-                         cudaStream_t st, const Gate& gate);
+                         cudaStream_t st, const Gate& gate, const TcLif* lif = nullptr);
 
 }  // namespace c3tc
 }  // namespace sf

@@ -343,14 +343,26 @@ sf_status run_conv(const void* x, const void* w_packed, const float* bias, void*
   const bool tc_shape = (!masks_in || x) && K == 3 && S == 1 && P == 1 && pol3 != 1 && c3tc::tc3_packs(Co, C, K) &&
                         (wdt == SF_DTYPE_F32 || wdt == SF_DTYPE_BF16) &&
                         c3tc::tc3_supported(T * N, C, H, W, Co);
-  // Fused conv + LIF: the tensor-core kernel writes the fp32 preactivations
-  // into the spike buffer and the multi-step LIF runs over them in place (v,
-  // spikes and event masks as the fused gather kernel writes them). fp32
-  // spikes only: a 16-bit buffer would round the preactivations.
+  // Fused conv + LIF: the tensor-core kernel with the multi-step LIF in its
+  // epilogue; when the caller wants the spikes' event masks, the kernel
+  // writes the fp32 preactivations into the spike buffer and the multi-step
+  // LIF with mask emission runs over them in place (v, spikes and event masks
+  // as the fused gather kernel writes them). fp32 spikes only: a 16-bit
+  // buffer would round the preactivations.
   const bool lif_tc = lif && tc_shape && xdt == SF_DTYPE_F32;
   auto tc_then_lif = [&](const Gate& g, cudaStream_t sx) -> sf_status {
     const int wsz = (int)dtype_size(wdt);
     const void* section = static_cast<const char*>(w_packed) + tc_section_offset(Co, C, K, wsz);
+    if (lif && !mask_out && !dev_knob("SF_LIF_TC_UNFUSED")) {
+      // One launch: the LIF runs in the tensor-core kernel's epilogue (unit
+      // by unit over t = 0..T-1, the membrane read and written by the same
+      // thread each step, kept in L2 between steps), so the preactivations
+      // never reach memory.
+      const c3tc::TcLif tl{T, v, lifd->tau, lifd->v_threshold, lifd->v_reset, lifd->hard_reset, lifd->decay_input};
+      sf_status r = c3tc::run_conv3x3_tc(x, w_packed, weight_block_cpl(C, K, Co, wsz), section, bias, y,
+                                         conv_error_word(), T * N, C, H, W, Co, xdt, wdt, sx, g, &tl);
+      if (r != SF_ERR_UNSUPPORTED) return r;
+    }
     sf_status r = c3tc::run_conv3x3_tc(x, w_packed, weight_block_cpl(C, K, Co, wsz), section, bias, y,
                                        conv_error_word(), T * N, C, H, W, Co, xdt, wdt, sx, g);
     if (r != SF_OK || !lif) return r;

@@ -122,10 +122,14 @@ def test_fused_lif_tau_values_match_oracle(tau):
     assert np.abs(v.cpu().numpy() - vo).max() < 1e-4
 
 
-def test_fused_conv_bn_lif_full_size_c3_vs_cudnn_path():
+@pytest.mark.parametrize("policy", [0, 2])
+def test_fused_conv_bn_lif_full_size_c3_vs_cudnn_path(policy):
     """Full C3 workload (T=16, N=64, C=128, 28x28, p=0.005, BN folded, tau=2 hard reset): spikes
     equal the cuDNN-fp32 conv + BN + LIF formula except where that path's membrane is within
-    1e-5 of the threshold; final membranes within 1e-4."""
+    1e-5 of the threshold; final membranes within 1e-4. Policy 0 lets the density gate choose
+    (the fused gather kernel at this density), 2 forces the tensor-core kernel with the LIF in
+    its epilogue."""
+    from sparseflow_b200 import _lib
     from sparseflow_b200.Ops.sparse_fused_conv_lif import FusedSparseConvLIF
     from sparseflow_b200.Ops.lif_node import LIFNode
     g = torch.Generator(device="cuda").manual_seed(3)
@@ -138,7 +142,8 @@ def test_fused_conv_bn_lif_full_size_c3_vs_cudnn_path():
     bn.running_mean = torch.randn(128, device="cuda", generator=g) * 0.1
     bn.running_var = torch.rand(128, device="cuda", generator=g) + 0.5
     m = FusedSparseConvLIF.from_conv_bn_lif(conv, bn, LIFNode(tau=2.0, v_threshold=1.0, v_reset=0.0))
-    s = m(x)
+    with _lib.path_policy(_lib.SF_POLICY_CONV3X3_PATH, policy):
+        s = m(x)
     prev = torch.backends.cudnn.allow_tf32
     torch.backends.cudnn.allow_tf32 = False
     try:

@@ -89,3 +89,28 @@ def test_lif_tensor_core_route_keeps_16bit_spikes_on_gather():
     a = _run(x, wt, None, v0, 2.0, 0.0, True, 2)
     f = _run(x, wt, None, v0, 2.0, 0.0, True, 1)
     assert torch.equal(a[0], f[0]) and torch.equal(a[1], f[1])
+
+
+@pytest.mark.parametrize("t,n,c,co,h,w,density,tau,vr,decay", CASES + [
+    (5, 3, 128, 128, 28, 28, 0.02, 2.0, 0.0, True),   # C3-like map: three-tile units, tile ring
+    (3, 2, 256, 96, 14, 14, 0.05, 3.0, 0.0, False),   # non power-of-two tau (IEEE division)
+])
+def test_lif_in_tensor_core_epilogue_equals_two_launch_route(t, n, c, co, h, w, density, tau, vr, decay):
+    """Without event masks the tensor-core route runs the LIF in the convolution's epilogue (one
+    launch; the membrane stays in L2 between steps). Spikes and membrane equal, bit for bit, the
+    route that writes the preactivations and runs the multi-step LIF over them (taken when masks
+    are asked for), and the spikes follow the oracle's near-threshold rule."""
+    g = torch.Generator().manual_seed(t * 7 + c + co)
+    x = (torch.rand(t, n, c, h, w, generator=g) < density).float()
+    wt = torch.randn(co, c, 3, 3, generator=g) * (3.0 / (c * 9 * density)) ** 0.5
+    b = torch.randn(co, generator=g) * 0.2
+    v0 = torch.rand(n, co, h, w, generator=g) * 0.5
+    xs, ws, bs, vs = x.cuda(), wt.cuda(), b.cuda(), v0.cuda()
+    s_f, v_f, _ = _run(xs, ws, bs, vs, tau, vr, decay, 2, masks=False)
+    s_m, v_m, _ = _run(xs, ws, bs, vs, tau, vr, decay, 2, masks=True)
+    assert torch.equal(s_f, s_m) and torch.equal(v_f, v_m)
+    so, near, vo = oracle.conv_lif_near(x.numpy(), wt.numpy(), b.numpy(), v0.numpy(), 1, 1, tau, 1.0, vr, decay)
+    assert 0.01 < so.mean() < 0.9
+    assert oracle.spikes_match(s_f.cpu().numpy(), so, near)
+    assert np.abs(v_f.cpu().numpy() - vo).max() < 1e-4
+
