@@ -271,7 +271,13 @@ enum {
   SF_POLICY_CONV3X3_PATH = 2,
   /* 1: sf_lif_multistep_events always uses its general lane-per-pixel kernel. */
   SF_POLICY_LIF_EVENTS_GENERAL = 3,
-  SF_POLICY_COUNT = 4
+  /* Fused conv + LIF on the tcgen05 3x3 kernel without event masks: 0
+   * automatic (the LIF in the convolution's epilogue, one launch, where the
+   * weights stream and one step's images fill the GPU; otherwise the
+   * convolution then the multi-step LIF over its output), 1 always the two
+   * launches, 2 the epilogue wherever the kernel can stage the membranes. */
+  SF_POLICY_LIF_TC_EPILOGUE = 4,
+  SF_POLICY_COUNT = 5
 };
 /* Sets a policy value (>= 0) for every later call in this process. Returns
  * SF_ERR_INVALID_ARG for an unknown key or a negative value. */

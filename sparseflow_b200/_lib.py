@@ -33,6 +33,7 @@ SF_DTYPE_F32, SF_DTYPE_F16, SF_DTYPE_BF16 = 0, 1, 2
 SF_LAYOUT_NCHW, SF_LAYOUT_NHWC = 0, 1
 # Path policy keys (sf_set_path_policy).
 SF_POLICY_CONV1X1_PATH, SF_POLICY_CONV1X1_TC_MIN_HW, SF_POLICY_CONV3X3_PATH, SF_POLICY_LIF_EVENTS_GENERAL = 0, 1, 2, 3
+SF_POLICY_LIF_TC_EPILOGUE = 4
 
 _TORCH2SF = {torch.float32: SF_DTYPE_F32, torch.float16: SF_DTYPE_F16, torch.bfloat16: SF_DTYPE_BF16}
 

@@ -30,6 +30,9 @@ struct TcLif {
   float* v;
   float tau, v_threshold, v_reset;
   int hard_reset, decay_input;
+  // false: only where it pays (streamed weights and at least 2 tiles per SM
+  // in one step's plane); true: wherever the membranes can be staged.
+  bool always;
 };
 // Runs the convolution (when `gate` selects it); with `lif`, the fused
 // convolution + multi-step LIF.

@@ -11,6 +11,7 @@ std::atomic<long long> g_policy[SF_POLICY_COUNT] = {
     {128},  // SF_POLICY_CONV1X1_TC_MIN_HW
     {0},    // SF_POLICY_CONV3X3_PATH: automatic
     {0},    // SF_POLICY_LIF_EVENTS_GENERAL
+    {0},    // SF_POLICY_LIF_TC_EPILOGUE: automatic
 };
 }  // namespace
 

@@ -291,11 +291,12 @@ double tc3_min_density(int C) {
 //   C_in 64 56x56:  masks 0.735 / 0.735 at 0.1 %, 0.809 / 0.734 at 0.3 %;
 //                   none  0.646 / 0.666 at 0.1 %, 0.705 / 0.664 at 0.3 %
 //   C_in 128 28x28: masks 0.649 / 0.668 at 0.3 %, 0.688 / 0.667 at 0.4 %;
-//                   none  0.616 / 0.632 at 0.5 %, 0.682 / 0.632 at 0.7 %
+//                   none  0.561 / 0.590 at 0.3 %, 0.592 / 0.590 at 0.4 %,
+//                         0.624 / 0.589 at 0.5 % (LIF in the epilogue)
 //   C_in 256 14x14: masks 0.553 / 0.550 at 0.6 %; none 0.548 / 0.528 at 0.6 %
 double tc3_lif_min_density(int C, bool masks) {
   if (C <= c3tc::kTcResidentMaxC) return masks ? 0.0 : 0.002;
-  if (C <= 160) return masks ? 0.0035 : 0.0055;
+  if (C <= 160) return masks ? 0.0035 : 0.004;
   return C <= 320 ? 0.0055 : 0.01;
 }
 constexpr int kDensitySamples = kMaxDensitySamples;
@@ -353,12 +354,14 @@ sf_status run_conv(const void* x, const void* w_packed, const float* bias, void*
   auto tc_then_lif = [&](const Gate& g, cudaStream_t sx) -> sf_status {
     const int wsz = (int)dtype_size(wdt);
     const void* section = static_cast<const char*>(w_packed) + tc_section_offset(Co, C, K, wsz);
-    if (lif && !mask_out && !dev_knob("SF_LIF_TC_UNFUSED")) {
+    const int epi = (int)policy(SF_POLICY_LIF_TC_EPILOGUE);
+    if (lif && !mask_out && epi != 1) {
       // One launch: the LIF runs in the tensor-core kernel's epilogue (unit
       // by unit over t = 0..T-1, the membrane read and written by the same
       // thread each step, kept in L2 between steps), so the preactivations
       // never reach memory.
-      const c3tc::TcLif tl{T, v, lifd->tau, lifd->v_threshold, lifd->v_reset, lifd->hard_reset, lifd->decay_input};
+      const c3tc::TcLif tl{T, v, lifd->tau, lifd->v_threshold, lifd->v_reset, lifd->hard_reset, lifd->decay_input,
+                           epi == 2};
       sf_status r = c3tc::run_conv3x3_tc(x, w_packed, weight_block_cpl(C, K, Co, wsz), section, bias, y,
                                          conv_error_word(), T * N, C, H, W, Co, xdt, wdt, sx, g, &tl);
       if (r != SF_ERR_UNSUPPORTED) return r;

@@ -9,10 +9,11 @@ from oracle import oracle
 pytestmark = pytest.mark.gpu
 
 
-def _run(x, w, b, v0, tau, vr, decay, policy, masks=False):
+def _run(x, w, b, v0, tau, vr, decay, policy, masks=False, epilogue=0):
     from sparseflow_b200 import _lib
     from sparseflow_b200.Kernels.fused_conv_lif import sparse_fused_conv_lif_forward, event_masks_of
-    with _lib.path_policy(_lib.SF_POLICY_CONV3X3_PATH, policy):
+    with _lib.path_policy(_lib.SF_POLICY_CONV3X3_PATH, policy), _lib.path_policy(_lib.SF_POLICY_LIF_TC_EPILOGUE,
+                                                                                 epilogue):
         s, v, _ = sparse_fused_conv_lif_forward(x, v0, w, b, tau, 1.0, vr, decay, kernel_size=3, stride=1,
                                                 padding=1, emit_event_masks=masks)
     torch.cuda.synchronize()
@@ -62,7 +63,7 @@ def test_lif_tensor_core_route_vs_oracle_and_gather(t, n, c, co, h, w, density, 
 
 @pytest.mark.parametrize("c,density,masks,expect", [
     (64, 0.001, False, 1), (64, 0.05, False, 2), (64, 0.001, True, 2),
-    (128, 0.002, True, 1), (128, 0.1, True, 2), (128, 0.004, False, 1), (256, 0.003, False, 1),
+    (128, 0.002, True, 1), (128, 0.1, True, 2), (128, 0.0025, False, 1), (256, 0.003, False, 1),
     (256, 0.05, True, 2)])
 def test_lif_density_gate_picks_one_route(c, density, masks, expect):
     """The sampled nonzero count picks the fused gather kernel or the tensor-core route on the
@@ -96,18 +97,18 @@ def test_lif_tensor_core_route_keeps_16bit_spikes_on_gather():
     (3, 2, 256, 96, 14, 14, 0.05, 3.0, 0.0, False),   # non power-of-two tau (IEEE division)
 ])
 def test_lif_in_tensor_core_epilogue_equals_two_launch_route(t, n, c, co, h, w, density, tau, vr, decay):
-    """Without event masks the tensor-core route runs the LIF in the convolution's epilogue (one
-    launch; the membrane stays in L2 between steps). Spikes and membrane equal, bit for bit, the
-    route that writes the preactivations and runs the multi-step LIF over them (taken when masks
-    are asked for), and the spikes follow the oracle's near-threshold rule."""
+    """Without event masks the tensor-core route can run the LIF in the convolution's epilogue
+    (one launch; the membrane stays in L2 between steps; forced here by policy). Spikes and
+    membrane equal, bit for bit, the route that writes the preactivations and runs the multi-step
+    LIF over them, and the spikes follow the oracle's near-threshold rule."""
     g = torch.Generator().manual_seed(t * 7 + c + co)
     x = (torch.rand(t, n, c, h, w, generator=g) < density).float()
     wt = torch.randn(co, c, 3, 3, generator=g) * (3.0 / (c * 9 * density)) ** 0.5
     b = torch.randn(co, generator=g) * 0.2
     v0 = torch.rand(n, co, h, w, generator=g) * 0.5
     xs, ws, bs, vs = x.cuda(), wt.cuda(), b.cuda(), v0.cuda()
-    s_f, v_f, _ = _run(xs, ws, bs, vs, tau, vr, decay, 2, masks=False)
-    s_m, v_m, _ = _run(xs, ws, bs, vs, tau, vr, decay, 2, masks=True)
+    s_f, v_f, _ = _run(xs, ws, bs, vs, tau, vr, decay, 2, epilogue=2)
+    s_m, v_m, _ = _run(xs, ws, bs, vs, tau, vr, decay, 2, epilogue=1)
     assert torch.equal(s_f, s_m) and torch.equal(v_f, v_m)
     so, near, vo = oracle.conv_lif_near(x.numpy(), wt.numpy(), b.numpy(), v0.numpy(), 1, 1, tau, 1.0, vr, decay)
     assert 0.01 < so.mean() < 0.9
