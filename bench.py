@@ -76,6 +76,9 @@ def parse():
                          "HxH maps, Bernoulli spikes) instead of the headline cell; an ncu-sized case with --images")
     ap.add_argument("--images", type=int, default=T_STEPS * N_BATCH,
                     help="T*N images per step (multiple of 16); smaller values make an ncu-sized case")
+    ap.add_argument("--path3x3", type=int, choices=[0, 1, 2], default=0,
+                    help="with --only-timed: SF_POLICY_CONV3X3_PATH (0 the density gate, 1 gather kernel, "
+                         "2 tensor cores), to profile one route of a gated cell")
     return ap.parse_args()
 
 
@@ -565,6 +568,9 @@ def main():
     if args.impl == "reference":
         run_reference(args)
         return
+    if args.only_timed and args.path3x3:
+        from sparseflow_b200 import _lib
+        _lib.set_path_policy(_lib.SF_POLICY_CONV3X3_PATH, args.path3x3)
     if args.sweep:
         run_sweep(args)
         return
