@@ -1286,10 +1286,12 @@ sf_status run_conv3x3_tc(const void* x, const void* w_gather, int cpl, const voi
     p.hard = lif->hard_reset;
     p.vr = lif->hard_reset ? lif->v_reset : 0.f;
     p.decay_input = lif->decay_input;
-    // Staged membranes (streamed weights) only: the direct loads of the
-    // resident-weight epilogue are latency-bound (C64 56x56: 1.37 ms against
-    // 0.66 ms for the two launches). And one step's plane must give every SM
-    // a few tiles: C256 14x14 (120 tiles) took 0.74 ms against 0.53.
+    // Streamed weights with staged membranes only. With resident weights
+    // (C_in <= 64) the epilogue's membrane traffic outweighs the MMAs of a
+    // tile: C64 56x56 took 1.37 ms with direct membrane loads and 0.79 ms
+    // with staged ones, against 0.68 ms for the two launches. And one step's
+    // plane must give every SM a few tiles: C256 14x14 (120 tiles) took
+    // 0.74 ms against 0.55.
     if (p.vs_off == 0) return SF_ERR_UNSUPPORTED;
     if (!lif->always && p.ntiles < 2ll * num_sms_current_device()) return SF_ERR_UNSUPPORTED;
   } else if (!plan_tc(p, smem, N, C, H, W, Co)) {
