@@ -171,6 +171,22 @@ __device__ __forceinline__ void emit(XT* y, float* vm, float vold, float a, cons
   }
 }
 
+// Two channels' outputs from their digit sums, with packed fp32 pairs
+// (sm_100 add/fma .f32x2, each half rounded exactly like the scalar form):
+// x2 = (D2 + 1.5 * 2^23 as float) - 1.5 * 2^23, t = x01 * 256 + x2,
+// y = s * t + bias.
+__device__ __forceinline__ void combine2(float x01a, float x01b, uint32_t d2a, uint32_t d2b, float4 sb, float& ya,
+                                         float& yb) {
+  asm("{\n\t.reg .b64 rx, rt, rk, rc, rs, rb;\n\t"
+      "mov.b64 rt, {%4, %5};\n\tmov.b64 rc, {%10, %10};\n\tadd.rn.f32x2 rt, rt, rc;\n\t"
+      "mov.b64 rx, {%2, %3};\n\tmov.b64 rk, {%11, %11};\n\tfma.rn.f32x2 rt, rx, rk, rt;\n\t"
+      "mov.b64 rs, {%6, %7};\n\tmov.b64 rb, {%8, %9};\n\tfma.rn.f32x2 rt, rs, rt, rb;\n\t"
+      "mov.b64 {%0, %1}, rt;\n\t}"
+      : "=f"(ya), "=f"(yb)
+      : "f"(x01a), "f"(x01b), "f"(__int_as_float((int)d2a + 0x4B400000)), "f"(__int_as_float((int)d2b + 0x4B400000)),
+        "f"(sb.x), "f"(sb.z), "f"(sb.y), "f"(sb.w), "f"(-12582912.f), "f"(256.f));
+}
+
 template <typename WT>
 __device__ __forceinline__ float gather_w(const Params& p, int co, int ci, int tap) {
   const int blk = co / (32 * p.cpl), rem = co - blk * 32 * p.cpl;
@@ -351,7 +367,18 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const XT* __restr
       tc::tmem_ld8(ta + (uint32_t)p.CB, r1);
       tc::tmem_ld8(ta + (uint32_t)(2 * p.CB), r2);
       tc::tmem_wait_ld();
-      if (valid) {
+      if (LM == 0 && valid) {
+        XT* yc = yp + (size_t)c8 * HW;
+#pragma unroll
+        for (int e = 0; e < 8; e += 2) {
+          float ya, yb;
+          combine2(__int2float_rn((int)r0[e] * 256 + (int)r1[e]), __int2float_rn((int)r0[e + 1] * 256 + (int)r1[e + 1]),
+                   r2[e], r2[e + 1], tb[(c8 + e) >> 1], ya, yb);
+          st_cs(yc, DT<XT>::from_f(ya));
+          st_cs(yc + HW, DT<XT>::from_f(yb));
+          yc += 2 * HW;
+        }
+      } else if (valid) {
         XT* yc = yp + (size_t)c8 * HW;
         float* vc = LM ? vp + (size_t)c8 * HW : nullptr;
 #pragma unroll
