@@ -756,6 +756,12 @@ def main():
     ev_cmp = [torch.cuda.Event() for _ in chunks]
     ev_out = [torch.cuda.Event() for _ in chunks]
 
+    # Each chunk's output stays referenced until the next step's output of that chunk replaces it;
+    # that allocation is ordered after the wait for the chunk's previous download, so reusing the
+    # memory is safe without record_stream (whose deferred frees made the allocator take fresh
+    # blocks from the driver every step: 88 ms instead of 18 ms per step).
+    ys = [None] * len(chunks)
+
     def e2e_step():
         for c, (a, b) in enumerate(chunks):
             with torch.cuda.stream(s_in):
@@ -765,12 +771,11 @@ def main():
             with torch.cuda.stream(s_cmp):
                 s_cmp.wait_event(ev_in[c])
                 s_cmp.wait_event(ev_out[c])  # the previous step's download of this chunk is done
-                y = mod(x_dev[a:b])
+                ys[c] = mod(x_dev[a:b])
                 ev_cmp[c].record(s_cmp)
             with torch.cuda.stream(s_out):
                 s_out.wait_event(ev_cmp[c])
-                y_host[a:b].copy_(y, non_blocking=True)
-                y.record_stream(s_out)
+                y_host[a:b].copy_(ys[c], non_blocking=True)
                 ev_out[c].record(s_out)
 
     with torch.no_grad():
