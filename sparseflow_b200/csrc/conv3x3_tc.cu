@@ -484,29 +484,26 @@ template <typename XT, int LM>
 __device__ __forceinline__ void lif_tile8(const Params& p, XT* ybase, const TilePos& tp, uint32_t ta,
                                           const float* vo, const float2* tab) {
   const size_t HW = (size_t)p.H * p.W;
-  // Two TMEM round trips (D0, D1 then D2) keep 16 registers in flight
-  // rather than 24, so the next tile's membranes stay in registers.
-  uint32_t r0[8], r1[8];
+  // The membranes wait in shared memory, so all three digit planes load
+  // with one TMEM round trip.
+  uint32_t r0[8], r1[8], r2[8];
   tc::tmem_ld8(ta, r0);
   tc::tmem_ld8(ta + (uint32_t)p.CB, r1);
-  tc::tmem_wait_ld();
-  float x01[8];
-#pragma unroll
-  for (int e = 0; e < 8; ++e) x01[e] = __int2float_rn((int)r0[e] * 256 + (int)r1[e]);
-  tc::tmem_ld8(ta + (uint32_t)(2 * p.CB), r0);
+  tc::tmem_ld8(ta + (uint32_t)(2 * p.CB), r2);
   tc::tmem_wait_ld();
   if (!tp.valid) return;
   const float4* tb = reinterpret_cast<const float4*>(tab);
   XT* yc = ybase + tp.off;
   float* vc = p.v + tp.off;
 #pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    const float4 sb = tb[e >> 1];
-    const float x2 = __int_as_float((int)r0[e] + 0x4B400000) - 12582912.f;
-    const float a = fmaf((e & 1) ? sb.z : sb.x, fmaf(x01[e], 256.f, x2), (e & 1) ? sb.w : sb.y);
-    emit<LM>(yc, vc, vo[e * 32], a, p);
-    yc += HW;
-    vc += HW;
+  for (int e = 0; e < 8; e += 2) {
+    float a0, a1;
+    combine2(__int2float_rn((int)r0[e] * 256 + (int)r1[e]), __int2float_rn((int)r0[e + 1] * 256 + (int)r1[e + 1]),
+             r2[e], r2[e + 1], tb[e >> 1], a0, a1);
+    emit<LM>(yc, vc, vo[e * 32], a0, p);
+    emit<LM>(yc + HW, vc + HW, vo[(e + 1) * 32], a1, p);
+    yc += 2 * HW;
+    vc += 2 * HW;
   }
 }
 
