@@ -924,9 +924,12 @@ __global__ void __launch_bounds__(cta_threads<LM>(), 1) conv3x3_tc_kernel(const 
       unsigned char* ab = abuf + (size_t)a * p.a_bytes;
       uint32_t nb = 0u;
       if constexpr (VEC)
-        // The LIF kernels keep x out of L1, which then holds the
-        // epilogue's spilled membranes.
-        convert_unit_vec4<LM != 0>(p, reinterpret_cast<const float*>(xs), ab, t0 * kM, warp, lane, kConv, nb);
+        // Streamed weights keep x out of L1 (C128 28x28 0.5 % faster): their
+        // units span many channels, so a unit's halo rows are gone from L1
+        // before the next unit reads them. With resident weights the next
+        // unit's halo rows still hit in L1: not allocating there cost the
+        // C64 56x56 cell 6 %.
+        convert_unit_vec4<STREAM>(p, reinterpret_cast<const float*>(xs), ab, t0 * kM, warp, lane, kConv, nb);
       else
         convert_unit_scalar<XT>(p, xs, ab, t0 * kM, warp, lane, kConv, nb);
       if (__any_sync(0xffffffffu, nb != 0u) && lane == 0)
